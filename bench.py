@@ -1,0 +1,279 @@
+"""Benchmark of the MoE block hot path (one JSON line on rank 0).
+
+Workload: 8K-token prefill -- 16 chunks of 512 tokens whose tokens share
+each expert's weight pass -- through 40 stacked Qwen3.6-35B-A3B MoE layers with 8-bit group-64
+weights (256 experts, top-8, intermediate 512, sigmoid-gated shared expert), bf16 activations
+~N(0,1), weights ~N(0,0.02) quantised by the min/max affine rule and generated on the device.
+A step is one pass of the 40-layer residual stack x += block_l(RMSNorm(x)) over the 8192 tokens.
+The batch-1 decode of configs[1] (same 40 layers, one token) is reported in "decode".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the CPU restatement of the reference's C# block arithmetic
+(oracle/, Qwen36Model.cs:218-262 semantics) on the host cores with the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "infer.net_b200"))
+
+LAYERS, TOKENS, D, E, I = 40, 8192, 2048, 256, 512
+SEED = 20261201
+# algorithmic counts (per token per layer): routed 8 x 6,291,456 + shared 6,291,456 + router 1,048,576
+# + shared-route gate 4,096 FLOPs; decode weight bytes per layer: 9 experts + router + gate
+FLOPS_TOKEN_LAYER = 8 * 6291456 + 6291456 + 1048576 + 4096
+GATE_UP_FLOPS_PER_ROUTE = 2 * 2 * I * D  # gate and up rows, 2 FLOPs per MAC
+DECODE_BYTES_LAYER = 9 * 3342336 + 557056 + 2176
+METRIC = "MoE-block prefill tokens/s @8K (16x512-token chunks, 40 layers, 8-bit g64)"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([v.strip() for v in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in self.rows for k in range(4) if len(r) > 5 + k and r[5 + k] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------------- reference arm
+
+def cpu_sample(tokens: int, threads: int):
+    """Time the oracle port of the reference block on `tokens` tokens of one full-size layer."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    L = O.Layer(SEED, layer=0, bits=8)
+    x = O.gen_bf16(SEED, O.ACT_STREAM, tokens * D).reshape(tokens, D)
+    O.moe_block(L, x[:4], O.MODE_F32, threads=threads)  # warm
+    t0 = time.perf_counter()
+    rc, *_ = O.moe_block(L, x, O.MODE_F32, threads=threads)
+    dt = time.perf_counter() - t0
+    assert rc == 0
+    return dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    tokens = 64
+    for _ in range(args.warmup):
+        cpu_sample(tokens, threads)
+    times = [cpu_sample(tokens, threads) for _ in range(args.steps)]
+    t = sum(times) / len(times)
+    value = tokens / (t * LAYERS)  # tokens/s through 40 layers, extrapolated from one layer
+    sample = f"{tokens} tokens x 1 of 40 layers per step (full geometry, 8-bit), extrapolated x40"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "prefill 8192 tokens x 40 MoE layers (CPU sample)", "tokens": TOKENS, "layers": LAYERS,
+                   "bits": 8, "experts": E, "top_k": 8},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ----------------------------------------------------------------------------------- our arm
+
+def run_ours(args):
+    global LAYERS, TOKENS
+    LAYERS, TOKENS = args.layers, args.tokens
+    import numpy as np
+    import torch
+
+    import deepinfer_cuda as di
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        raise SystemExit("expert-parallel multi-GPU run is not available in this build")
+    torch.cuda.set_device(local)
+    ctx = di.Context(resident=0)
+    layers = [di.MoeLayer.generated(ctx, SEED, l, bits=8) for l in range(LAYERS)]
+    norms = torch.ones((LAYERS, D), dtype=torch.float32, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(SEED)
+    x0 = torch.randn((TOKENS, D), generator=gen, device="cuda").to(torch.bfloat16).float()
+    x = torch.empty_like(x0)
+    arr = (di.C.c_void_p * LAYERS)(*[l.h for l in layers])
+    err = di.C.create_string_buffer(2048)
+
+    def stack(xptr, T, flags):
+        ms = di.C.c_double()
+        rc = di.lib().di_moe_stack(ctx.h, di.C.cast(arr, di.C.c_void_p), norms.data_ptr() if flags & di.DEVICE_IO
+                                   else norms_host.ctypes.data, LAYERS, 1e-6, xptr, T, None, None, flags,
+                                   di.C.byref(ms), err, 2048)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return ms.value
+
+    norms_host = np.ones((LAYERS, D), np.float32)
+    flags = di.DEVICE_IO | di.PATH_GROUPED | di.PROFILE
+    # ---- device-resident timed region (value)
+    for _ in range(args.warmup):
+        x.copy_(x0)
+        torch.cuda.synchronize()
+        stack(x.data_ptr(), TOKENS, flags)
+    torch.cuda.synchronize()
+    stage_tot = {}
+    step_ms = []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            x.copy_(x0)
+            torch.cuda.synchronize()
+            step_ms.append(stack(x.data_ptr(), TOKENS, flags))
+            for k, v in ctx.last_profile().items():
+                stage_tot[k] = stage_tot.get(k, 0.0) + v
+    torch.cuda.synchronize()
+    ms = sum(step_ms) / len(step_ms)
+    value = TOKENS / (ms / 1e3)
+    # ---- end to end through the public API with pinned host buffers
+    e2e, dec_us, dstage = None, None, {}
+    if not args.only_prefill:
+        e2e, dec_us, dstage = e2e_and_decode(args, di, torch, ctx, stack, x0)
+    pk = peaks()
+
+    # ---- roofline of the dominant kernel: grouped gate/up + SwiGLU
+    gate_up_ms = stage_tot.get("gate_up", 0.0) / (args.steps * LAYERS)
+    gu_flops = (8 * TOKENS + TOKENS) * GATE_UP_FLOPS_PER_ROUTE
+    achieved = gu_flops / (gate_up_ms * 1e-3) / 1e12 if gate_up_ms > 0 else None
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        tok = 64
+        t = cpu_sample(tok, threads)
+        cpu = {"value": tok / (t * LAYERS), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{tok} tokens x 1 of 40 layers (full geometry, 8-bit) on the oracle port, extrapolated x40"}
+    total_flops = FLOPS_TOKEN_LAYER * TOKENS * LAYERS
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "prefill 8192 tokens (16 x 512 chunks) x 40 MoE layers, 8-bit g64",
+                   "tokens": TOKENS, "layers": LAYERS, "experts": E, "top_k": 8, "intermediate": I, "hidden": D,
+                   "parallelism": "ep1", "l2": "inputs larger than L2 (34.4 GB of weights per step)"},
+        "tensor_frac_step": total_flops / (ms * 1e-3) / (pk["bf16_tflops_sustained"] * 1e12),
+        "roofline": {"kernel": "grouped_gemm<gate_up,8bit>", "bound": "tensor", "achieved": achieved,
+                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
+                     "traffic": None, "peak_source": pk["source"] + " sustained bf16"},
+        "stage_ms_per_step": {k: v / args.steps for k, v in stage_tot.items()},
+        "cpu_baseline": cpu,
+        "e2e": None if e2e is None else {
+            "value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": TOKENS * D * 4 + LAYERS * D * 4,
+            "d2h_bytes_per_step": TOKENS * D * 4},
+        "decode": None if dec_us is None else {
+            "workload": "batch-1 decode, 40 layers (configs[1])", "us_per_token": dec_us,
+            "gbs": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9,
+            "hbm_frac": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9 / pk["hbm_gbs"],
+            "stage_us": {k: v * 1e3 for k, v in dstage.items()}},
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps * LAYERS * 8,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for l in layers:
+        l.close()
+    ctx.close()
+
+
+def e2e_and_decode(args, di, torch, ctx, stack, x0):
+    """End-to-end prefill through the host-buffer API, then the batch-1 decode stack."""
+    xh = x0.cpu().pin_memory()
+    xo = torch.empty_like(xh).pin_memory()
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        xo.copy_(xh)
+        t0 = time.perf_counter()
+        stack(xo.data_ptr(), TOKENS, di.PATH_GROUPED)
+        dt = (time.perf_counter() - t0) * 1e3
+        if i >= args.warmup:
+            e2e_ms.append(dt)
+    e2e = TOKENS / (sum(e2e_ms) / len(e2e_ms) / 1e3)
+    x1 = x0[:1].clone()
+    dflags = di.DEVICE_IO | di.PATH_GEMV | di.PROFILE
+    for _ in range(args.warmup):
+        stack(x1.data_ptr(), 1, dflags)
+    n = max(args.steps, 5)
+    dms, dstage = [], {}
+    for _ in range(n):
+        x1.copy_(x0[:1])
+        dms.append(stack(x1.data_ptr(), 1, dflags))
+        for k, v in ctx.last_profile().items():
+            dstage[k] = dstage.get(k, 0.0) + v / n
+    return e2e, 1e3 * sum(dms) / len(dms), dstage
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="profiling case: fewer stacked layers")
+    ap.add_argument("--tokens", type=int, default=TOKENS, help="profiling case: fewer prefill tokens")
+    ap.add_argument("--only-prefill", action="store_true", help="profiling case: skip the e2e and decode legs")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

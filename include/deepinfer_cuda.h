@@ -1,0 +1,140 @@
+/*
+ * deepinfer_cuda -- B200 (sm_100a) backend for the Qwen3.6-35B-A3B MoE feed-forward block.
+ *
+ * Plain C ABI: opaque handles, plain pointers and sizes, UTF-8 error text written into a
+ * caller buffer (error, capacity). Every call validates all of its arguments before any
+ * GPU work; an invalid call returns NULL / a nonzero status, submits nothing and leaves
+ * every output untouched (native/DeepInfer.Metal/quantized.mm:323-331, :354-361).
+ * Calls are synchronous: outputs are visible on return, and `ms` receives the GPU time
+ * of the call's work measured with CUDA events (quantized.mm:215-229).
+ * One context owns one CUDA stream on the device that was current at creation; a
+ * context is not thread-safe (callers serialise per model, Qwen36Model.cs:18, :47-53).
+ *
+ * Part 1 replaces the managed QuantNative table (src/DeepInfer.Backends/Compute/
+ * QuantizedMetal.cs:242-274, bound to native/DeepInfer.Metal/quantized.mm:241-397).
+ * Part 2 adds batched entries for the whole block (router -> top-8 -> permute -> grouped
+ * expert GEMMs -> shared expert -> combine); they replace the MoE part of
+ * di_graph_forward / di_graph_prefill (gpu_graph.mm:307-320, gpu_prefill.mm:700-706).
+ */
+#ifndef DEEPINFER_CUDA_H
+#define DEEPINFER_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DI_ABI_VERSION 1
+
+/* ABI version probe; the C# loader checks it like di_cuda_prefix_abi_version
+   (native/DeepInfer.Cuda/split_prefix.cu:14, src/DeepInfer.Backends/Split/SplitSessions.cs:66). */
+int di_abi_version(void);
+
+/* ------------------------------------------------------------------------------------
+ * Part 1. Quantised GEMV operators (drop-in for QuantNative / deepinfer_metal).
+ * Matrices are [experts, rows, columns] affine group-64 stacks in MLX layout:
+ *   index 0 packed  uint32 [experts, rows, columns*bits/32], codes LSB-first, crossing words
+ *   index 1 scales  bf16   [experts, rows, columns/64]
+ *   index 2 biases  bf16   [experts, rows, columns/64]
+ * and dequantise as w = q*scale + bias (quantized.mm:62-82).
+ * ---------------------------------------------------------------------------------- */
+
+/* QuantNative.Job (QuantizedMetal.cs:250-258; quantized.mm:24-30). Host float arrays. */
+typedef struct di_quant_job {
+    void *matrix;
+    const float *input;       /* columns floats, or count*columns when batched */
+    float *output;            /* count*rows floats */
+    const uint32_t *experts;  /* count expert ids */
+    int32_t count, batched;
+} di_quant_job;
+
+/* di_quant_create (quantized.mm:282-286; QuantizedMetal.cs:264). Reads DEEPINFER_CUDA_RESIDENCY
+   and DEEPINFER_CUDA_RESIDENCY_REFRESH_MS like the Metal variant reads its residency variables. */
+void *di_quant_create(char *error, int capacity);
+/* di_quant_create_configured (quantized.mm:242-280; QuantizedMetal.cs:244-245). resident must be
+   0 or 1 and refresh_ms in [0, 60000]. Weights are always device-resident on CUDA; resident=1
+   additionally accounts them in di_quant_residency_bytes. */
+void *di_quant_create_configured(int resident, int refresh_ms, char *error, int capacity);
+void di_quant_destroy(void *ctx);                               /* quantized.mm:293 */
+uint64_t di_quant_residency_bytes(void *ctx);                   /* quantized.mm:287-289 */
+/* Uploads every host-staged weight buffer and waits (quantized.mm:290-292). */
+void di_quant_residency_prepare(void *ctx);
+
+/* quantized.mm:294-315: experts 1..256, rows >= 1, columns % 64 == 0, bits 5 or 8, group 64. */
+void *di_quant_matrix_create(void *ctx, int experts, int rows, int columns, int bits, int group,
+                             char *error, int capacity);
+/* quantized.mm:316-319. Returns a HOST-writable staging buffer (pinned) for index 0/1/2 that the
+   caller fills (QuantizedMetal.cs:162-177); its contents are uploaded to the device before the
+   next compute call or at di_quant_residency_prepare. NULL for a bad index. */
+void *di_quant_matrix_buffer(void *matrix, int index);
+void di_quant_matrix_destroy(void *matrix);                     /* quantized.mm:320 */
+
+/* quantized.mm:321-345: 1..8 independent GEMV jobs on distinct matrices, one submission. */
+int di_quant_batch(void *ctx, const di_quant_job *jobs, int count, double *ms, char *error, int capacity);
+/* quantized.mm:346-349 */
+int di_quant_matvec(void *ctx, void *matrix, const float *x, float *y, const uint32_t *experts, int count,
+                    int batched, double *ms, char *error, int capacity);
+/* quantized.mm:350-383: gate/up -> SwiGLU -> down for `count` selected experts sharing `input`,
+   plus the independent shared-expert down projection of `shared_input`. */
+int di_quant_experts(void *ctx, void *gate, void *up, void *down, void *shared, const float *input,
+                     const float *shared_input, const uint32_t *experts, int count, float *expert_output,
+                     float *shared_output, double *ms, char *error, int capacity);
+/* quantized.mm:384-397: dequantised row `token` of a one-expert matrix into out[columns]. */
+int di_quant_embedding(void *matrix, int token, float *out);
+
+/* Device-side access (no reference counterpart: Metal buffers are host-visible, CUDA device
+   memory is not). */
+void *di_quant_matrix_device_buffer(void *matrix, int index);
+/* Copies `bytes` from host memory into buffer `index` (bytes must equal the buffer size). */
+int di_quant_matrix_upload(void *matrix, int index, const void *src, uint64_t bytes, char *error, int capacity);
+/* Fills the matrix with synthetic weights ~N(0, stddev) quantised by the min/max affine group-64
+   rule, generated on the device bit-identically to the test oracle (seed, stream). */
+int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, float stddev, char *error,
+                             int capacity);
+
+/* ------------------------------------------------------------------------------------
+ * Part 2. The MoE block.
+ * A layer binds the eight matrices of one block (Qwen36Weights.cs:93-100):
+ *   router [1,E,D] 8-bit, gate/up [E,I,D], down [E,D,I], shared_gate/shared_up [1,I,D],
+ *   shared_down [1,D,I], shared_route [1,1,D] 8-bit; E in [8,256], D % 256 == 0, I % 64 == 0.
+ * ---------------------------------------------------------------------------------- */
+
+void *di_moe_layer_create(void *ctx, void *router, void *gate, void *up, void *down, void *shared_gate,
+                          void *shared_up, void *shared_down, void *shared_route, char *error, int capacity);
+void di_moe_layer_destroy(void *layer);
+/* Optional per-expert logit bias (host f32[E]); NULL clears it. Used by the Zipf load config. */
+int di_moe_layer_set_router_bias(void *layer, const float *bias, char *error, int capacity);
+
+/* flags for di_moe_block / di_moe_stack */
+#define DI_MOE_DEVICE_IO 1      /* x, y, ids, probs (and norms/traces) are device pointers */
+#define DI_MOE_FORCE_ROUTES 2   /* ids is an INPUT [T,8]: forced expert ids (gpu_graph.mm:153-159) */
+#define DI_MOE_PATH_GEMV 4      /* force the decode GEMV path */
+#define DI_MOE_PATH_GROUPED 8   /* force the grouped tensor-core path */
+#define DI_MOE_PROFILE 16       /* di_moe_stack: record per-stage CUDA events (read by di_moe_last_profile) */
+
+/* y[t] = sigmoid(x_t . w_sr) * shared(x_t) + sum_j p[t,j] * expert_{ids[t,j]}(x_t)
+   (Qwen36Model.cs:218-245). x: bf16 [T, D] (the normalised layer input); y: bf16 [T, D].
+   ids (int32 [T,8]) and probs (f32 [T,8]) may be NULL unless DI_MOE_FORCE_ROUTES.
+   Routing: 8 largest router logits in descending order, ties to the lower expert id,
+   probs = softmax over the 8 (Qwen36Model.cs:246-262); a non-finite logit fails the call
+   with "Non-finite router logits" and y is left untouched. T in [1, 65536]. */
+int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint16_t *y, int32_t *ids, float *probs,
+                 int flags, double *ms, char *error, int capacity);
+
+/* n_layers stacked blocks over an f32 residual stream x [T, D] (in/out):
+     h = bf16(RMSNorm(x) * norms[l]);  x += block_l(h)      (gpu_graph.mm:48-61)
+   norms: f32 [n_layers, D]. h_trace (bf16 [n_layers, T, D]) and ids_trace (int32 [n_layers, T, 8])
+   are optional per-layer dumps for teacher-forced checks. Decode-sized T runs as CUDA graph. */
+int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_layers, float eps, float *x, int tokens,
+                 uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error, int capacity);
+
+/* Per-stage GPU milliseconds of the last di_moe_block (or profiled di_moe_stack, summed over its
+   layers) on this context: [router, top8+count, scan, scatter, gate_up, down, combine, rmsnorm];
+   returns the number written. */
+int di_moe_last_profile(void *ctx, double *stage_ms, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

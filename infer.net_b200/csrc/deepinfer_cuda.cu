@@ -1,0 +1,1074 @@
+// deepinfer_cuda: C ABI of the B200 MoE block backend (see include/deepinfer_cuda.h).
+#include "../../include/deepinfer_cuda.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "generate.cuh"
+#include "grouped_gemm.cuh"
+#include "route.cuh"
+
+#define API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+using namespace di;
+
+void set_error(char *error, int capacity, const char *fmt, ...) {
+    if (!error || capacity <= 0) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(error, (size_t)capacity, fmt, ap);
+    va_end(ap);
+}
+
+struct CudaFail {
+    std::string what;
+};
+#define CK(call)                                                                                        \
+    do {                                                                                                \
+        cudaError_t e_ = (call);                                                                        \
+        if (e_ != cudaSuccess) throw CudaFail{std::string(#call) + ": " + cudaGetErrorString(e_)};      \
+    } while (0)
+
+struct Context;
+
+struct Matrix {
+    Context *ctx = nullptr;
+    int experts = 0, rows = 0, cols = 0, bits = 0;
+    void *d[3] = {nullptr, nullptr, nullptr};
+    void *h[3] = {nullptr, nullptr, nullptr};
+    size_t bytes[3] = {0, 0, 0};
+    bool dirty[3] = {false, false, false};
+    int refs = 1;  // the caller's handle plus one per layer binding it
+    bool destroyed = false;
+    QView view() const {
+        return QView{(const uint32_t *)d[0], (const uint16_t *)d[1], (const uint16_t *)d[2], experts, rows, cols, bits};
+    }
+};
+
+struct Layer {
+    Context *ctx = nullptr;
+    Matrix *m[8] = {};  // router, gate, up, down, shared_gate, shared_up, shared_down, shared_route
+    float *bias = nullptr;  // device [E] or null
+    int E = 0, D = 0, I = 0, bits = 0;
+};
+
+// Device scratch of one context; grows, never shrinks.
+struct Workspace {
+    void *base = nullptr;
+    size_t cap = 0;
+};
+
+enum Stage { S_ROUTER, S_TOPK, S_SCAN, S_SCATTER, S_GATE_UP, S_DOWN, S_COMBINE, S_N };
+constexpr int kProfileSlots = S_N + 1;  // + rmsnorm for stacks
+
+struct Context {
+    int device = 0, sms = 0;
+    bool resident = false;
+    int refresh_ms = 1000;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_stop = nullptr, ev_stage[S_N + 1] = {};
+    std::set<Matrix *> matrices;
+    Workspace ws;
+    uint32_t *d_err = nullptr, *h_err = nullptr;
+    double last_stage_ms[kProfileSlots] = {};
+    bool have_profile = false;
+    std::vector<cudaEvent_t> layer_events;  // [layer][S_N + 2] for profiled stacks
+};
+
+std::mutex g_registry;
+std::set<Context *> g_contexts;
+std::set<Matrix *> g_matrices;
+std::set<Layer *> g_layers;
+
+bool live_context(void *p) {
+    std::lock_guard<std::mutex> g(g_registry);
+    return p && g_contexts.count(static_cast<Context *>(p));
+}
+bool live_matrix(void *p) {
+    std::lock_guard<std::mutex> g(g_registry);
+    return p && g_matrices.count(static_cast<Matrix *>(p)) && !static_cast<Matrix *>(p)->destroyed;
+}
+bool live_layer(void *p) {
+    std::lock_guard<std::mutex> g(g_registry);
+    return p && g_layers.count(static_cast<Layer *>(p));
+}
+
+void release_matrix(Matrix *m) {
+    if (--m->refs > 0) return;
+    {
+        std::lock_guard<std::mutex> g(g_registry);
+        g_matrices.erase(m);
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m->ctx->device);
+    for (int i = 0; i < 3; ++i) {
+        if (m->d[i]) cudaFree(m->d[i]);
+        if (m->h[i]) cudaFreeHost(m->h[i]);
+    }
+    m->ctx->matrices.erase(m);
+    cudaSetDevice(prev);
+    delete m;
+}
+
+struct DeviceGuard {
+    int prev = 0;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+// Upload every host-staged buffer of m that was handed out since its last upload.
+void sync_matrix(Matrix *m) {
+    for (int i = 0; i < 3; ++i)
+        if (m->dirty[i]) {
+            CK(cudaMemcpyAsync(m->d[i], m->h[i], m->bytes[i], cudaMemcpyHostToDevice, m->ctx->stream));
+            m->dirty[i] = false;
+        }
+}
+
+// Bump allocator over the context workspace; sizes are computed before any launch.
+struct Carve {
+    size_t off = 0;
+    template <class T>
+    size_t take(size_t n) {
+        off = (off + 255) & ~(size_t)255;
+        size_t o = off;
+        off += n * sizeof(T);
+        return o;
+    }
+};
+
+void ensure_workspace(Context *c, size_t bytes) {
+    if (c->ws.cap >= bytes) return;
+    if (c->ws.base) {
+        CK(cudaStreamSynchronize(c->stream));
+        CK(cudaFree(c->ws.base));
+        c->ws.base = nullptr;
+        c->ws.cap = 0;
+    }
+    size_t cap = std::max(bytes, (size_t)64 << 20);
+    CK(cudaMalloc(&c->ws.base, cap));
+    c->ws.cap = cap;
+}
+
+template <class T>
+T *at(Context *c, size_t off) {
+    return reinterpret_cast<T *>(static_cast<uint8_t *>(c->ws.base) + off);
+}
+
+int launch_check(char *error, int capacity) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(error, capacity, "CUDA launch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+bool kernels_configured = false;
+void configure_kernels() {
+    if (kernels_configured) return;
+    cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(router::Smem));
+    cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::Cfg<gg::MODE_GATE_UP>::SMEM);
+    cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::Cfg<gg::MODE_GATE_UP>::SMEM);
+    cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::Cfg<gg::MODE_DOWN>::SMEM);
+    cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::Cfg<gg::MODE_DOWN>::SMEM);
+    kernels_configured = true;
+}
+
+// ------------------------------------------------------------------------ the block
+
+struct BlockBuffers {
+    uint16_t *x, *y;
+    float *logits, *probs, *gate;
+    int32_t *ids, *block_counts, *block_base, *seg_count, *seg_off, *n_tiles, *perm;
+    Tile *tiles;
+    uint16_t *act, *yr, *ys;
+    float *act32;
+    int nblocks, max_tiles;
+};
+
+size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b, bool host_io, bool gemv) {
+    const int E = L->E, D = L->D, I = L->I;
+    b.nblocks = (T + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA;
+    b.max_tiles = (8 * T + gg::BN - 1) / gg::BN + E + (T + gg::BN - 1) / gg::BN + 1;
+    size_t o_x = host_io ? cv.take<uint16_t>((size_t)T * D) : 0;
+    size_t o_y = host_io ? cv.take<uint16_t>((size_t)T * D) : 0;
+    size_t o_lg = cv.take<float>((size_t)T * E);
+    size_t o_p = cv.take<float>((size_t)T * 8);
+    size_t o_g = cv.take<float>((size_t)T);
+    size_t o_ids = cv.take<int32_t>((size_t)T * 8);
+    size_t o_bc = cv.take<int32_t>((size_t)b.nblocks * E);
+    size_t o_bb = cv.take<int32_t>((size_t)b.nblocks * E);
+    size_t o_sc = cv.take<int32_t>(E + 1);
+    size_t o_so = cv.take<int32_t>(E + 1);
+    size_t o_nt = cv.take<int32_t>(1);
+    size_t o_pm = cv.take<int32_t>((size_t)T * 8);
+    size_t o_t = cv.take<Tile>((size_t)b.max_tiles);
+    size_t o_a = gemv ? 0 : cv.take<uint16_t>((size_t)T * 9 * I);
+    size_t o_yr = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
+    size_t o_ys = gemv ? 0 : cv.take<uint16_t>((size_t)T * D);
+    size_t o_a32 = gemv ? cv.take<float>((size_t)T * 9 * I) : 0;
+    size_t need = cv.off + 256;
+    ensure_workspace(c, need);
+    b.x = host_io ? at<uint16_t>(c, o_x) : nullptr;
+    b.y = host_io ? at<uint16_t>(c, o_y) : nullptr;
+    b.logits = at<float>(c, o_lg);
+    b.probs = at<float>(c, o_p);
+    b.gate = at<float>(c, o_g);
+    b.ids = at<int32_t>(c, o_ids);
+    b.block_counts = at<int32_t>(c, o_bc);
+    b.block_base = at<int32_t>(c, o_bb);
+    b.seg_count = at<int32_t>(c, o_sc);
+    b.seg_off = at<int32_t>(c, o_so);
+    b.n_tiles = at<int32_t>(c, o_nt);
+    b.perm = at<int32_t>(c, o_pm);
+    b.tiles = at<Tile>(c, o_t);
+    b.act = gemv ? nullptr : at<uint16_t>(c, o_a);
+    b.yr = gemv ? nullptr : at<uint16_t>(c, o_yr);
+    b.ys = gemv ? nullptr : at<uint16_t>(c, o_ys);
+    b.act32 = gemv ? at<float>(c, o_a32) : nullptr;
+    return need;
+}
+
+cudaEvent_t *g_marks = nullptr;  // event array the current enqueue records into
+void stage_mark(Context *c, int s) { CK(cudaEventRecord(g_marks ? g_marks[s] : c->ev_stage[s], c->stream)); }
+
+// Enqueue the block on the context stream. x/y/ids/probs are device pointers; resid (f32)
+// optional. forced: ids holds input routes. Returns nothing; errors surface via d_err.
+void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_t *y, float *resid,
+                   const int32_t *forced_ids, float *probs_out, bool gemv, BlockBuffers &b, bool profile) {
+    const int E = L->E, D = L->D, I = L->I;
+    cudaStream_t st = c->stream;
+    const QView R = L->m[0]->view(), G = L->m[1]->view(), U = L->m[2]->view(), Dn = L->m[3]->view();
+    const QView SG = L->m[4]->view(), SU = L->m[5]->view(), SD = L->m[6]->view(), SR = L->m[7]->view();
+    int32_t *ids = b.ids;  // sanitised ids; every later kernel indexes with these
+    float *probs = probs_out ? probs_out : b.probs;
+    if (profile) stage_mark(c, S_ROUTER);
+    // 1. router logits (canonical f32 order)
+    if (gemv) {
+        router_logits_gemv_kernel<<<(E * 32 + 255) / 256, 256, 0, st>>>(x, T, D, R, L->bias, b.logits);
+    } else {
+        dim3 grid((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE);
+        router_logits_kernel<<<grid, router::THREADS, sizeof(router::Smem), st>>>(x, T, D, R, L->bias, b.logits);
+    }
+    if (profile) stage_mark(c, S_TOPK);
+    // 2. top-8 + probabilities + shared gate logit + per-block expert counts
+    topk_count_kernel<<<b.nblocks, topk::WARPS * 32, 0, st>>>(b.logits, T, E, x, D, SR, forced_ids, ids, probs,
+                                                               b.gate, b.block_counts, c->d_err);
+    if (gemv) {
+        if (profile) {
+            stage_mark(c, S_SCAN);
+            stage_mark(c, S_SCATTER);
+            stage_mark(c, S_GATE_UP);
+        }
+        const int warps = T * 9 * I;
+        const size_t xs = (size_t)D * sizeof(uint16_t);
+        if (L->bits == 8)
+            decode_gate_up_kernel<8><<<warps / 8, 256, xs, st>>>(x, T, D, I, G, U, SG, SU, ids, b.act32);
+        else
+            decode_gate_up_kernel<5><<<warps / 8, 256, xs, st>>>(x, T, D, I, G, U, SG, SU, ids, b.act32);
+        if (profile) stage_mark(c, S_DOWN);
+        const int dw = T * D;
+        if (L->bits == 8)
+            decode_down_kernel<8><<<(dw + 7) / 8, 256, 0, st>>>(b.act32, T, D, I, Dn, SD, ids, probs, b.gate, y, resid,
+                                                               c->d_err);
+        else
+            decode_down_kernel<5><<<(dw + 7) / 8, 256, 0, st>>>(b.act32, T, D, I, Dn, SD, ids, probs, b.gate, y, resid,
+                                                               c->d_err);
+        if (profile) stage_mark(c, S_COMBINE);
+        if (profile) stage_mark(c, S_N);
+        return;
+    }
+    if (profile) stage_mark(c, S_SCAN);
+    // 3. scan counts, segment offsets, GEMM tile list
+    scan_tiles_kernel<<<1, 1024, 0, st>>>(b.block_counts, b.nblocks, E, T, gg::BN, b.block_base, b.seg_count,
+                                          b.seg_off, b.tiles, b.n_tiles, b.max_tiles, c->d_err);
+    if (profile) stage_mark(c, S_SCATTER);
+    // 4. stable scatter of routes into expert-grouped order
+    scatter_routes_kernel<<<b.nblocks, 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm);
+    if (profile) stage_mark(c, S_GATE_UP);
+    // 5. grouped gate/up + SwiGLU (routed experts and the shared expert)
+    const int grid = c->sms;
+    {
+        gg::Params p{G, U, SG, SU, x, b.perm, b.tiles, b.n_tiles, T, D, I, E, b.act, nullptr, c->d_err};
+        if (L->bits == 8)
+            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8><<<grid, gg::THREADS, gg::Cfg<gg::MODE_GATE_UP>::SMEM, st>>>(p);
+        else
+            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5><<<grid, gg::THREADS, gg::Cfg<gg::MODE_GATE_UP>::SMEM, st>>>(p);
+    }
+    if (profile) stage_mark(c, S_DOWN);
+    // 6. grouped down -> expert rows in route order, shared rows
+    {
+        gg::Params p{Dn, Dn, SD, SD, b.act, b.perm, b.tiles, b.n_tiles, T, I, D, E, b.yr, b.ys, c->d_err};
+        if (L->bits == 8)
+            gg::grouped_gemm_kernel<gg::MODE_DOWN, 8><<<grid, gg::THREADS, gg::Cfg<gg::MODE_DOWN>::SMEM, st>>>(p);
+        else
+            gg::grouped_gemm_kernel<gg::MODE_DOWN, 5><<<grid, gg::THREADS, gg::Cfg<gg::MODE_DOWN>::SMEM, st>>>(p);
+    }
+    if (profile) stage_mark(c, S_COMBINE);
+    // 7. combine
+    {
+        const size_t n = (size_t)T * (D / 8);
+        combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(b.yr, b.ys, b.gate, probs, T, D, y, resid,
+                                                                     c->d_err);
+    }
+    if (profile) stage_mark(c, S_N);
+}
+
+const char *device_error_text(uint32_t e) {
+    if (e & kErrNonFinite) return "Non-finite router logits.";
+    if (e & kErrBadExpert) return "Expert ID out of bounds";
+    if (e & kErrTimeout) return "Device wait timed out";
+    return "Internal work list overflow";
+}
+
+bool env_flag(const char *name) {
+    const char *v = std::getenv(name);
+    return v && std::strcmp(v, "1") == 0;
+}
+
+}  // namespace
+
+// ============================================================================ Part 1
+
+API int di_abi_version(void) { return DI_ABI_VERSION; }
+
+API void *di_quant_create_configured(int resident, int refresh_ms, char *error, int capacity) {
+    if ((resident != 0 && resident != 1) || refresh_ms < 0 || refresh_ms > 60000) {
+        set_error(error, capacity, "Invalid residency configuration");
+        return nullptr;
+    }
+    int dev = 0, count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count < 1) {
+        cudaGetLastError();
+        set_error(error, capacity, "No CUDA device");
+        return nullptr;
+    }
+    cudaGetDevice(&dev);
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+        set_error(error, capacity, "Cannot query CUDA device");
+        return nullptr;
+    }
+    if (prop.major != 10 || prop.minor != 0) {
+        set_error(error, capacity, "deepinfer_cuda requires an sm_100 (B200) device, found sm_%d%d", prop.major,
+                  prop.minor);
+        return nullptr;
+    }
+    Context *c = new Context();
+    c->device = dev;
+    c->sms = prop.multiProcessorCount;
+    c->resident = resident == 1;
+    c->refresh_ms = refresh_ms;
+    try {
+        CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+        CK(cudaEventCreate(&c->ev_start));
+        CK(cudaEventCreate(&c->ev_stop));
+        for (int i = 0; i <= S_N; ++i) CK(cudaEventCreate(&c->ev_stage[i]));
+        CK(cudaMalloc(&c->d_err, sizeof(uint32_t)));
+        CK(cudaMallocHost(&c->h_err, sizeof(uint32_t)));
+        configure_kernels();
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        delete c;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> g(g_registry);
+    g_contexts.insert(c);
+    return c;
+}
+
+API void *di_quant_create(char *error, int capacity) {
+    const char *v = std::getenv("DEEPINFER_CUDA_RESIDENCY_REFRESH_MS");
+    return di_quant_create_configured(env_flag("DEEPINFER_CUDA_RESIDENCY") ? 1 : 0, v ? std::atoi(v) : 1000, error,
+                                      capacity);
+}
+
+API void di_quant_destroy(void *p) {
+    if (!live_context(p)) return;
+    Context *c = static_cast<Context *>(p);
+    {
+        std::lock_guard<std::mutex> g(g_registry);
+        g_contexts.erase(c);
+    }
+    DeviceGuard dg(c->device);
+    cudaStreamSynchronize(c->stream);
+    // matrices still alive keep their memory until their own destroy; detach them
+    if (c->ws.base) cudaFree(c->ws.base);
+    if (c->d_err) cudaFree(c->d_err);
+    if (c->h_err) cudaFreeHost(c->h_err);
+    for (int i = 0; i <= S_N; ++i)
+        if (c->ev_stage[i]) cudaEventDestroy(c->ev_stage[i]);
+    for (cudaEvent_t e : c->layer_events) cudaEventDestroy(e);
+    if (c->ev_start) cudaEventDestroy(c->ev_start);
+    if (c->ev_stop) cudaEventDestroy(c->ev_stop);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    // Context memory is intentionally kept while matrices reference it.
+    if (c->matrices.empty()) delete c;
+}
+
+API uint64_t di_quant_residency_bytes(void *p) {
+    if (!live_context(p)) return 0;
+    Context *c = static_cast<Context *>(p);
+    if (!c->resident) return 0;
+    uint64_t total = 0;
+    for (Matrix *m : c->matrices)
+        if (!m->destroyed) total += m->bytes[0] + m->bytes[1] + m->bytes[2];
+    return total;
+}
+
+API void di_quant_residency_prepare(void *p) {
+    if (!live_context(p)) return;
+    Context *c = static_cast<Context *>(p);
+    DeviceGuard dg(c->device);
+    try {
+        for (Matrix *m : c->matrices)
+            if (!m->destroyed) sync_matrix(m);
+        CK(cudaStreamSynchronize(c->stream));
+    } catch (const CudaFail &) {
+    }
+}
+
+API void *di_quant_matrix_create(void *ctx, int experts, int rows, int columns, int bits, int group, char *error,
+                                 int capacity) {
+    if (!live_context(ctx) || experts < 1 || experts > 256 || rows < 1 || columns < 64 || (bits != 5 && bits != 8) ||
+        group != 64 || columns % 64) {
+        set_error(error, capacity, "Unsupported quantized matrix shape");
+        return nullptr;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    DeviceGuard dg(c->device);
+    Matrix *m = new Matrix();
+    m->ctx = c;
+    m->experts = experts;
+    m->rows = rows;
+    m->cols = columns;
+    m->bits = bits;
+    const size_t nrow = (size_t)experts * rows;
+    m->bytes[0] = nrow * columns * bits / 8;
+    m->bytes[1] = m->bytes[2] = nrow * (columns / 64) * 2;
+    for (int i = 0; i < 3; ++i) {
+        // +16 bytes of slack so vector loads of the last row stay inside the allocation
+        if (cudaMalloc(&m->d[i], m->bytes[i] + 16) != cudaSuccess) {
+            cudaGetLastError();
+            for (int j = 0; j < i; ++j) cudaFree(m->d[j]);
+            delete m;
+            set_error(error, capacity, "Quantized buffer allocation failed");
+            return nullptr;
+        }
+        cudaMemsetAsync(m->d[i], 0, m->bytes[i] + 16, c->stream);
+    }
+    c->matrices.insert(m);
+    std::lock_guard<std::mutex> g(g_registry);
+    g_matrices.insert(m);
+    return m;
+}
+
+API void *di_quant_matrix_buffer(void *matrix, int index) {
+    if (!live_matrix(matrix) || index < 0 || index > 2) return nullptr;
+    Matrix *m = static_cast<Matrix *>(matrix);
+    DeviceGuard dg(m->ctx->device);
+    if (!m->h[index]) {
+        if (cudaMallocHost(&m->h[index], m->bytes[index]) != cudaSuccess) {
+            cudaGetLastError();
+            m->h[index] = nullptr;
+            return nullptr;
+        }
+        // the staging copy starts as the current device contents
+        if (cudaMemcpy(m->h[index], m->d[index], m->bytes[index], cudaMemcpyDeviceToHost) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFreeHost(m->h[index]);
+            m->h[index] = nullptr;
+            return nullptr;
+        }
+    }
+    m->dirty[index] = true;
+    return m->h[index];
+}
+
+API void *di_quant_matrix_device_buffer(void *matrix, int index) {
+    if (!live_matrix(matrix) || index < 0 || index > 2) return nullptr;
+    return static_cast<Matrix *>(matrix)->d[index];
+}
+
+API int di_quant_matrix_upload(void *matrix, int index, const void *src, uint64_t bytes, char *error, int capacity) {
+    if (!live_matrix(matrix) || index < 0 || index > 2 || !src) {
+        set_error(error, capacity, "Invalid quantized buffer upload");
+        return -1;
+    }
+    Matrix *m = static_cast<Matrix *>(matrix);
+    if (bytes != m->bytes[index]) {
+        set_error(error, capacity, "Quantized buffer length mismatch.");
+        return -1;
+    }
+    DeviceGuard dg(m->ctx->device);
+    try {
+        CK(cudaMemcpyAsync(m->d[index], src, bytes, cudaMemcpyHostToDevice, m->ctx->stream));
+        CK(cudaStreamSynchronize(m->ctx->stream));
+        if (m->h[index]) std::memcpy(m->h[index], src, bytes);
+        m->dirty[index] = false;
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+API int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, float stddev, char *error,
+                                 int capacity) {
+    if (!live_matrix(matrix) || !(stddev > 0.0f)) {
+        set_error(error, capacity, "Invalid synthetic weight request");
+        return -1;
+    }
+    Matrix *m = static_cast<Matrix *>(matrix);
+    DeviceGuard dg(m->ctx->device);
+    try {
+        const int64_t rows = (int64_t)m->experts * m->rows;
+        const int64_t groups = rows * (m->cols / 64);
+        const float scale = (1.7320508075688772f / 65536.0f) * stddev;
+        gen_quant_kernel<<<(unsigned)((groups + 127) / 128), 128, 0, m->ctx->stream>>>(
+            stream_base(seed, stream), scale, rows, m->cols, m->bits, (uint32_t *)m->d[0], (uint16_t *)m->d[1],
+            (uint16_t *)m->d[2]);
+        CK(cudaGetLastError());
+        CK(cudaStreamSynchronize(m->ctx->stream));
+        for (int i = 0; i < 3; ++i) {
+            m->dirty[i] = false;
+            if (m->h[i]) CK(cudaMemcpy(m->h[i], m->d[i], m->bytes[i], cudaMemcpyDeviceToHost));
+        }
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+API void di_quant_matrix_destroy(void *matrix) {
+    if (!live_matrix(matrix)) return;
+    Matrix *m = static_cast<Matrix *>(matrix);
+    m->destroyed = true;
+    Context *c = m->ctx;
+    DeviceGuard dg(c->device);
+    cudaStreamSynchronize(c->stream);
+    release_matrix(m);
+}
+
+API int di_quant_batch(void *ctx, const di_quant_job *jobs, int count, double *ms, char *error, int capacity) {
+    if (!live_context(ctx) || !jobs || count < 1 || count > 8) {
+        set_error(error, capacity, "Invalid GEMV batch");
+        return -1;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    for (int j = 0; j < count; ++j) {
+        const di_quant_job &job = jobs[j];
+        if (!live_matrix(job.matrix) || !job.input || !job.output || !job.experts || job.count < 1 || job.count > 8) {
+            set_error(error, capacity, "Invalid quantized GEMV arguments");
+            return -1;
+        }
+        Matrix *m = static_cast<Matrix *>(job.matrix);
+        if (m->ctx != c) {
+            set_error(error, capacity, "Batch matrices must belong to this device.");
+            return -1;
+        }
+        for (int i = 0; i < job.count; ++i)
+            if (job.experts[i] >= (uint32_t)m->experts) {
+                set_error(error, capacity, "Expert ID out of bounds");
+                return -1;
+            }
+        for (int i = 0; i < j; ++i)
+            if (jobs[i].matrix == job.matrix) {
+                set_error(error, capacity, "Batch matrices must be distinct");
+                return -1;
+            }
+    }
+    DeviceGuard dg(c->device);
+    try {
+        Carve cv;
+        std::vector<size_t> o_in(count), o_out(count), o_ex(count);
+        for (int j = 0; j < count; ++j) {
+            const Matrix *m = static_cast<Matrix *>(jobs[j].matrix);
+            o_in[j] = cv.take<float>((size_t)m->cols * (jobs[j].batched ? jobs[j].count : 1));
+            o_out[j] = cv.take<float>((size_t)m->rows * jobs[j].count);
+            o_ex[j] = cv.take<uint32_t>(8);
+        }
+        size_t o_jobs = cv.take<GemvJob>(8);
+        ensure_workspace(c, cv.off + 256);
+        std::vector<GemvJob> hj(count);
+        int max_warps = 0;
+        for (int j = 0; j < count; ++j) {
+            Matrix *m = static_cast<Matrix *>(jobs[j].matrix);
+            sync_matrix(m);
+            const size_t nin = (size_t)m->cols * (jobs[j].batched ? jobs[j].count : 1);
+            CK(cudaMemcpyAsync(at<float>(c, o_in[j]), jobs[j].input, nin * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(at<uint32_t>(c, o_ex[j]), jobs[j].experts, jobs[j].count * 4, cudaMemcpyHostToDevice,
+                               c->stream));
+            hj[j] = GemvJob{m->view(), at<float>(c, o_in[j]), at<float>(c, o_out[j]), at<uint32_t>(c, o_ex[j]),
+                            jobs[j].count, jobs[j].batched ? 1 : 0};
+            max_warps = std::max(max_warps, m->rows * jobs[j].count);
+        }
+        CK(cudaMemcpyAsync(at<GemvJob>(c, o_jobs), hj.data(), sizeof(GemvJob) * count, cudaMemcpyHostToDevice,
+                           c->stream));
+        CK(cudaEventRecord(c->ev_start, c->stream));
+        quant_gemv_kernel<<<dim3((max_warps + 7) / 8, count), 256, 0, c->stream>>>(at<GemvJob>(c, o_jobs));
+        if (launch_check(error, capacity)) return -1;
+        CK(cudaEventRecord(c->ev_stop, c->stream));
+        for (int j = 0; j < count; ++j) {
+            const Matrix *m = static_cast<Matrix *>(jobs[j].matrix);
+            CK(cudaMemcpyAsync(jobs[j].output, at<float>(c, o_out[j]), (size_t)m->rows * jobs[j].count * 4,
+                               cudaMemcpyDeviceToHost, c->stream));
+        }
+        CK(cudaStreamSynchronize(c->stream));
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
+        if (ms) *ms = t;
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+API int di_quant_matvec(void *ctx, void *matrix, const float *x, float *y, const uint32_t *experts, int count,
+                        int batched, double *ms, char *error, int capacity) {
+    di_quant_job job{matrix, x, y, experts, count, batched};
+    return di_quant_batch(ctx, &job, 1, ms, error, capacity);
+}
+
+API int di_quant_experts(void *ctx, void *gate, void *up, void *down, void *shared, const float *input,
+                         const float *shared_input, const uint32_t *experts, int count, float *expert_output,
+                         float *shared_output, double *ms, char *error, int capacity) {
+    // quantized.mm:354-361 checks, plus context ownership
+    Matrix *g = live_matrix(gate) ? static_cast<Matrix *>(gate) : nullptr;
+    Matrix *u = live_matrix(up) ? static_cast<Matrix *>(up) : nullptr;
+    Matrix *d = live_matrix(down) ? static_cast<Matrix *>(down) : nullptr;
+    Matrix *s = live_matrix(shared) ? static_cast<Matrix *>(shared) : nullptr;
+    if (!live_context(ctx) || !g || !u || !d || !s || !input || !shared_input || !experts || !expert_output ||
+        !shared_output || count < 1 || count > 8 || g == u || g == d || g == s || u == d || u == s || d == s ||
+        g->rows != u->rows || g->cols != u->cols || g->experts != u->experts || g->bits != u->bits ||
+        d->experts != g->experts || d->cols != g->rows || d->rows != g->cols || s->experts != 1 ||
+        s->rows != d->rows) {
+        set_error(error, capacity, "Incompatible fused expert matrices/arguments");
+        return -1;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    if (g->ctx != c || u->ctx != c || d->ctx != c || s->ctx != c) {
+        set_error(error, capacity, "Expert matrices must belong to this device.");
+        return -1;
+    }
+    for (int i = 0; i < count; ++i)
+        if (experts[i] >= (uint32_t)g->experts) {
+            set_error(error, capacity, "Expert ID out of bounds");
+            return -1;
+        }
+    DeviceGuard dg(c->device);
+    try {
+        Carve cv;
+        size_t o_x = cv.take<float>(g->cols), o_sx = cv.take<float>(s->cols), o_ex = cv.take<uint32_t>(8);
+        size_t o_act = cv.take<float>((size_t)g->rows * count), o_y = cv.take<float>((size_t)d->rows * count);
+        size_t o_sy = cv.take<float>(s->rows), o_jobs = cv.take<GemvJob>(2), o_zero = cv.take<uint32_t>(1);
+        ensure_workspace(c, cv.off + 256);
+        for (Matrix *m : {g, u, d, s}) sync_matrix(m);
+        CK(cudaMemcpyAsync(at<float>(c, o_x), input, (size_t)g->cols * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(at<float>(c, o_sx), shared_input, (size_t)s->cols * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(at<uint32_t>(c, o_ex), experts, (size_t)count * 4, cudaMemcpyHostToDevice, c->stream));
+        GemvJob hj[2] = {
+            GemvJob{d->view(), at<float>(c, o_act), at<float>(c, o_y), at<uint32_t>(c, o_ex), count, 1},
+            GemvJob{s->view(), at<float>(c, o_sx), at<float>(c, o_sy), at<uint32_t>(c, o_zero), 1, 0}};
+        CK(cudaMemsetAsync(at<uint32_t>(c, o_zero), 0, 4, c->stream));
+        CK(cudaMemcpyAsync(at<GemvJob>(c, o_jobs), hj, sizeof(hj), cudaMemcpyHostToDevice, c->stream));
+        CK(cudaEventRecord(c->ev_start, c->stream));
+        quant_gate_up_kernel<<<(g->rows * count + 7) / 8, 256, 0, c->stream>>>(g->view(), u->view(), at<float>(c, o_x),
+                                                                              at<uint32_t>(c, o_ex), count,
+                                                                              at<float>(c, o_act));
+        const int warps = std::max(d->rows * count, s->rows);
+        quant_gemv_kernel<<<dim3((warps + 7) / 8, 2), 256, 0, c->stream>>>(at<GemvJob>(c, o_jobs));
+        if (launch_check(error, capacity)) return -1;
+        CK(cudaEventRecord(c->ev_stop, c->stream));
+        CK(cudaMemcpyAsync(expert_output, at<float>(c, o_y), (size_t)d->rows * count * 4, cudaMemcpyDeviceToHost,
+                           c->stream));
+        CK(cudaMemcpyAsync(shared_output, at<float>(c, o_sy), (size_t)s->rows * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
+        if (ms) *ms = t;
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+API int di_quant_embedding(void *matrix, int token, float *out) {
+    if (!live_matrix(matrix) || !out) return -1;
+    Matrix *m = static_cast<Matrix *>(matrix);
+    if (token < 0 || token >= m->rows || m->experts != 1) return -1;
+    Context *c = m->ctx;
+    DeviceGuard dg(c->device);
+    try {
+        Carve cv;
+        size_t o = cv.take<float>(m->cols);
+        ensure_workspace(c, cv.off + 256);
+        sync_matrix(m);
+        embedding_kernel<<<(m->cols + 255) / 256, 256, 0, c->stream>>>(m->view(), token, at<float>(c, o));
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(out, at<float>(c, o), (size_t)m->cols * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+    } catch (const CudaFail &) {
+        return -1;
+    }
+    return 0;
+}
+
+// ============================================================================ Part 2
+
+API void *di_moe_layer_create(void *ctx, void *router, void *gate, void *up, void *down, void *shared_gate,
+                              void *shared_up, void *shared_down, void *shared_route, char *error, int capacity) {
+    void *ptrs[8] = {router, gate, up, down, shared_gate, shared_up, shared_down, shared_route};
+    if (!live_context(ctx)) {
+        set_error(error, capacity, "Invalid context");
+        return nullptr;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    Matrix *m[8];
+    for (int i = 0; i < 8; ++i) {
+        if (!live_matrix(ptrs[i])) {
+            set_error(error, capacity, "MoE layer matrix %d is missing or destroyed", i);
+            return nullptr;
+        }
+        m[i] = static_cast<Matrix *>(ptrs[i]);
+        if (m[i]->ctx != c) {
+            set_error(error, capacity, "MoE layer matrices must belong to this device.");
+            return nullptr;
+        }
+        for (int j = 0; j < i; ++j)
+            if (m[j] == m[i]) {
+                set_error(error, capacity, "MoE layer matrices must be distinct.");
+                return nullptr;
+            }
+    }
+    const int E = m[0]->rows, D = m[0]->cols, I = m[1]->rows, bits = m[1]->bits;
+    auto shape = [](Matrix *x, int e, int r, int col) { return x->experts == e && x->rows == r && x->cols == col; };
+    bool okg = m[0]->experts == 1 && m[0]->bits == 8 && E >= 8 && E <= 256 && D % 256 == 0 && I % 64 == 0 &&
+               shape(m[1], E, I, D) && shape(m[2], E, I, D) && shape(m[3], E, D, I) && shape(m[4], 1, I, D) &&
+               shape(m[5], 1, I, D) && shape(m[6], 1, D, I) && shape(m[7], 1, 1, D) && m[7]->bits == 8;
+    for (int i = 1; i < 7; ++i) okg = okg && m[i]->bits == bits;
+    if (!okg) {
+        set_error(error, capacity,
+                  "Unsupported MoE layer geometry: router [1,E,D] 8-bit, gate/up [E,I,D], down [E,D,I], shared "
+                  "[1,I,D]/[1,D,I], shared_route [1,1,D] 8-bit; E in [8,256], D %% 256 == 0, I %% 64 == 0");
+        return nullptr;
+    }
+    Layer *L = new Layer();
+    L->ctx = c;
+    for (int i = 0; i < 8; ++i) {
+        L->m[i] = m[i];
+        m[i]->refs++;
+    }
+    L->E = E;
+    L->D = D;
+    L->I = I;
+    L->bits = bits;
+    std::lock_guard<std::mutex> g(g_registry);
+    g_layers.insert(L);
+    return L;
+}
+
+API void di_moe_layer_destroy(void *layer) {
+    if (!live_layer(layer)) return;
+    Layer *L = static_cast<Layer *>(layer);
+    {
+        std::lock_guard<std::mutex> g(g_registry);
+        g_layers.erase(L);
+    }
+    DeviceGuard dg(L->ctx->device);
+    cudaStreamSynchronize(L->ctx->stream);
+    if (L->bias) cudaFree(L->bias);
+    for (int i = 0; i < 8; ++i) release_matrix(L->m[i]);
+    delete L;
+}
+
+API int di_moe_layer_set_router_bias(void *layer, const float *bias, char *error, int capacity) {
+    if (!live_layer(layer)) {
+        set_error(error, capacity, "Invalid MoE layer");
+        return -1;
+    }
+    Layer *L = static_cast<Layer *>(layer);
+    DeviceGuard dg(L->ctx->device);
+    try {
+        if (!bias) {
+            if (L->bias) CK(cudaFree(L->bias));
+            L->bias = nullptr;
+            return 0;
+        }
+        for (int e = 0; e < L->E; ++e)
+            if (!std::isfinite(bias[e])) {
+                set_error(error, capacity, "Router bias must be finite");
+                return -1;
+            }
+        if (!L->bias) CK(cudaMalloc(&L->bias, sizeof(float) * L->E));
+        CK(cudaMemcpyAsync(L->bias, bias, sizeof(float) * L->E, cudaMemcpyHostToDevice, L->ctx->stream));
+        CK(cudaStreamSynchronize(L->ctx->stream));
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+namespace {
+bool pick_gemv(int T, int flags) {
+    if (flags & DI_MOE_PATH_GEMV) return true;
+    if (flags & DI_MOE_PATH_GROUPED) return false;
+    return T <= 4;
+}
+}  // namespace
+
+API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint16_t *y, int32_t *ids, float *probs,
+                     int flags, double *ms, char *error, int capacity) {
+    if (!live_context(ctx) || !live_layer(layer)) {
+        set_error(error, capacity, "Invalid context or MoE layer");
+        return -1;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    Layer *L = static_cast<Layer *>(layer);
+    const bool dev_io = flags & DI_MOE_DEVICE_IO, forced = flags & DI_MOE_FORCE_ROUTES;
+    if (L->ctx != c) {
+        set_error(error, capacity, "MoE layer must belong to this device.");
+        return -1;
+    }
+    if (!x || !y || tokens < 1 || tokens > 65536 || (flags & ~15) ||
+        ((flags & DI_MOE_PATH_GEMV) && (flags & DI_MOE_PATH_GROUPED)) || (forced && !ids) ||
+        ((flags & DI_MOE_PATH_GEMV) && tokens > 64)) {
+        set_error(error, capacity, "Invalid MoE block arguments");
+        return -1;
+    }
+    for (int i = 0; i < 8; ++i)
+        if (L->m[i]->destroyed) {
+            set_error(error, capacity, "MoE layer matrix was destroyed");
+            return -1;
+        }
+    if (forced && !dev_io)
+        for (size_t i = 0; i < (size_t)tokens * 8; ++i)
+            if (ids[i] < 0 || ids[i] >= L->E) {
+                set_error(error, capacity, "Expert ID out of bounds");
+                return -1;
+            }
+    const int T = tokens, D = L->D;
+    const bool gemv = pick_gemv(T, flags);
+    DeviceGuard dg(c->device);
+    try {
+        for (int i = 0; i < 8; ++i) sync_matrix(L->m[i]);
+        Carve cv;
+        BlockBuffers b{};
+        size_t o_ids_io = 0, o_probs_io = 0;
+        if (!dev_io) {
+            o_ids_io = cv.take<int32_t>((size_t)T * 8);
+            o_probs_io = cv.take<float>((size_t)T * 8);
+        }
+        plan_block(c, L, T, cv, b, !dev_io, gemv);
+        const uint16_t *dx = dev_io ? x : b.x;
+        uint16_t *dy = dev_io ? y : b.y;
+        int32_t *dids = dev_io ? ids : at<int32_t>(c, o_ids_io);
+        float *dprobs = dev_io ? probs : at<float>(c, o_probs_io);
+        CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
+        CK(cudaEventRecord(c->ev_start, c->stream));
+        if (!dev_io) {
+            CK(cudaMemcpyAsync(b.x, x, (size_t)T * D * 2, cudaMemcpyHostToDevice, c->stream));
+            if (forced) CK(cudaMemcpyAsync(dids, ids, (size_t)T * 8 * 4, cudaMemcpyHostToDevice, c->stream));
+        }
+        const bool profile = true;
+        g_marks = nullptr;
+        enqueue_block(c, L, dx, T, dy, nullptr, forced ? dids : nullptr, (dev_io && !probs) ? nullptr : dprobs, gemv,
+                      b, profile);
+        if (ids && !forced) {
+            if (dev_io) CK(cudaMemcpyAsync(ids, b.ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, c->stream));
+            else CK(cudaMemcpyAsync(dids, b.ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, c->stream));
+        }
+        if (launch_check(error, capacity)) return -1;
+        CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+        if (dev_io) CK(cudaEventRecord(c->ev_stop, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        if (*c->h_err) {
+            set_error(error, capacity, "%s", device_error_text(*c->h_err));
+            return -1;
+        }
+        if (!dev_io) {
+            // outputs reach the caller only after the device reported success; `ms` covers the
+            // host->device copies, the block and these device->host copies
+            CK(cudaMemcpyAsync(y, b.y, (size_t)T * D * 2, cudaMemcpyDeviceToHost, c->stream));
+            if (ids && !forced) CK(cudaMemcpyAsync(ids, dids, (size_t)T * 8 * 4, cudaMemcpyDeviceToHost, c->stream));
+            if (probs) CK(cudaMemcpyAsync(probs, dprobs, (size_t)T * 8 * 4, cudaMemcpyDeviceToHost, c->stream));
+            CK(cudaEventRecord(c->ev_stop, c->stream));
+            CK(cudaStreamSynchronize(c->stream));
+        }
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
+        if (ms) *ms = t;
+        for (int s = 0; s < S_N; ++s) {
+            float st = 0;
+            cudaEventElapsedTime(&st, c->ev_stage[s], c->ev_stage[s + 1]);
+            c->last_stage_ms[s] = st;
+        }
+        c->last_stage_ms[S_N] = 0;
+        c->have_profile = true;
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_layers, float eps, float *x, int tokens,
+                     uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error, int capacity) {
+    if (!live_context(ctx) || !layers || n_layers < 1 || n_layers > 1024 || !norms || !x || tokens < 1 ||
+        tokens > 65536 || !(eps > 0.0f) ||
+        (flags & ~(DI_MOE_DEVICE_IO | DI_MOE_PATH_GEMV | DI_MOE_PATH_GROUPED | DI_MOE_PROFILE)) ||
+        ((flags & DI_MOE_PATH_GEMV) && (flags & DI_MOE_PATH_GROUPED)) || ((flags & DI_MOE_PATH_GEMV) && tokens > 64)) {
+        set_error(error, capacity, "Invalid MoE stack arguments");
+        return -1;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    int D = -1;
+    for (int l = 0; l < n_layers; ++l) {
+        if (!live_layer(layers[l]) || static_cast<Layer *>(layers[l])->ctx != c) {
+            set_error(error, capacity, "Invalid MoE layer %d", l);
+            return -1;
+        }
+        Layer *L = static_cast<Layer *>(layers[l]);
+        if (D < 0) D = L->D;
+        if (L->D != D) {
+            set_error(error, capacity, "MoE stack layers must share the hidden size");
+            return -1;
+        }
+        for (int i = 0; i < 8; ++i)
+            if (L->m[i]->destroyed) {
+                set_error(error, capacity, "MoE layer matrix was destroyed");
+                return -1;
+            }
+    }
+    const bool dev_io = flags & DI_MOE_DEVICE_IO, profile = flags & DI_MOE_PROFILE;
+    const int T = tokens;
+    const bool gemv = pick_gemv(T, flags);
+    DeviceGuard dg(c->device);
+    try {
+        const size_t need_events = profile ? (size_t)n_layers * (S_N + 2) : 0;
+        while (c->layer_events.size() < need_events) {
+            cudaEvent_t e;
+            CK(cudaEventCreate(&e));
+            c->layer_events.push_back(e);
+        }
+        for (int l = 0; l < n_layers; ++l)
+            for (int i = 0; i < 8; ++i) sync_matrix(static_cast<Layer *>(layers[l])->m[i]);
+        Carve cv;
+        size_t o_x = dev_io ? 0 : cv.take<float>((size_t)T * D);
+        size_t o_n = dev_io ? 0 : cv.take<float>((size_t)n_layers * D);
+        size_t o_h = cv.take<uint16_t>((size_t)T * D);
+        size_t o_ht = (!dev_io && h_trace) ? cv.take<uint16_t>((size_t)n_layers * T * D) : 0;
+        size_t o_it = (!dev_io && ids_trace) ? cv.take<int32_t>((size_t)n_layers * T * 8) : 0;
+        int Emax = 0, Imax = 0;
+        for (int l = 0; l < n_layers; ++l) {
+            Emax = std::max(Emax, static_cast<Layer *>(layers[l])->E);
+            Imax = std::max(Imax, static_cast<Layer *>(layers[l])->I);
+        }
+        BlockBuffers b{};
+        // size the block buffers for the widest layer (layers of one stack share E and I in practice)
+        Layer probe = *static_cast<Layer *>(layers[0]);
+        probe.E = Emax;
+        probe.I = Imax;
+        plan_block(c, &probe, T, cv, b, false, gemv);
+        float *dx = dev_io ? x : at<float>(c, o_x);
+        const float *dn = dev_io ? norms : at<float>(c, o_n);
+        uint16_t *dh = at<uint16_t>(c, o_h);
+        uint16_t *dht = dev_io ? h_trace : (h_trace ? at<uint16_t>(c, o_ht) : nullptr);
+        int32_t *dit = dev_io ? ids_trace : (ids_trace ? at<int32_t>(c, o_it) : nullptr);
+        CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
+        CK(cudaEventRecord(c->ev_start, c->stream));
+        if (!dev_io) {
+            CK(cudaMemcpyAsync(dx, x, (size_t)T * D * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(const_cast<float *>(dn), norms, (size_t)n_layers * D * 4, cudaMemcpyHostToDevice,
+                               c->stream));
+        }
+        for (int l = 0; l < n_layers; ++l) {
+            Layer *L = static_cast<Layer *>(layers[l]);
+            cudaEvent_t *ev = profile ? &c->layer_events[(size_t)l * (S_N + 2)] : nullptr;
+            if (profile) CK(cudaEventRecord(ev[S_N + 1], c->stream));
+            rmsnorm_kernel<<<T, 256, 0, c->stream>>>(dx, dn + (size_t)l * D, D, eps, dh,
+                                                     dht ? dht + (size_t)l * T * D : nullptr);
+            g_marks = ev;
+            enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, gemv, b, profile);
+            g_marks = nullptr;
+            if (dit)
+                CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, b.ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice,
+                                   c->stream));
+        }
+        if (launch_check(error, capacity)) return -1;
+        CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+        if (dev_io) CK(cudaEventRecord(c->ev_stop, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        if (*c->h_err) {
+            set_error(error, capacity, "%s", device_error_text(*c->h_err));
+            return -1;
+        }
+        if (!dev_io) {
+            CK(cudaMemcpyAsync(x, dx, (size_t)T * D * 4, cudaMemcpyDeviceToHost, c->stream));
+            if (h_trace)
+                CK(cudaMemcpyAsync(h_trace, dht, (size_t)n_layers * T * D * 2, cudaMemcpyDeviceToHost, c->stream));
+            if (ids_trace)
+                CK(cudaMemcpyAsync(ids_trace, dit, (size_t)n_layers * T * 8 * 4, cudaMemcpyDeviceToHost, c->stream));
+            CK(cudaEventRecord(c->ev_stop, c->stream));
+            CK(cudaStreamSynchronize(c->stream));
+        }
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
+        if (ms) *ms = t;
+        if (profile) {
+            for (int s = 0; s < kProfileSlots; ++s) c->last_stage_ms[s] = 0;
+            for (int l = 0; l < n_layers; ++l) {
+                cudaEvent_t *ev = &c->layer_events[(size_t)l * (S_N + 2)];
+                for (int s = 0; s < S_N; ++s) {
+                    float st = 0;
+                    CK(cudaEventElapsedTime(&st, ev[s], ev[s + 1]));
+                    c->last_stage_ms[s] += st;
+                }
+                float rn = 0;
+                CK(cudaEventElapsedTime(&rn, ev[S_N + 1], ev[S_ROUTER]));
+                c->last_stage_ms[S_N] += rn;
+            }
+            c->have_profile = true;
+        }
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+API int di_moe_last_profile(void *ctx, double *stage_ms, int n) {
+    if (!live_context(ctx) || !stage_ms || n < 1) return 0;
+    Context *c = static_cast<Context *>(ctx);
+    if (!c->have_profile) return 0;
+    const int k = std::min(n, kProfileSlots);
+    for (int i = 0; i < k; ++i) stage_ms[i] = c->last_stage_ms[i];
+    return k;
+}

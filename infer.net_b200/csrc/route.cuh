@@ -1,0 +1,428 @@
+// Router, top-8 selection and the stable expert-grouped permutation.
+//
+// Router logits follow one fixed f32 evaluation order so that expert ids are reproducible
+// bit for bit by the CPU oracle: lane l of a 32-lane group owns columns 256*b + 8*l + j
+// (j = 0..7), accumulated b-major with w = fma(q, scale, bias) and acc = fma(w, x, acc),
+// then the xor butterfly 16,8,4,2,1 -- the lane partition and reduction of the reference
+// CUDA gemv kernel (native/DeepInfer.Cuda/split_prefix.cu:63-67, :106-120).
+#pragma once
+#include "common.cuh"
+
+namespace di {
+
+// ------------------------------------------------------------------ shared helpers
+
+// fma over a pair of f32 lanes: d = a*b + c elementwise, one rounding each (sm_100 FFMA2).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// Canonical dot product of one 8-bit router row with one bf16 activation row, evaluated
+// by a whole warp; returns the same value in every lane.
+__device__ __forceinline__ float canonical_dot_warp(const QView &m, int row, const uint16_t *x, int D) {
+    const uint32_t lane = lane_id();
+    const uint32_t *w = m.packed + (size_t)row * m.words_per_row();
+    const uint16_t *sc = m.scales + (size_t)row * m.groups_per_row();
+    const uint16_t *bi = m.biases + (size_t)row * m.groups_per_row();
+    float acc = 0.0f;
+    for (int base = lane * 8; base < D; base += 256) {
+        uint2 q = __ldg(reinterpret_cast<const uint2 *>(w + base / 4));
+        uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x + base));
+        float s = bf16_bits_to_f32(__ldg(sc + base / 64)), b = bf16_bits_to_f32(__ldg(bi + base / 64));
+        uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float wv = fmaf(byte_to_f32(j < 4 ? q.x : q.y, j & 3), s, b);
+            float xf = (j & 1) ? bf16_hi(xw[j >> 1]) : bf16_lo(xw[j >> 1]);
+            acc = fmaf(wv, xf, acc);
+        }
+    }
+    return warp_sum_butterfly(acc);
+}
+
+// ------------------------------------------------------------------ router GEMM (SIMT)
+//
+// logits[t, e] for a tile of 32 tokens x 16 experts per CTA (8 warps: 4 token groups x 2
+// expert groups, 8x8 outputs per warp). Each 256-column block of x and of the 8-bit codes
+// is staged in shared memory (double buffered with cp.async); every lane keeps 64 partial
+// sums in the canonical order and the warp reduces them with the butterfly at the end.
+namespace router {
+constexpr int TT = 32, TE = 16, KB = 256, THREADS = 256;
+struct Smem {
+    uint16_t x[2][TT][KB];        // 16 KB per stage
+    uint8_t w[2][TE][KB];         // 4 KB per stage
+    uint16_t s[2][TE][KB / 64];
+    uint16_t b[2][TE][KB / 64];
+};
+}  // namespace router
+
+__global__ void __launch_bounds__(router::THREADS, 1)
+router_logits_kernel(const uint16_t *__restrict__ x, int T, int D, QView W, const float *__restrict__ bias,
+                     float *__restrict__ logits) {
+    using namespace router;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
+    const int E = W.rows;
+    const int wt = (warp & 3) * 8, we = (warp >> 2) * 8;  // warp's token / expert offsets in the tile
+    const int nkb = D / KB;
+    const int wpr = W.words_per_row(), gpr = W.groups_per_row();
+
+    auto stage = [&](int kb, int buf) {
+        // x: 32 rows x 512 B = 1024 chunks of 16 B, 4 per thread
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            int c = tid + i * THREADS, r = c >> 5, ch = c & 31;
+            int t = t0 + r;
+            const uint16_t *src = x + (size_t)min(t, T - 1) * D + kb * KB + ch * 8;
+            cp_async_16(&sm.x[buf][r][ch * 8], src, t < T);
+        }
+        // codes: 16 rows x 256 B = 256 chunks, 1 per thread
+        {
+            int r = tid >> 4, ch = tid & 15, e = e0 + r;
+            const uint32_t *src = W.packed + (size_t)min(e, E - 1) * wpr + kb * (KB / 4) + ch * 4;
+            cp_async_16(&sm.w[buf][r][ch * 16], src, e < E);
+        }
+        if (tid < TE) {
+            int e = min(e0 + tid, E - 1);
+            const uint16_t *ss = W.scales + (size_t)e * gpr + kb * (KB / 64);
+            const uint16_t *bb = W.biases + (size_t)e * gpr + kb * (KB / 64);
+#pragma unroll
+            for (int g = 0; g < KB / 64; ++g) {
+                sm.s[buf][tid][g] = __ldg(ss + g);
+                sm.b[buf][tid][g] = __ldg(bb + g);
+            }
+        }
+        cp_async_commit();
+    };
+
+    float2 acc[4][8];  // [token pair][expert]: (token 2p, token 2p+1)
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[p][e] = make_float2(0.f, 0.f);
+
+    stage(0, 0);
+    for (int kb = 0; kb < nkb; ++kb) {
+        const int buf = kb & 1;
+        if (kb + 1 < nkb) {
+            stage(kb + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        // x values of this lane's 8 columns for the warp's 8 tokens, as f32 pairs (t, t+1)
+        float2 xp[4][8];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            uint4 a = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p][lane * 8]);
+            uint4 c = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p + 1][lane * 8]);
+            uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                xp[p][j] = make_float2((j & 1) ? bf16_hi(aw[j >> 1]) : bf16_lo(aw[j >> 1]),
+                                       (j & 1) ? bf16_hi(cw[j >> 1]) : bf16_lo(cw[j >> 1]));
+        }
+        const int g = lane >> 3;  // group of columns 8*lane .. 8*lane+7 within the 256 block
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            uint2 q = *reinterpret_cast<const uint2 *>(&sm.w[buf][we + e][lane * 8]);
+            float s = bf16_bits_to_f32(sm.s[buf][we + e][g]), b = bf16_bits_to_f32(sm.b[buf][we + e][g]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float wv = fmaf(byte_to_f32(j < 4 ? q.x : q.y, j & 3), s, b);
+                float2 w2 = make_float2(wv, wv);
+#pragma unroll
+                for (int p = 0; p < 4; ++p) acc[p][e] = ffma2(xp[p][j], w2, acc[p][e]);
+            }
+        }
+        __syncthreads();
+    }
+    // butterfly per output, then lane (e) writes
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float a = warp_sum_butterfly(acc[p][e].x), c = warp_sum_butterfly(acc[p][e].y);
+            if (lane == e) {
+                int ee = e0 + we + e, ta = t0 + wt + 2 * p;
+                if (ee < E) {
+                    float bb = bias ? bias[ee] : 0.f;
+                    if (ta < T) logits[(size_t)ta * E + ee] = a + bb;
+                    if (ta + 1 < T) logits[(size_t)(ta + 1) * E + ee] = c + bb;
+                }
+            }
+        }
+}
+
+// Decode-sized router: one warp per expert row, all T (<= 8) tokens per warp.
+__global__ void router_logits_gemv_kernel(const uint16_t *__restrict__ x, int T, int D, QView W,
+                                          const float *__restrict__ bias, float *__restrict__ logits) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (warp >= W.rows) return;
+    const float bb = bias ? bias[warp] : 0.f;
+    for (int t = 0; t < T; ++t) {
+        float v = canonical_dot_warp(W, warp, x + (size_t)t * D, D);
+        if (lane_id() == 0) logits[(size_t)t * W.rows + warp] = v + bb;
+    }
+}
+
+// ------------------------------------------------------------------ top-8 + histogram
+//
+// One warp per token. Selection: 8 rounds of a warp arg-max over (value desc, index asc),
+// i.e. the 8 largest logits in descending order with ties to the lower expert id
+// (Qwen36Model.cs:246-258; graph_top8 in gpu_graph.mm:134-146). probs = softmax over the
+// 8 chosen logits (Qwen36Model.cs:259-261, :293-298). Non-finite logits set kErrNonFinite.
+// The warp also computes the shared-route gate logit (canonical order). Each CTA owns a
+// contiguous token range and writes the per-expert route counts of that range.
+namespace topk {
+constexpr int WARPS = 8, TOK_PER_WARP = 8, TOK_PER_CTA = WARPS * TOK_PER_WARP;  // 64 tokens = 512 routes
+}
+
+__global__ void __launch_bounds__(topk::WARPS * 32)
+topk_count_kernel(const float *__restrict__ logits, int T, int E, const uint16_t *__restrict__ x, int D,
+                  QView gateW, const int32_t *__restrict__ forced_ids, int32_t *__restrict__ ids, float *__restrict__ probs,
+                  float *__restrict__ gate_logit, int32_t *__restrict__ block_counts, uint32_t *__restrict__ err) {
+    using namespace topk;
+    __shared__ int32_t hist[256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int k = 0; k < TOK_PER_WARP; ++k) {
+        const int t = blockIdx.x * TOK_PER_CTA + warp * TOK_PER_WARP + k;
+        if (t >= T) break;
+        const float *lg = logits + (size_t)t * E;
+        int32_t sel[8];
+        float chosen[8];
+        if (forced_ids) {
+            // graph_force_route (gpu_graph.mm:153-159): ids given, probs from their logits;
+            // out-of-range ids are flagged and clamped so later kernels stay in bounds
+            bool bad = false;
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                int id = forced_ids[(size_t)t * 8 + n];
+                bad |= (id < 0 || id >= E);
+                sel[n] = min(max(id, 0), E - 1);
+                chosen[n] = lg[sel[n]];
+            }
+            if (bad && lane == 0) atomicOr(err, kErrBadExpert);
+        } else {
+            float v[8];
+            bool nonfinite = false;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                int e = lane + 32 * j;
+                v[j] = e < E ? lg[e] : 0.f;
+                // a non-finite logit fails the call; it is ranked as -inf so that the
+                // selection stays well defined (valid, distinct ids) for the later kernels
+                if (e < E && !isfinite(v[j])) {
+                    nonfinite = true;
+                    v[j] = -INFINITY;
+                }
+            }
+            if (__any_sync(kFull, nonfinite) && lane == 0) atomicOr(err, kErrNonFinite);
+            uint32_t used = 0;  // bit j: candidate lane+32j taken
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                float best = -INFINITY;
+                int bid = 0x7fffffff;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    int e = lane + 32 * j;
+                    bool ok = e < E && !((used >> j) & 1u);
+                    if (ok && (v[j] > best || bid == 0x7fffffff)) {
+                        best = v[j];
+                        bid = e;
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    float ob = __shfl_xor_sync(kFull, best, off);
+                    int oi = __shfl_xor_sync(kFull, bid, off);
+                    if (oi != 0x7fffffff && (bid == 0x7fffffff || ob > best || (ob == best && oi < bid))) {
+                        best = ob;
+                        bid = oi;
+                    }
+                }
+                sel[n] = bid;
+                chosen[n] = best;
+                if ((bid & 31) == lane) used |= 1u << (bid >> 5);
+            }
+        }
+        // softmax over the chosen logits
+        float mx = chosen[0];
+#pragma unroll
+        for (int n = 1; n < 8; ++n) mx = fmaxf(mx, chosen[n]);
+        float p[8], sum = 0.f;
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+            p[n] = expf(chosen[n] - mx);
+            sum += p[n];
+        }
+        float g = canonical_dot_warp(gateW, 0, x + (size_t)t * D, D);
+        if (lane < 8) {
+            int n = lane;
+            float pv = 0.f;
+            int32_t sv = 0;
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+                if (m == n) {
+                    pv = p[m];
+                    sv = sel[m];
+                }
+            ids[(size_t)t * 8 + n] = sv;
+            probs[(size_t)t * 8 + n] = pv / sum;
+            atomicAdd(&hist[sv], 1);
+        }
+        if (lane == 0) gate_logit[t] = g;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < E; i += blockDim.x) block_counts[(size_t)blockIdx.x * E + i] = hist[i];
+}
+
+// ------------------------------------------------------------------ scan + tile list
+//
+// Single CTA. For expert e: block_base[blk][e] = routes of e in blocks before blk;
+// counts[e]; segment offsets (exclusive scan over experts). The shared expert is segment E
+// with T rows placed after all routed rows (offset 8T). Emits the work tiles of the
+// grouped GEMMs: (segment, first row, valid rows) with at most `bn` rows each.
+struct Tile {
+    int32_t seg, p0, n;
+};
+
+__global__ void __launch_bounds__(1024)
+scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int E, int T, int bn,
+                  int32_t *__restrict__ block_base, int32_t *__restrict__ seg_count, int32_t *__restrict__ seg_off,
+                  Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles, int max_tiles, uint32_t *__restrict__ err) {
+    __shared__ int32_t cnt[257], ntile[257], toff[258], off[258];
+    const int tid = threadIdx.x;
+    if (tid < E) {
+        int run = 0;
+        for (int b = 0; b < nblocks; ++b) {
+            block_base[(size_t)b * E + tid] = run;
+            run += block_counts[(size_t)b * E + tid];
+        }
+        cnt[tid] = run;
+    }
+    if (tid == 0) cnt[E] = T;
+    __syncthreads();
+    if (tid <= E) ntile[tid] = (cnt[tid] + bn - 1) / bn;
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0, tr = 0;
+        for (int e = 0; e <= E; ++e) {
+            off[e] = (e == E) ? 8 * T : run;
+            run += (e < E) ? cnt[e] : 0;
+            toff[e] = tr;
+            tr += ntile[e];
+        }
+        toff[E + 1] = tr;
+        if (tr > max_tiles) {
+            atomicOr(err, kErrCapacity);
+            tr = 0;
+        }
+        *n_tiles = tr;
+    }
+    __syncthreads();
+    if (tid <= E) {
+        seg_count[tid] = cnt[tid];
+        seg_off[tid] = off[tid];
+        if (toff[E + 1] <= max_tiles)
+            for (int i = 0; i < ntile[tid]; ++i) {
+                int p0 = i * bn;
+                tiles[toff[tid] + i] = Tile{tid, off[tid] + p0, min(bn, cnt[tid] - p0)};
+            }
+    }
+}
+
+// ------------------------------------------------------------------ stable scatter
+//
+// Each CTA re-reads the routes of its token range in ascending route order and places
+// route r = t*8 + slot at seg_off[e] + block_base[blk][e] + (rank of r among earlier
+// routes of e in this block): the stable counting sort (prefill_moe.mm:12-14 order).
+__global__ void __launch_bounds__(32)
+scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32_t *__restrict__ block_base,
+                      const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route) {
+    __shared__ int32_t run[256];
+    const int lane = threadIdx.x;
+    for (int i = lane; i < E; i += 32) run[i] = 0;
+    __syncwarp();
+    const int r0 = blockIdx.x * topk::TOK_PER_CTA * 8;
+    const int r1 = min(r0 + topk::TOK_PER_CTA * 8, T * 8);
+    for (int base = r0; base < r1; base += 32) {
+        const int r = base + lane;
+        const bool valid = r < r1;
+        const int e = valid ? ids[r] : -1 - lane;  // invalid lanes never match real experts
+        const unsigned peers = __match_any_sync(kFull, e);
+        const int leader = __ffs(peers) - 1;
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        int b = 0;
+        if (valid && lane == leader) b = run[e];
+        b = __shfl_sync(kFull, b, leader);
+        __syncwarp();
+        if (valid && lane == leader) run[e] = b + __popc(peers);
+        if (valid) perm_route[seg_off[e] + block_base[(size_t)blockIdx.x * E + e] + b + rank] = r;
+        __syncwarp();
+    }
+}
+
+// ------------------------------------------------------------------ combine
+//
+// out[t] = sigmoid(gate_t) * shared[t] + sum_j p[t,j] * y[8t+j]   (Qwen36Model.cs:242-244),
+// f32 arithmetic in that order, rounded once to bf16. 8 columns per thread.
+__global__ void combine_kernel(const uint16_t *__restrict__ y, const uint16_t *__restrict__ ys,
+                               const float *__restrict__ gate_logit, const float *__restrict__ probs, int T, int D,
+                               uint16_t *__restrict__ out, float *__restrict__ resid,
+                               const uint32_t *__restrict__ err) {
+    const int per_tok = D / 8;
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)T * per_tok) return;
+    if (*err) return;  // a failed call leaves the output untouched
+    const int t = idx / per_tok, c = (idx % per_tok) * 8;
+    const float g = sigmoid_ref(gate_logit[t]);
+    float o[8];
+    {
+        uint4 v = *reinterpret_cast<const uint4 *>(ys + (size_t)t * D + c);
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = ((j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1])) * g;
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const float p = probs[(size_t)t * 8 + s];
+        uint4 v = *reinterpret_cast<const uint4 *>(y + ((size_t)t * 8 + s) * D + c);
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float prod = p * ((j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]));
+            o[j] = o[j] + prod;
+        }
+    }
+    if (out) {
+        uint4 r;
+        r.x = pack_bf16x2(o[0], o[1]);
+        r.y = pack_bf16x2(o[2], o[3]);
+        r.z = pack_bf16x2(o[4], o[5]);
+        r.w = pack_bf16x2(o[6], o[7]);
+        *reinterpret_cast<uint4 *>(out + (size_t)t * D + c) = r;
+    }
+    if (resid) {
+        float4 *rp = reinterpret_cast<float4 *>(resid + (size_t)t * D + c);
+        float4 a = rp[0], b = rp[1];
+        a.x += o[0]; a.y += o[1]; a.z += o[2]; a.w += o[3];
+        b.x += o[4]; b.y += o[5]; b.z += o[6]; b.w += o[7];
+        rp[0] = a;
+        rp[1] = b;
+    }
+}
+
+}  // namespace di

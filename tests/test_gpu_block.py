@@ -1,0 +1,168 @@
+"""GPU parity of the MoE block (di_moe_block / di_moe_stack) against the CPU oracle.
+
+Bar (north star): routing ids and the permutation bit-exact, ties to the lower expert id;
+block outputs within max-abs 2e-2 and relative-L2 5e-3 of the oracle's f32 reference
+semantics (Qwen36Model.cs:218-262) in bf16.
+"""
+import numpy as np
+import pytest
+
+import deepinfer_cuda as di
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, REL_L2 = 2e-2, 5e-3
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = di.Context(resident=0)
+    yield c
+    c.close()
+
+
+_layers = {}
+
+
+def layer_pair(ctx, seed, bits, E, D, I, layer=0):
+    key = (seed, bits, E, D, I, layer)
+    if key not in _layers:
+        L = O.Layer(seed, layer=layer, bits=bits, E=E, D=D, I=I)
+        _layers[key] = (L, di.MoeLayer.from_oracle(ctx, L))
+    return _layers[key]
+
+
+def check_block(ctx, L, G, T, flags, seed=5, forced=None):
+    x = O.gen_bf16(seed, O.ACT_STREAM + T, T * L.D).reshape(T, L.D)
+    y, ids, probs, ms = di.moe_block(G, x, flags, forced=forced)
+    rc, out, oids, oprobs, logits = O.moe_block(L, x, O.MODE_F32, forced=forced)
+    assert rc == 0
+    assert np.array_equal(ids, oids), "routing ids differ"
+    assert np.max(np.abs(probs - oprobs)) <= 1e-6
+    yf = O.bf16_to_f32(y).reshape(T, L.D)
+    ma, rl = O.tolerance_report(yf, out)
+    assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
+    return yf, out, ids
+
+
+@pytest.mark.parametrize("bits", [8, 5])
+@pytest.mark.parametrize("T", [1, 3])
+def test_decode_gemv_path_small_geometry(ctx, bits, T):
+    L, G = layer_pair(ctx, 31, bits, 64, 256, 128)
+    check_block(ctx, L, G, T, di.PATH_GEMV)
+
+
+@pytest.mark.parametrize("bits", [8, 5])
+@pytest.mark.parametrize("T", [1, 17, 64, 65, 200])
+def test_grouped_path_small_geometry(ctx, bits, T):
+    L, G = layer_pair(ctx, 32, bits, 64, 256, 128)
+    check_block(ctx, L, G, T, di.PATH_GROUPED)
+
+
+def test_grouped_path_row_tail(ctx):
+    # intermediate 192 = one full and one half 128-row tile of the grouped GEMM
+    L, G = layer_pair(ctx, 33, 8, 32, 512, 192)
+    check_block(ctx, L, G, 100, di.PATH_GROUPED)
+
+
+def test_grouped_matches_bf16_operand_oracle_tightly(ctx):
+    L, G = layer_pair(ctx, 34, 8, 64, 256, 128)
+    T = 96
+    x = O.gen_bf16(9, O.ACT_STREAM, T * L.D).reshape(T, L.D)
+    y, ids, _, _ = di.moe_block(G, x, di.PATH_GROUPED)
+    _, out, _, _, _ = O.moe_block(L, x, O.MODE_BF16OPS)
+    ma, rl = O.tolerance_report(O.bf16_to_f32(y).reshape(T, L.D), out)
+    assert rl < 2e-3, (ma, rl)
+
+
+@pytest.mark.parametrize("pattern", [0, 1, 2])
+def test_forced_route_patterns(ctx, pattern):
+    # prefill_expert_checks.mm:26-27 hot / scattered / skewed route patterns
+    L, G = layer_pair(ctx, 35, 8, 256, 256, 64)
+    T = 129
+    t = np.arange(T)[:, None]
+    s = np.arange(8)[None, :]
+    forced = [s + 0 * t, (t * 7 + s * 13) % 256, (t // 5 * 11 + s * 19) % 256][pattern].astype(np.int32)
+    check_block(ctx, L, G, T, di.PATH_GROUPED, forced=forced)
+
+
+def test_full_geometry_cfg0_prefill_512_tokens(ctx):
+    # T=512, hidden 2048, 256 experts, top-8, I=512, shared expert, 8-bit
+    L, G = layer_pair(ctx, 1, 8, 256, 2048, 512)
+    check_block(ctx, L, G, 512, 0)
+
+
+@pytest.mark.parametrize("bits", [8, 5])
+def test_full_geometry_decode_token(ctx, bits):
+    L, G = layer_pair(ctx, 2, bits, 256, 2048, 512)
+    check_block(ctx, L, G, 1, 0)
+
+
+def test_paths_agree_and_are_batch_independent(ctx):
+    # each token's result must not depend on which other tokens share the batch
+    L, G = layer_pair(ctx, 36, 8, 64, 256, 128)
+    T = 40
+    x = O.gen_bf16(12, O.ACT_STREAM, T * L.D).reshape(T, L.D)
+    y_all, ids_all, _, _ = di.moe_block(G, x, di.PATH_GROUPED)
+    y_a, ids_a, _, _ = di.moe_block(G, x[:17], di.PATH_GROUPED)
+    y_b, ids_b, _, _ = di.moe_block(G, x[17:], di.PATH_GROUPED)
+    assert np.array_equal(np.concatenate([ids_a, ids_b]), ids_all)
+    assert np.array_equal(np.concatenate([y_a, y_b]), y_all)
+
+
+def test_non_finite_input_fails_and_leaves_output(ctx):
+    L, G = layer_pair(ctx, 37, 8, 64, 256, 128)
+    T = 8
+    x = O.gen_bf16(13, O.ACT_STREAM, T * L.D).reshape(T, L.D)
+    x[3, 5] = 0x7FC0  # NaN
+    y = np.full_like(x, 0x1234)
+    for flags in (di.PATH_GROUPED, di.PATH_GEMV):
+        with pytest.raises(di.DeepInferError, match="Non-finite"):
+            G.block(x, T, y, None, None, flags)
+        assert np.all(y == 0x1234)
+
+
+def test_invalid_block_calls_rejected_before_submission(ctx):
+    L, G = layer_pair(ctx, 37, 8, 64, 256, 128)
+    x = np.zeros((4, 256), np.uint16)
+    y = np.full_like(x, 7)
+    with pytest.raises(di.DeepInferError):
+        G.block(x, 0, y)
+    with pytest.raises(di.DeepInferError):
+        G.block(x, 4, y, flags=di.PATH_GEMV | di.PATH_GROUPED)
+    bad = np.full((4, 8), 64, np.int32)
+    with pytest.raises(di.DeepInferError, match="out of bounds"):
+        G.block(x, 4, y, bad, None, di.FORCE_ROUTES)
+    assert np.all(y == 7)
+
+
+def test_zipf_router_bias_shifts_load(ctx):
+    E = 64
+    b = (-1.1 * np.log(np.arange(E) + 1.0)).astype(np.float32)
+    L = O.Layer(38, bits=8, E=E, D=256, I=64, router_bias=b)
+    G = di.MoeLayer.from_oracle(ctx, L)
+    _, _, ids = check_block(ctx, L, G, 256, di.PATH_GROUPED)
+    counts = np.bincount(ids.reshape(-1), minlength=E)
+    assert counts[:8].sum() > counts[-8:].sum()
+    G.close()
+
+
+def test_stack_teacher_forced_layers(ctx):
+    # x_{l+1} = x_l + block_l(bf16(RMSNorm(x_l) * w_l)); every layer is checked on the GPU's own
+    # layer input h_l, so routing must match bit for bit at every depth
+    n, T, D = 3, 24, 256
+    pairs = [layer_pair(ctx, 40, 8, 64, D, 128, layer=l) for l in range(n)]
+    norms = (1.0 + 0.1 * np.sin(np.arange(n * D))).astype(np.float32).reshape(n, D)
+    x0 = O.bf16_to_f32(O.gen_bf16(14, O.ACT_STREAM, T * D)).reshape(T, D)
+    for flags in (di.PATH_GROUPED, di.PATH_GEMV):
+        if flags == di.PATH_GEMV and T > 64:
+            continue
+        xg, ht, it, _ = di.moe_stack(ctx, [p[1] for p in pairs], norms, x0, 1e-6, flags, trace=True)
+        x = x0.copy()
+        for l, (L, _) in enumerate(pairs):
+            rc, out, ids, _, _ = O.moe_block(L, ht[l], O.MODE_F32)
+            assert rc == 0 and np.array_equal(ids, it[l])
+            x = x + out
+        ma, rl = O.tolerance_report(xg, x)
+        assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
