@@ -134,6 +134,25 @@ int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_layer
    returns the number written. */
 int di_moe_last_profile(void *ctx, double *stage_ms, int n);
 
+/* Allocation-free small-batch block. No counterpart in the reference; it exists for callers
+   that must not allocate GPU memory once they are running: code recording a CUDA graph
+   (cudaMalloc is not allowed while a stream is being captured), serving loops with a
+   no-allocation rule after start-up, and processes whose device memory is already reserved
+   by another allocator, where a late cudaMalloc would fail. It computes what di_moe_block
+   computes with the decode (GEMV) path and device pointers only: x bf16 [T,D] in, y bf16
+   [T,D] out, ids int32 [T,8] and probs f32 [T,8] optional outputs, T in [1, 16].
+   Its scratch is one fixed device array of DI_MOE_STATIC_SCRATCH_BYTES per GPU that loads
+   the library (held until process exit); a call that would need more (T*E*4 + T*9*I*4 + a
+   few KB) is rejected with an error before any GPU work, and the call itself allocates
+   nothing. The first call on a device resolves that array's device address, so make it
+   before any stream capture. Every call on a device shares the array and it keeps the last
+   call's contents: calls that overlap on the GPU (other threads, other contexts on the same
+   device) race and must be serialised by the caller. */
+#define DI_MOE_STATIC_MAX_TOKENS 16
+#define DI_MOE_STATIC_SCRATCH_BYTES (512u * 1024u)
+int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int tokens, uint16_t *y, int32_t *ids,
+                        float *probs, double *ms, char *error, int capacity);
+
 #ifdef __cplusplus
 }
 #endif

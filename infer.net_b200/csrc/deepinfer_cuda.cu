@@ -1072,3 +1072,102 @@ API int di_moe_last_profile(void *ctx, double *stage_ms, int n) {
     for (int i = 0; i < k; ++i) stage_ms[i] = c->last_stage_ms[i];
     return k;
 }
+
+// ============================================================================ allocation-free block
+
+namespace {
+// Scratch of di_moe_block_static: one fixed array on every GPU that loads this library,
+// held until the process exits. Host code must not take its address directly (that is a
+// host-side stand-in); the device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) uint8_t g_static_scratch[DI_MOE_STATIC_SCRATCH_BYTES];
+constexpr int kMaxStaticDevices = 64;
+void *g_static_addr[kMaxStaticDevices] = {};  // device address of g_static_scratch, per device
+std::mutex g_static_mutex;
+}  // namespace
+
+API int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int tokens, uint16_t *y, int32_t *ids,
+                            float *probs, double *ms, char *error, int capacity) {
+    if (!live_context(ctx) || !live_layer(layer)) {
+        set_error(error, capacity, "Invalid context or MoE layer");
+        return -1;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    Layer *L = static_cast<Layer *>(layer);
+    if (L->ctx != c) {
+        set_error(error, capacity, "MoE layer must belong to this device.");
+        return -1;
+    }
+    if (!x || !y || tokens < 1 || tokens > DI_MOE_STATIC_MAX_TOKENS) {
+        set_error(error, capacity, "Invalid allocation-free MoE block arguments: device x and y, 1 <= tokens <= %d",
+                  DI_MOE_STATIC_MAX_TOKENS);
+        return -1;
+    }
+    for (int i = 0; i < 8; ++i)
+        if (L->m[i]->destroyed) {
+            set_error(error, capacity, "MoE layer matrix was destroyed");
+            return -1;
+        }
+    if (c->device < 0 || c->device >= kMaxStaticDevices) {
+        set_error(error, capacity, "Device ordinal %d is outside the allocation-free entry's table", c->device);
+        return -1;
+    }
+    const int T = tokens, E = L->E, I = L->I;
+    // carve the fixed array: the same buffers the decode path of di_moe_block uses
+    BlockBuffers b{};
+    b.nblocks = (T + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA;
+    Carve cv;
+    const size_t o_lg = cv.take<float>((size_t)T * E), o_p = cv.take<float>((size_t)T * 8);
+    const size_t o_g = cv.take<float>((size_t)T), o_ids = cv.take<int32_t>((size_t)T * 8);
+    const size_t o_bc = cv.take<int32_t>((size_t)b.nblocks * E), o_a = cv.take<float>((size_t)T * 9 * I);
+    if (cv.off > DI_MOE_STATIC_SCRATCH_BYTES) {
+        set_error(error, capacity,
+                  "Allocation-free MoE block needs %zu bytes of scratch for T=%d, E=%d, I=%d; the fixed array holds %u",
+                  cv.off, T, E, I, (unsigned)DI_MOE_STATIC_SCRATCH_BYTES);
+        return -1;
+    }
+    DeviceGuard dg(c->device);
+    try {
+        uint8_t *base = nullptr;
+        {
+            // once per device, with that device current: resolve the array's device address
+            std::lock_guard<std::mutex> g(g_static_mutex);
+            if (!g_static_addr[c->device]) {
+                void *p = nullptr;
+                cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+                if (e != cudaSuccess || !p) {
+                    set_error(error, capacity, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+                    return -1;
+                }
+                g_static_addr[c->device] = p;
+            }
+            base = static_cast<uint8_t *>(g_static_addr[c->device]);
+        }
+        b.logits = reinterpret_cast<float *>(base + o_lg);
+        b.probs = reinterpret_cast<float *>(base + o_p);
+        b.gate = reinterpret_cast<float *>(base + o_g);
+        b.ids = reinterpret_cast<int32_t *>(base + o_ids);
+        b.block_counts = reinterpret_cast<int32_t *>(base + o_bc);
+        b.act32 = reinterpret_cast<float *>(base + o_a);
+        for (int i = 0; i < 8; ++i) sync_matrix(L->m[i]);
+        // every buffer above is fully rewritten by the kernels; only the error word starts at zero
+        CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
+        CK(cudaEventRecord(c->ev_start, c->stream));
+        enqueue_block(c, L, x, T, y, nullptr, nullptr, probs, true, b, false);
+        if (launch_check(error, capacity)) return -1;
+        if (ids) CK(cudaMemcpyAsync(ids, b.ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaEventRecord(c->ev_stop, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        if (*c->h_err) {
+            set_error(error, capacity, "%s", device_error_text(*c->h_err));
+            return -1;
+        }
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
+        if (ms) *ms = t;
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}

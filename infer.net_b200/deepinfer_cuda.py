@@ -65,6 +65,8 @@ SIGNATURES = {
     "di_moe_stack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_int,
                                C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
     "di_moe_last_profile": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.c_int]),
+    "di_moe_block_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
 }
 
 
