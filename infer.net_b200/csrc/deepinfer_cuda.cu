@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decode.cuh"
 #include "gemv.cuh"
 #include "generate.cuh"
 #include "grouped_gemm.cuh"
@@ -64,7 +65,9 @@ struct Layer {
     Matrix *m[8] = {};  // router, gate, up, down, shared_gate, shared_up, shared_down, shared_route
     float *bias = nullptr;  // device [E] or null
     int E = 0, D = 0, I = 0, bits = 0;
+    uint64_t gen = 0;       // unique per layer object, for graph cache keys
 };
+uint64_t g_layer_gen = 0;
 
 // Device scratch of one context; grows, never shrinks.
 struct Workspace {
@@ -87,6 +90,9 @@ struct Context {
     double last_stage_ms[kProfileSlots] = {};
     bool have_profile = false;
     std::vector<cudaEvent_t> layer_events;  // [layer][S_N + 2] for profiled stacks
+    // CUDA graph of the last decode-path stack, replayed while its key matches
+    std::vector<uint64_t> graph_key;
+    cudaGraphExec_t graph_exec = nullptr;
 };
 
 std::mutex g_registry;
@@ -182,18 +188,44 @@ int launch_check(char *error, int capacity) {
     return 0;
 }
 
+// Kernel launch, optionally with programmatic dependent launch (the kernel may start while
+// the previous one on the stream finishes; it orders itself with griddepcontrol.wait).
+template <typename... KArgs, typename... Args>
+void launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    CK(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
+
+constexpr int kDecodeSmemMax = 96 * 1024;  // decode_route_kernel: T*D bf16 rows
+
+uint64_t eps_bits(float eps) {
+    uint32_t u;
+    std::memcpy(&u, &eps, 4);
+    return u;
+}
+
 bool kernels_configured = false;
 void configure_kernels() {
     if (kernels_configured) return;
     cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(router::Smem));
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::Cfg<gg::MODE_GATE_UP>::SMEM);
+                         gg::SMEM);
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::Cfg<gg::MODE_GATE_UP>::SMEM);
+                         gg::SMEM);
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::Cfg<gg::MODE_DOWN>::SMEM);
+                         gg::SMEM);
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::Cfg<gg::MODE_DOWN>::SMEM);
+                         gg::SMEM);
+    cudaFuncSetAttribute(decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecodeSmemMax);
     kernels_configured = true;
 }
 
@@ -206,6 +238,7 @@ struct BlockBuffers {
     Tile *tiles;
     uint16_t *act, *yr, *ys;
     float *act32;
+    uint32_t *counter;  // last-CTA ticket of decode_route_kernel (kept at zero between launches)
     int nblocks, max_tiles;
 };
 
@@ -230,6 +263,7 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     size_t o_yr = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
     size_t o_ys = gemv ? 0 : cv.take<uint16_t>((size_t)T * D);
     size_t o_a32 = gemv ? cv.take<float>((size_t)T * 9 * I) : 0;
+    size_t o_ctr = cv.take<uint32_t>(1);
     size_t need = cv.off + 256;
     ensure_workspace(c, need);
     b.x = host_io ? at<uint16_t>(c, o_x) : nullptr;
@@ -249,6 +283,7 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     b.yr = gemv ? nullptr : at<uint16_t>(c, o_yr);
     b.ys = gemv ? nullptr : at<uint16_t>(c, o_ys);
     b.act32 = gemv ? at<float>(c, o_a32) : nullptr;
+    b.counter = at<uint32_t>(c, o_ctr);
     return need;
 }
 
@@ -257,8 +292,11 @@ void stage_mark(Context *c, int s) { CK(cudaEventRecord(g_marks ? g_marks[s] : c
 
 // Enqueue the block on the context stream. x/y/ids/probs are device pointers; resid (f32)
 // optional. forced: ids holds input routes. Returns nothing; errors surface via d_err.
+// Stack mode (decode path only): `x` is the bf16 scratch row that decode_route_kernel fills from
+// the f32 residual `resid` normalised by `norm_w`; otherwise `x` is the block input.
 void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_t *y, float *resid,
-                   const int32_t *forced_ids, float *probs_out, bool gemv, BlockBuffers &b, bool profile) {
+                   const int32_t *forced_ids, float *probs_out, bool gemv, BlockBuffers &b, bool profile,
+                   const float *norm_w = nullptr, float eps = 0.f, uint16_t *h_trace = nullptr) {
     const int E = L->E, D = L->D, I = L->I;
     cudaStream_t st = c->stream;
     const QView R = L->m[0]->view(), G = L->m[1]->view(), U = L->m[2]->view(), Dn = L->m[3]->view();
@@ -266,6 +304,42 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     int32_t *ids = b.ids;  // sanitised ids; every later kernel indexes with these
     float *probs = probs_out ? probs_out : b.probs;
     if (profile) stage_mark(c, S_ROUTER);
+    if (gemv && !forced_ids) {
+        // decode path: three kernels chained with programmatic dependent launch
+        const bool stacked = norm_w != nullptr;
+        launch(decode_route_kernel, dim3((E + 7) / 8), dim3(256), (size_t)T * D * 2, st, true,
+               stacked ? (const float *)resid : nullptr, norm_w, eps, stacked ? nullptr : x, T, D, R, SR,
+               (const float *)L->bias, stacked ? const_cast<uint16_t *>(x) : nullptr, h_trace, b.logits, ids, probs,
+               b.gate, b.counter, c->d_err);
+        if (profile) {
+            stage_mark(c, S_TOPK);
+            stage_mark(c, S_SCAN);
+            stage_mark(c, S_SCATTER);
+            stage_mark(c, S_GATE_UP);
+        }
+        const int gw = T * 9 * I;
+        if (L->bits == 8)
+            launch(decode_gate_up_kernel<8>, dim3(gw / 8), dim3(256), (size_t)D * 2, st, true, x, T, D, I, G, U, SG, SU,
+                   (const int32_t *)ids, b.act32);
+        else
+            launch(decode_gate_up_kernel<5>, dim3(gw / 8), dim3(256), (size_t)D * 2, st, true, x, T, D, I, G, U, SG, SU,
+                   (const int32_t *)ids, b.act32);
+        if (profile) stage_mark(c, S_DOWN);
+        const int dw = T * D;
+        if (L->bits == 8)
+            launch(decode_down_kernel<8>, dim3((dw + 7) / 8), dim3(256), 0, st, true, (const float *)b.act32, T, D, I,
+                   Dn, SD, (const int32_t *)ids, (const float *)probs, (const float *)b.gate, y, stacked ? resid : nullptr,
+                   (const uint32_t *)c->d_err);
+        else
+            launch(decode_down_kernel<5>, dim3((dw + 7) / 8), dim3(256), 0, st, true, (const float *)b.act32, T, D, I,
+                   Dn, SD, (const int32_t *)ids, (const float *)probs, (const float *)b.gate, y, stacked ? resid : nullptr,
+                   (const uint32_t *)c->d_err);
+        if (profile) {
+            stage_mark(c, S_COMBINE);
+            stage_mark(c, S_N);
+        }
+        return;
+    }
     // 1. router logits (canonical f32 order)
     if (gemv) {
         router_logits_gemv_kernel<<<(E * 32 + 255) / 256, 256, 0, st>>>(x, T, D, R, L->bias, b.logits);
@@ -314,18 +388,18 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     {
         gg::Params p{G, U, SG, SU, x, b.perm, b.tiles, b.n_tiles, T, D, I, E, b.act, nullptr, c->d_err};
         if (L->bits == 8)
-            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8><<<grid, gg::THREADS, gg::Cfg<gg::MODE_GATE_UP>::SMEM, st>>>(p);
+            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
         else
-            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5><<<grid, gg::THREADS, gg::Cfg<gg::MODE_GATE_UP>::SMEM, st>>>(p);
+            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
     }
     if (profile) stage_mark(c, S_DOWN);
     // 6. grouped down -> expert rows in route order, shared rows
     {
         gg::Params p{Dn, Dn, SD, SD, b.act, b.perm, b.tiles, b.n_tiles, T, I, D, E, b.yr, b.ys, c->d_err};
         if (L->bits == 8)
-            gg::grouped_gemm_kernel<gg::MODE_DOWN, 8><<<grid, gg::THREADS, gg::Cfg<gg::MODE_DOWN>::SMEM, st>>>(p);
+            gg::grouped_gemm_kernel<gg::MODE_DOWN, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
         else
-            gg::grouped_gemm_kernel<gg::MODE_DOWN, 5><<<grid, gg::THREADS, gg::Cfg<gg::MODE_DOWN>::SMEM, st>>>(p);
+            gg::grouped_gemm_kernel<gg::MODE_DOWN, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
     }
     if (profile) stage_mark(c, S_COMBINE);
     // 7. combine
@@ -422,6 +496,7 @@ API void di_quant_destroy(void *p) {
     for (int i = 0; i <= S_N; ++i)
         if (c->ev_stage[i]) cudaEventDestroy(c->ev_stage[i]);
     for (cudaEvent_t e : c->layer_events) cudaEventDestroy(e);
+    if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
     if (c->ev_start) cudaEventDestroy(c->ev_start);
     if (c->ev_stop) cudaEventDestroy(c->ev_stop);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -789,6 +864,7 @@ API void *di_moe_layer_create(void *ctx, void *router, void *gate, void *up, voi
     L->D = D;
     L->I = I;
     L->bits = bits;
+    L->gen = ++g_layer_gen;
     std::lock_guard<std::mutex> g(g_registry);
     g_layers.insert(L);
     return L;
@@ -859,7 +935,7 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
     }
     if (!x || !y || tokens < 1 || tokens > 65536 || (flags & ~15) ||
         ((flags & DI_MOE_PATH_GEMV) && (flags & DI_MOE_PATH_GROUPED)) || (forced && !ids) ||
-        ((flags & DI_MOE_PATH_GEMV) && tokens > 64)) {
+        ((flags & DI_MOE_PATH_GEMV) && tokens > kDecodeMaxTokens)) {
         set_error(error, capacity, "Invalid MoE block arguments");
         return -1;
     }
@@ -876,6 +952,10 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
             }
     const int T = tokens, D = L->D;
     const bool gemv = pick_gemv(T, flags);
+    if (gemv && !forced && (size_t)T * D * 2 > (size_t)kDecodeSmemMax) {
+        set_error(error, capacity, "Decode path supports T*D <= %d; use the grouped path", kDecodeSmemMax / 2);
+        return -1;
+    }
     DeviceGuard dg(c->device);
     try {
         for (int i = 0; i < 8; ++i) sync_matrix(L->m[i]);
@@ -892,6 +972,7 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
         int32_t *dids = dev_io ? ids : at<int32_t>(c, o_ids_io);
         float *dprobs = dev_io ? probs : at<float>(c, o_probs_io);
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
+        CK(cudaMemsetAsync(b.counter, 0, sizeof(uint32_t), c->stream));
         CK(cudaEventRecord(c->ev_start, c->stream));
         if (!dev_io) {
             CK(cudaMemcpyAsync(b.x, x, (size_t)T * D * 2, cudaMemcpyHostToDevice, c->stream));
@@ -944,7 +1025,8 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
     if (!live_context(ctx) || !layers || n_layers < 1 || n_layers > 1024 || !norms || !x || tokens < 1 ||
         tokens > 65536 || !(eps > 0.0f) ||
         (flags & ~(DI_MOE_DEVICE_IO | DI_MOE_PATH_GEMV | DI_MOE_PATH_GROUPED | DI_MOE_PROFILE)) ||
-        ((flags & DI_MOE_PATH_GEMV) && (flags & DI_MOE_PATH_GROUPED)) || ((flags & DI_MOE_PATH_GEMV) && tokens > 64)) {
+        ((flags & DI_MOE_PATH_GEMV) && (flags & DI_MOE_PATH_GROUPED)) ||
+        ((flags & DI_MOE_PATH_GEMV) && tokens > kDecodeMaxTokens)) {
         set_error(error, capacity, "Invalid MoE stack arguments");
         return -1;
     }
@@ -970,6 +1052,10 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
     const bool dev_io = flags & DI_MOE_DEVICE_IO, profile = flags & DI_MOE_PROFILE;
     const int T = tokens;
     const bool gemv = pick_gemv(T, flags);
+    if (gemv && (size_t)T * D * 2 > (size_t)kDecodeSmemMax) {
+        set_error(error, capacity, "Decode path supports T*D <= %d; use the grouped path", kDecodeSmemMax / 2);
+        return -1;
+    }
     DeviceGuard dg(c->device);
     try {
         const size_t need_events = profile ? (size_t)n_layers * (S_N + 2) : 0;
@@ -1009,18 +1095,62 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
             CK(cudaMemcpyAsync(const_cast<float *>(dn), norms, (size_t)n_layers * D * 4, cudaMemcpyHostToDevice,
                                c->stream));
         }
-        for (int l = 0; l < n_layers; ++l) {
-            Layer *L = static_cast<Layer *>(layers[l]);
-            cudaEvent_t *ev = profile ? &c->layer_events[(size_t)l * (S_N + 2)] : nullptr;
-            if (profile) CK(cudaEventRecord(ev[S_N + 1], c->stream));
-            rmsnorm_kernel<<<T, 256, 0, c->stream>>>(dx, dn + (size_t)l * D, D, eps, dh,
-                                                     dht ? dht + (size_t)l * T * D : nullptr);
-            g_marks = ev;
-            enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, gemv, b, profile);
-            g_marks = nullptr;
-            if (dit)
-                CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, b.ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice,
-                                   c->stream));
+        auto enqueue_layers = [&]() {
+            for (int l = 0; l < n_layers; ++l) {
+                Layer *L = static_cast<Layer *>(layers[l]);
+                cudaEvent_t *ev = profile ? &c->layer_events[(size_t)l * (S_N + 2)] : nullptr;
+                if (profile) CK(cudaEventRecord(ev[S_N + 1], c->stream));
+                uint16_t *trace_l = dht ? dht + (size_t)l * T * D : nullptr;
+                g_marks = ev;
+                if (gemv) {
+                    // RMSNorm is fused into the decode route kernel
+                    enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, true, b, profile, dn + (size_t)l * D, eps,
+                                  trace_l);
+                } else {
+                    rmsnorm_kernel<<<T, 256, 0, c->stream>>>(dx, dn + (size_t)l * D, D, eps, dh, trace_l);
+                    enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, false, b, profile);
+                }
+                g_marks = nullptr;
+                if (dit)
+                    CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, b.ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice,
+                                       c->stream));
+            }
+        };
+        CK(cudaMemsetAsync(b.counter, 0, sizeof(uint32_t), c->stream));
+        if (gemv && !profile) {
+            // decode: one CUDA graph for the whole stack, rebuilt only when its inputs change
+            std::vector<uint64_t> key = {(uint64_t)n_layers, (uint64_t)T, (uint64_t)(uintptr_t)dx,
+                                         (uint64_t)(uintptr_t)dn, (uint64_t)(uintptr_t)dht, (uint64_t)(uintptr_t)dit,
+                                         (uint64_t)(uintptr_t)c->ws.base, (uint64_t)c->ws.cap,
+                                         eps_bits(eps)};
+            for (int l = 0; l < n_layers; ++l) {
+                const Layer *L = static_cast<Layer *>(layers[l]);
+                key.push_back(L->gen);
+                key.push_back((uint64_t)(uintptr_t)L->bias);
+            }
+            if (!c->graph_exec || key != c->graph_key) {
+                if (c->graph_exec) {
+                    cudaGraphExecDestroy(c->graph_exec);
+                    c->graph_exec = nullptr;
+                }
+                cudaGraph_t graph = nullptr;
+                CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+                try {
+                    enqueue_layers();
+                } catch (...) {
+                    cudaStreamEndCapture(c->stream, &graph);
+                    if (graph) cudaGraphDestroy(graph);
+                    throw;
+                }
+                CK(cudaStreamEndCapture(c->stream, &graph));
+                cudaError_t ie = cudaGraphInstantiate(&c->graph_exec, graph, 0);
+                cudaGraphDestroy(graph);
+                CK(ie);
+                c->graph_key = key;
+            }
+            CK(cudaGraphLaunch(c->graph_exec, c->stream));
+        } else {
+            enqueue_layers();
         }
         if (launch_check(error, capacity)) return -1;
         CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
@@ -1119,6 +1249,7 @@ API int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int token
     const size_t o_lg = cv.take<float>((size_t)T * E), o_p = cv.take<float>((size_t)T * 8);
     const size_t o_g = cv.take<float>((size_t)T), o_ids = cv.take<int32_t>((size_t)T * 8);
     const size_t o_bc = cv.take<int32_t>((size_t)b.nblocks * E), o_a = cv.take<float>((size_t)T * 9 * I);
+    const size_t o_ctr = cv.take<uint32_t>(1);
     if (cv.off > DI_MOE_STATIC_SCRATCH_BYTES) {
         set_error(error, capacity,
                   "Allocation-free MoE block needs %zu bytes of scratch for T=%d, E=%d, I=%d; the fixed array holds %u",
@@ -1148,9 +1279,12 @@ API int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int token
         b.ids = reinterpret_cast<int32_t *>(base + o_ids);
         b.block_counts = reinterpret_cast<int32_t *>(base + o_bc);
         b.act32 = reinterpret_cast<float *>(base + o_a);
+        b.counter = reinterpret_cast<uint32_t *>(base + o_ctr);
         for (int i = 0; i < 8; ++i) sync_matrix(L->m[i]);
-        // every buffer above is fully rewritten by the kernels; only the error word starts at zero
+        // every buffer above is fully rewritten by the kernels; the error word and the route
+        // kernel's completion ticket must start at zero
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
+        CK(cudaMemsetAsync(b.counter, 0, sizeof(uint32_t), c->stream));
         CK(cudaEventRecord(c->ev_start, c->stream));
         enqueue_block(c, L, x, T, y, nullptr, nullptr, probs, true, b, false);
         if (launch_check(error, capacity)) return -1;

@@ -100,91 +100,6 @@ __device__ __forceinline__ void load_x16_bf16(const uint16_t *x, int c, float *v
     for (int i = 0; i < 16; ++i) v[i] = (i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]);
 }
 
-// act[t, j, i] = silu(gate_j[i] . x_t) * (up_j[i] . x_t) for the 8 routed slots (j < 8,
-// expert ids[t, j]) and the shared expert (j = 8). One warp per (t, j, i); x staged in smem.
-template <int BITS>
-__global__ void __launch_bounds__(256) decode_gate_up_kernel(const uint16_t *__restrict__ x, int T, int D, int I,
-                                                             QView g, QView u, QView sg, QView su,
-                                                             const int32_t *__restrict__ ids, float *__restrict__ act) {
-    extern __shared__ __align__(16) uint16_t xs[];
-    const int per_tok = 9 * I;
-    const int warp0 = blockIdx.x * 8;
-    const int t = warp0 / per_tok;  // one token per CTA (per_tok is a multiple of 8)
-    if (t >= T) return;
-    for (int i = threadIdx.x; i < D / 8; i += blockDim.x)
-        reinterpret_cast<uint4 *>(xs)[i] = reinterpret_cast<const uint4 *>(x + (size_t)t * D)[i];
-    __syncthreads();
-    const int w = warp0 + (threadIdx.x >> 5) - t * per_tok;
-    const int j = w / I, i = w % I;
-    const bool shared = j == 8;
-    const QView G = shared ? sg : g, U = shared ? su : u;
-    const size_t row = (size_t)(shared ? 0 : ids[(size_t)t * 8 + j]) * I + i;
-    float ga = 0.f, ua = 0.f;
-    for (int c = lane_id(); c < D / 16; c += 32) {
-        float wg[16], wu[16], xv[16];
-        load_weights16<BITS>(G, row, c, wg);
-        load_weights16<BITS>(U, row, c, wu);
-        load_x16_bf16(xs, c, xv);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            ga = fmaf(wg[k], xv[k], ga);
-            ua = fmaf(wu[k], xv[k], ua);
-        }
-    }
-    ga = warp_sum_butterfly(ga);
-    ua = warp_sum_butterfly(ua);
-    if (lane_id() == 0) act[((size_t)t * 9 + j) * I + i] = silu_ref(ga) * ua;
-}
-
-// out[t, d] = sigmoid(gate_t) * (shared_down[d] . act_s) + sum_j p[t,j] * (down_j[d] . act_j)
-// (Qwen36Model.cs:242-244). One warp per (t, d): 9 dot products over I then the combine.
-// Optional residual: resid[t, d] += out (f32 stream of di_moe_stack).
-template <int BITS>
-__global__ void __launch_bounds__(256) decode_down_kernel(const float *__restrict__ act, int T, int D, int I, QView dn,
-                                                          QView sd, const int32_t *__restrict__ ids,
-                                                          const float *__restrict__ probs,
-                                                          const float *__restrict__ gate_logit,
-                                                          uint16_t *__restrict__ out, float *__restrict__ resid,
-                                                          const uint32_t *__restrict__ err) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (warp >= T * D) return;
-    const int t = warp / D, d = warp % D;
-    float y[9];
-#pragma unroll
-    for (int j = 0; j < 9; ++j) {
-        const bool shared = j == 8;
-        const QView M = shared ? sd : dn;
-        const size_t row = (size_t)(shared ? 0 : ids[(size_t)t * 8 + j]) * D + d;
-        const float *a = act + ((size_t)t * 9 + j) * I;
-        float acc = 0.f;
-        for (int c = lane_id(); c < I / 16; c += 32) {
-            float w[16];
-            load_weights16<BITS>(M, row, c, w);
-            const float4 *ap = reinterpret_cast<const float4 *>(a + c * 16);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float4 av = ap[k];
-                acc = fmaf(w[4 * k], av.x, acc);
-                acc = fmaf(w[4 * k + 1], av.y, acc);
-                acc = fmaf(w[4 * k + 2], av.z, acc);
-                acc = fmaf(w[4 * k + 3], av.w, acc);
-            }
-        }
-        y[j] = warp_sum_butterfly(acc);
-    }
-    if (lane_id() == 0) {
-        if (*err) return;
-        float o = y[8] * sigmoid_ref(gate_logit[t]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float prod = probs[(size_t)t * 8 + j] * y[j];
-            o = o + prod;
-        }
-        if (out) out[(size_t)t * D + d] = f32_to_bf16_bits(o);
-        if (resid) resid[(size_t)t * D + d] += o;
-    }
-}
-
 // h[t] = bf16(x[t] * rsqrt(mean(x[t]^2) + eps) * w) (gpu_graph.mm:48-61), one CTA per token.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int D,
                                                       float eps, uint16_t *__restrict__ h, uint16_t *__restrict__ trace) {

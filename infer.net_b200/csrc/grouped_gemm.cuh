@@ -1,20 +1,24 @@
 // Grouped expert GEMMs on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
-// D[f, n] = sum_k W[e][f, k] * B[n, k] for every work unit (expert segment tile, 128-row
-// block of W). W is an affine-quantised MLX stack dequantised in shared memory; B rows are
-// the tokens routed to the expert (gathered from x for gate/up, contiguous activation rows
-// for down). Both operands are K-major bf16 tiles with the 128-byte swizzle; the f32
-// accumulator lives in tensor memory.
+// D[m, n] = sum_k A[m, k] * B[n, k] for every work unit (a token tile of one expert segment
+// x a block of weight rows). A is dequantised in shared memory from the affine-quantised MLX
+// codes; B rows are the tokens routed to the expert (gathered from x for gate/up, contiguous
+// activation rows for down). Both operands are K-major bf16 tiles with the 64-byte swizzle;
+// the f32 accumulators live in tensor memory.
 //
-//   MODE_GATE_UP: two accumulators (gate rows, up rows of the same 128 intermediate
-//                 indices), epilogue act = silu(gate) * up -> bf16 act[p, i]
-//                 (quantized.mm:148-189; prefill_moe.mm:23-53 semantics)
-//   MODE_DOWN:    one accumulator, double buffered; epilogue writes the bf16 expert row
-//                 to its route slot y[r, d] (r = t*8 + slot) or the shared row ys[t, d]
+//   MODE_GATE_UP: the 128 A rows of a unit interleave 16 gate rows and the 16 up rows of the
+//                 same intermediate indices in every 32-lane TMEM quadrant, so the SwiGLU
+//                 epilogue pairs them with one warp shuffle; a unit covers 64 intermediate
+//                 indices and up to 512 tokens (two 256-column accumulators), so at 8K tokens
+//                 every expert's weights are dequantised once. act = silu(gate) * up -> bf16
+//                 act[p, i] (quantized.mm:148-189; prefill_moe.mm:23-53 semantics)
+//   MODE_DOWN:    128 rows of the down matrix; the epilogue writes each bf16 expert row to its
+//                 route slot y[r, d] (r = t*8 + slot) or the shared row ys[t, d]
 //                 (prefill_moe.mm:54-78 semantics)
 //
-// Warp roles (512 threads): 0-3 epilogue (TMEM lane quadrants), 4 MMA issue + TMEM owner,
-// 5-7 B loaders (cp.async), 8-15 W dequantisers.
+// Warp roles (512 threads): 0-3 epilogue (one TMEM lane quadrant each), 4 MMA issue + TMEM
+// owner, 5-7 B loaders (cp.async), 8-15 A dequantisers in two groups of 4 warps that take
+// alternate pipeline stages.
 #pragma once
 #include "common.cuh"
 #include "route.cuh"
@@ -23,20 +27,22 @@ namespace di {
 namespace gg {
 
 constexpr int MODE_GATE_UP = 0, MODE_DOWN = 1;
-constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int BM = 128;          // A rows per unit (one MMA M)
+constexpr int BN = 512;          // max tokens per unit (two accumulators of 256 columns)
+constexpr int BK = 32;           // K per pipeline stage: 64-byte rows
+constexpr int STAGES = 5;
+constexpr int LOAD_DEPTH = 3;   // B-loader stages in flight (< STAGES)
 constexpr int THREADS = 512;
-constexpr int kA = BM * 128;        // bytes of one 128 x 64 bf16 A tile
-constexpr int kB = BN * 128;        // bytes of one <=256 x 64 bf16 B tile
+constexpr int kA = BM * 64;      // bytes of one A stage tile
+constexpr int kB = BN * 64;      // bytes of one B stage tile
+constexpr int STAGE_BYTES = kA + kB;
+constexpr int kTable = BN * 4;   // token row table of the B loaders
+constexpr int kStageOut = 4 * 16 * 64;  // epilogue staging: 4 warps x 16 tokens x 64 bytes
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + kTable + kStageOut + 256;
+constexpr uint32_t TMEM_COLS = 512;
 
 template <int MODE>
-struct Cfg {
-    static constexpr int NA = MODE == MODE_GATE_UP ? 2 : 1;
-    static constexpr int STAGES = MODE == MODE_GATE_UP ? 3 : 4;
-    static constexpr int STAGE_BYTES = NA * kA + kB;
-    static constexpr int ACC_SLOTS = MODE == MODE_GATE_UP ? 1 : 2;
-    static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
-};
+__host__ __device__ constexpr int rows_per_unit() { return MODE == MODE_GATE_UP ? 64 : 128; }
 
 struct Params {
     QView w1, w2;              // routed experts: gate, up (GATE_UP) or down (DOWN)
@@ -45,7 +51,7 @@ struct Params {
     const int32_t *perm_route; // [8T] route id of each permuted position
     const Tile *tiles;
     const int32_t *n_tiles;
-    int T, K, rows, E;
+    int T, K, rows, E;         // rows: I (GATE_UP) or D (DOWN)
     uint16_t *out;             // GATE_UP: act [P, rows]; DOWN: y [8T, rows]
     uint16_t *out_shared;      // DOWN: ys [T, rows]
     uint32_t *err;
@@ -53,55 +59,188 @@ struct Params {
 
 __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
 
-// 16 codes of an 8-bit row chunk -> 8 packed bf16x2 words.
+// Byte offset of 16-byte chunk c (0..3) of row r in a 64B-swizzled K-major tile
+// (address bits [7,9) XOR-ed into bits [4,6)).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t r, uint32_t c) {
+    return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4);
+}
+
+// Shared-memory descriptor: K-major, 64-byte swizzle, 8-row atoms 512 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;             // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(512u >> 4) << 32;    // stride byte offset between 8-row groups
+    d |= (uint64_t)1u << 46;             // descriptor version for tcgen05
+    d |= (uint64_t)4u << 61;             // SWIZZLE_64B
+    return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// Two codes (integer-valued f32 magics 2^23 + q) -> bf16x2 of q*s + b.
+__device__ __forceinline__ uint32_t dq_pair(uint32_t m0, uint32_t m1, float2 s2, float2 b2) {
+    const float2 magic = make_float2(-8388608.0f, -8388608.0f);
+    float2 q = fadd2(make_float2(__uint_as_float(m0), __uint_as_float(m1)), magic);
+    float2 w = ffma2(q, s2, b2);
+    return pack_bf16x2(w.x, w.y);
+}
+
+// 16 codes of an 8-bit chunk -> 8 packed bf16x2 words.
 __device__ __forceinline__ void dequant16_8bit(uint4 q, float s, float b, uint32_t *o) {
-    uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    const float2 s2 = make_float2(s, s), b2 = make_float2(b, b);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        float v0 = fmaf(byte_to_f32(w[i], 0), s, b), v1 = fmaf(byte_to_f32(w[i], 1), s, b);
-        float v2 = fmaf(byte_to_f32(w[i], 2), s, b), v3 = fmaf(byte_to_f32(w[i], 3), s, b);
-        o[2 * i] = pack_bf16x2(v0, v1);
-        o[2 * i + 1] = pack_bf16x2(v2, v3);
+        o[2 * i] = dq_pair(__byte_perm(w[i], 0x4B000000u, 0x7540u), __byte_perm(w[i], 0x4B000000u, 0x7541u), s2, b2);
+        o[2 * i + 1] =
+            dq_pair(__byte_perm(w[i], 0x4B000000u, 0x7542u), __byte_perm(w[i], 0x4B000000u, 0x7543u), s2, b2);
     }
 }
 
 // 32 codes of a 5-bit half group (5 words, bit 0 aligned) -> 16 packed bf16x2 words.
 __device__ __forceinline__ void dequant32_5bit(const uint32_t *w, float s, float b, uint32_t *o) {
+    const float2 s2 = make_float2(s, s), b2 = make_float2(b, b);
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
-        float v[2];
+        uint32_t m[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int bit = 5 * (i + h), a = bit >> 5, sh = bit & 31;
-            uint32_t q = (sh + 5 <= 32) ? (w[a] >> sh) : __funnelshift_r(w[a], w[a + 1], sh);
-            v[h] = fmaf(code_to_f32(q & 31u), s, b);
+            const uint32_t q = (sh + 5 <= 32) ? (w[a] >> sh) : __funnelshift_r(w[a], w[a + 1], sh);
+            m[h] = 0x4B000000u | (q & 31u);
         }
-        o[i >> 1] = pack_bf16x2(v[0], v[1]);
+        o[i >> 1] = dq_pair(m[0], m[1], s2, b2);
     }
 }
 
+// A-tile row m of a unit -> weight row. GATE_UP: in quadrant q = m/32, lanes 0-15 are gate rows
+// and lanes 16-31 the up rows of intermediates rb*64 + 16q + (m & 15).
+template <int MODE>
+__device__ __forceinline__ void a_row(int m, int rb, int &mat, int &row) {
+    if constexpr (MODE == MODE_GATE_UP) {
+        mat = (m >> 4) & 1;
+        row = rb * 64 + (m >> 5) * 16 + (m & 15);
+    } else {
+        mat = 0;
+        row = rb * 128 + m;
+    }
+}
+
+// Accumulator slots: a unit with N <= 256 takes one 256-column slot (alternating), a larger
+// unit takes both. Every role derives the same assignment from the unit sequence.
+struct SlotPlan {
+    int next = 0;
+    uint32_t uses[2] = {0, 0};
+    // returns a bitmask of slots; phase[s] = completed fills of slot s before this unit
+    __device__ __forceinline__ int take(int N, uint32_t *phase) {
+        const int mask = N <= 256 ? (1 << next) : 3;
+        if (N <= 256) next ^= 1;
+        for (int s = 0; s < 2; ++s) {
+            phase[s] = uses[s];
+            if (mask >> s & 1) uses[s]++;
+        }
+        return mask;
+    }
+};
+
+// Codes, scale and bias of one dequantiser thread's share of one stage (2 jobs of 16 codes
+// for 8-bit, 1 job of 32 codes for 5-bit), loaded ahead of use.
+template <int BITS>
+struct Fetch {
+    static constexpr int JOBS = BITS == 8 ? 2 : 1, WORDS = BITS == 8 ? 4 : 5;
+    uint32_t q[JOBS][WORDS];
+    float s[JOBS], b[JOBS];
+    bool live[JOBS];
+    bool valid;
+
+    template <int MODE>
+    __device__ __forceinline__ void load(const Params &p, const Tile &tl, int rb, int kb, int tid) {
+        const bool shared = tl.seg >= p.E;
+        const int expert = shared ? 0 : tl.seg;
+#pragma unroll
+        for (int j = 0; j < JOBS; ++j) {
+            const int job = j * 128 + tid;
+            // 8-bit: job = (m, part), 2 parts of 16 codes per 32-wide row; 5-bit: job = m
+            const int m = BITS == 8 ? (job >> 1) : job, part = BITS == 8 ? (job & 1) : 0;
+            int mat, row;
+            a_row<MODE>(m, rb, mat, row);
+            const QView W = mat ? (shared ? p.s2 : p.w2) : (shared ? p.s1 : p.w1);
+            live[j] = row < p.rows;
+            const size_t ridx = (size_t)expert * W.rows + min(row, p.rows - 1);
+            const uint32_t *src = W.packed + ridx * W.words_per_row();
+            if constexpr (BITS == 8) {
+                const uint4 v = ldg_nc_v4(src + kb * 8 + part * 4);
+                q[j][0] = v.x; q[j][1] = v.y; q[j][2] = v.z; q[j][3] = v.w;
+            } else {
+#pragma unroll
+                for (int w = 0; w < 5; ++w) q[j][w] = ldg_nc_u32(src + kb * 5 + w);
+            }
+            s[j] = bf16_bits_to_f32(__ldg(W.scales + ridx * W.groups_per_row() + (kb >> 1)));
+            b[j] = bf16_bits_to_f32(__ldg(W.biases + ridx * W.groups_per_row() + (kb >> 1)));
+        }
+    }
+
+    template <int MODE>
+    __device__ __forceinline__ void store(uint8_t *t, int tid) const {
+#pragma unroll
+        for (int j = 0; j < JOBS; ++j) {
+            const int job = j * 128 + tid;
+            if constexpr (BITS == 8) {
+                const int m = job >> 1, part = job & 1;
+                uint32_t o[8];
+                if (live[j]) dequant16_8bit(make_uint4(q[j][0], q[j][1], q[j][2], q[j][3]), s[j], b[j], o);
+                else
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) o[i] = 0;
+                *reinterpret_cast<uint4 *>(t + sw64_offset(m, 2 * part)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4 *>(t + sw64_offset(m, 2 * part + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+            } else {
+                const int m = job;
+                uint32_t o[16];
+                if (live[j]) dequant32_5bit(q[j], s[j], b[j], o);
+                else
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[i] = 0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    *reinterpret_cast<uint4 *>(t + sw64_offset(m, c)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+            }
+        }
+    }
+};
+
 template <int MODE, int BITS>
 __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
-    using C = Cfg<MODE>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
     uint8_t *smem = smem_raw + pad;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
-    uint64_t *full = bars, *empty = bars + C::STAGES;
-    uint64_t *accf = bars + 2 * C::STAGES, *acce = accf + 2;
+    int32_t *tok_table = reinterpret_cast<int32_t *>(smem + STAGES * STAGE_BYTES);
+    uint8_t *stage_out = reinterpret_cast<uint8_t *>(tok_table + BN);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
+    uint64_t *full = bars, *empty = bars + STAGES;
+    uint64_t *accf = bars + 2 * STAGES, *acce = accf + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
-    auto a_tile = [&](int s, int m) { return smem + s * C::STAGE_BYTES + m * kA; };
-    auto b_tile = [&](int s) { return smem + s * C::STAGE_BYTES + C::NA * kA; };
+    auto a_tile = [&](int s) { return smem + s * STAGE_BYTES; };
+    auto b_tile = [&](int s) { return smem + s * STAGE_BYTES + kA; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int RB = (p.rows + BM - 1) / BM;
+    constexpr int RPU = rows_per_unit<MODE>();
+    const int RB = (p.rows + RPU - 1) / RPU;
     const int nk = p.K / BK;
     const int n_units = (*p.n_tiles) * RB;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], 8 + 3);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 4 + 3);  // one dequant group (4 warps) + 3 loader warps
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -111,7 +250,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
         fence_mbarrier_init();
     }
     if (warp == 4) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -120,72 +259,33 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
 
+    // Flat pipeline index `it`: unit u = blockIdx.x + (it / nk) * gridDim.x, k-block it % nk.
     if (warp >= 8) {
-        // ---------------------------------------------------------------- W dequantisers
-        const int tid = threadIdx.x - 256;
-        constexpr int JOBS = MODE == MODE_GATE_UP ? (BITS == 8 ? 4 : 2) : (BITS == 8 ? 2 : 1);
-        int it = 0;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        // ---------------------------------------------------------------- A dequantisers
+        // group g (warps 8-11 or 12-15) fills the stages it with it % 2 == g. Each thread keeps
+        // the codes of its next two stages in flight in a 3-deep register ring.
+        const int g = (warp - 8) >> 2, tid = threadIdx.x - 256 - 128 * g;  // 0..127
+        const int total = (int)blockIdx.x < n_units ? ((n_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1) * nk : 0;
+        Fetch<BITS> ring[3];
+        auto fetch = [&](int it, Fetch<BITS> &f) {
+            f.valid = it < total;
+            if (!f.valid) return;
+            const int u = blockIdx.x + (it / nk) * gridDim.x, kb = it % nk;
             const Tile tl = p.tiles[u / RB];
-            const int rb = u % RB;
-            const bool shared = tl.seg >= p.E;
-            const int expert = shared ? 0 : tl.seg;
-            for (int kb = 0; kb < nk && ok; ++kb, ++it) {
-                // issue this k-block's global loads before waiting for the stage
-                uint32_t qw[JOBS][BITS == 8 ? 4 : 5];
-                float sc[JOBS], bi[JOBS];
-                bool live[JOBS];
+            f.template load<MODE>(p, tl, u % RB, kb, tid);
+        };
+        fetch(g, ring[0]);
+        fetch(g + 2, ring[1]);
+        for (int it = g; it < total && ok; it += 6) {
 #pragma unroll
-                for (int j = 0; j < JOBS; ++j) {
-                    const int job = j * 256 + tid;
-                    int mat, r, part;
-                    if constexpr (BITS == 8) { mat = job >> 9; r = (job & 511) >> 2; part = job & 3; }
-                    else { mat = job >> 8; r = (job & 255) >> 1; part = job & 1; }
-                    const QView W = mat ? (shared ? p.s2 : p.w2) : (shared ? p.s1 : p.w1);
-                    const int row = rb * BM + r;
-                    live[j] = row < p.rows;
-                    const size_t ridx = (size_t)expert * W.rows + min(row, p.rows - 1);
-                    const uint32_t *src = W.packed + ridx * W.words_per_row();
-                    if constexpr (BITS == 8) {
-                        uint4 q = ldg_nc_v4(src + kb * 16 + part * 4);
-                        qw[j][0] = q.x; qw[j][1] = q.y; qw[j][2] = q.z; qw[j][3] = q.w;
-                    } else {
-#pragma unroll
-                        for (int w = 0; w < 5; ++w) qw[j][w] = ldg_nc_u32(src + kb * 10 + part * 5 + w);
-                    }
-                    sc[j] = bf16_bits_to_f32(__ldg(W.scales + ridx * W.groups_per_row() + kb));
-                    bi[j] = bf16_bits_to_f32(__ldg(W.biases + ridx * W.groups_per_row() + kb));
-                }
-                const int s = it % C::STAGES;
-                const uint32_t ph = (it / C::STAGES) & 1;
+            for (int r = 0; r < 3; ++r) {
+                const int cur = it + 2 * r;
+                if (cur >= total || !ok) break;
+                fetch(cur + 4, ring[(r + 2) % 3]);
+                const int s = cur % STAGES;
+                const uint32_t ph = (cur / STAGES) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeout)) { ok = false; break; }
-#pragma unroll
-                for (int j = 0; j < JOBS; ++j) {
-                    const int job = j * 256 + tid;
-                    if constexpr (BITS == 8) {
-                        const int mat = job >> 9, r = (job & 511) >> 2, part = job & 3;
-                        uint32_t o[8];
-                        if (live[j]) dequant16_8bit(make_uint4(qw[j][0], qw[j][1], qw[j][2], qw[j][3]), sc[j], bi[j], o);
-                        else
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) o[i] = 0;
-                        uint8_t *t = a_tile(s, mat);
-                        *reinterpret_cast<uint4 *>(t + sw128_offset(r, 2 * part)) = make_uint4(o[0], o[1], o[2], o[3]);
-                        *reinterpret_cast<uint4 *>(t + sw128_offset(r, 2 * part + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-                    } else {
-                        const int mat = job >> 8, r = (job & 255) >> 1, part = job & 1;
-                        uint32_t o[16];
-                        if (live[j]) dequant32_5bit(qw[j], sc[j], bi[j], o);
-                        else
-#pragma unroll
-                            for (int i = 0; i < 16; ++i) o[i] = 0;
-                        uint8_t *t = a_tile(s, mat);
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            *reinterpret_cast<uint4 *>(t + sw128_offset(r, 4 * part + c)) =
-                                make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-                    }
-                }
+                ring[r].template store<MODE>(a_tile(s), tid);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
@@ -193,130 +293,168 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
         }
     } else if (warp >= 5) {
         // ---------------------------------------------------------------- B loaders
-        const int tid = threadIdx.x - 160;  // 0..95
-        int it = 0, pending = -1;
+        // loader warp w owns the 8-row groups g with g % 3 == w: it alone writes and reads
+        // their table entries, so only __syncwarp is needed. Per group, lane l copies 16-byte
+        // chunk l % 4 of row 8g + l / 4.
+        const int w = warp - 5;
+        int it = 0, done = 0;  // stages issued / stages published
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const Tile tl = p.tiles[u / RB];
             const bool shared = tl.seg >= p.E;
             const int N = round16(tl.n);
+            __syncwarp();
+            for (int g8 = w; g8 < N / 8; g8 += 3) {
+                if (lane < 8) {
+                    const int n = g8 * 8 + lane;
+                    const int pos = tl.p0 + min(n, tl.n - 1);
+                    int row;
+                    if constexpr (MODE == MODE_GATE_UP) row = shared ? pos - 8 * p.T : (p.perm_route[pos] >> 3);
+                    else row = pos;
+                    tok_table[n] = row;
+                }
+            }
+            __syncwarp();
             for (int kb = 0; kb < nk && ok; ++kb, ++it) {
-                const int s = it % C::STAGES;
-                const uint32_t ph = (it / C::STAGES) & 1;
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeout)) { ok = false; break; }
                 uint8_t *bt = b_tile(s);
-                for (int c = tid; c < N * 8; c += 96) {
-                    const int n = c >> 3, ch = c & 7;
-                    const bool valid = n < tl.n;
-                    const int pos = tl.p0 + min(n, tl.n - 1);
-                    size_t row;
-                    if constexpr (MODE == MODE_GATE_UP) row = shared ? (size_t)(pos - 8 * p.T) : (size_t)(p.perm_route[pos] >> 3);
-                    else row = (size_t)pos;
-                    cp_async_16(bt + sw128_offset(n, ch), p.src + row * p.K + kb * BK + ch * 8, valid);
+                const uint16_t *base = p.src + kb * BK;
+                for (int g8 = w; g8 < N / 8; g8 += 3) {
+                    const int n = g8 * 8 + (lane >> 2), ch = lane & 3;
+                    cp_async_16(bt + sw64_offset(n, ch), base + (size_t)tok_table[n] * p.K + ch * 8, n < tl.n);
                 }
                 cp_async_commit();
-                if (pending >= 0) {
-                    cp_async_wait<1>();
+                // keep LOAD_DEPTH stages in flight; publish the oldest once its copies landed
+                if (it - done >= LOAD_DEPTH) {
+                    cp_async_wait<LOAD_DEPTH>();
                     fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&full[pending]);
+                    if (lane == 0) mbar_arrive(&full[done % STAGES]);
+                    ++done;
                 }
-                pending = s;
             }
         }
-        if (pending >= 0) {
-            cp_async_wait<0>();
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0 && ok) mbar_arrive(&full[pending]);
-        }
+        cp_async_wait<0>();
+        fence_proxy_async_smem();
+        __syncwarp();
+        for (; done < it && ok; ++done)
+            if (lane == 0) mbar_arrive(&full[done % STAGES]);
     } else if (warp == 4) {
         // ---------------------------------------------------------------- MMA issue
         if (lane == 0) {
-            int it = 0, uc = 0;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++uc) {
+            int it = 0;
+            SlotPlan plan;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const Tile tl = p.tiles[u / RB];
                 const int N = round16(tl.n);
-                const uint32_t idesc = idesc_bf16_f32(BM, N);
-                const int slot = C::ACC_SLOTS == 2 ? (uc & 1) : 0;
-                const uint32_t use = C::ACC_SLOTS == 2 ? (uc >> 1) : uc;
-                if (!mbar_wait(&acce[slot], (use & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
+                uint32_t phase[2];
+                const int mask = plan.take(N, phase);
+                for (int s2 = 0; s2 < 2 && ok; ++s2)
+                    if (mask >> s2 & 1)
+                        if (!mbar_wait(&acce[s2], (phase[s2] & 1) ^ 1, p.err, kErrTimeout)) ok = false;
+                if (!ok) break;
                 tc_fence_after();
-                const uint32_t d0 = tmem + slot * 256;
+                // tokens [0, n0) accumulate in the first slot of the mask, [256, N) in slot 1
+                const int first = (mask == 2) ? 1 : 0;
+                const int n0 = N < 256 ? N : 256, n1 = N - n0;
+                const uint32_t d0 = tmem + first * 256, d1 = tmem + 256;
+                const uint32_t id0 = idesc_bf16_f32(BM, n0), id1 = n1 > 0 ? idesc_bf16_f32(BM, n1) : 0;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % C::STAGES;
-                    const uint32_t ph = (it / C::STAGES) & 1;
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
                     if (!mbar_wait(&full[s], ph, p.err, kErrTimeout)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(b_tile(s)));
-                    const uint64_t a1 = smem_desc_sw128(smem_u32(a_tile(s, 0)));
+                    const uint64_t adesc = smem_desc_sw64(smem_u32(a_tile(s)));
+                    const uint64_t bdesc = smem_desc_sw64(smem_u32(b_tile(s)));
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         const uint32_t acc = (kb | k) != 0;
-                        tc_mma_bf16(d0, a1 + 2 * k, bdesc + 2 * k, idesc, acc);
-                        if constexpr (MODE == MODE_GATE_UP) {
-                            const uint64_t a2 = smem_desc_sw128(smem_u32(a_tile(s, 1)));
-                            tc_mma_bf16(tmem + 256, a2 + 2 * k, bdesc + 2 * k, idesc, acc);
-                        }
+                        tc_mma_bf16(d0, adesc + 2 * k, bdesc + 2 * k, id0, acc);
+                        // second accumulator: B rows from 256 on start 256 x 64 bytes further
+                        if (n1 > 0) tc_mma_bf16(d1, adesc + 2 * k, bdesc + ((256 * 64) >> 4) + 2 * k, id1, acc);
                     }
                     tc_commit(&empty[s]);
                 }
                 if (!ok) break;
-                tc_commit(&accf[slot]);
+                for (int s2 = 0; s2 < 2; ++s2)
+                    if (mask >> s2 & 1) tc_commit(&accf[s2]);
             }
         }
         __syncwarp();
     } else {
         // ---------------------------------------------------------------- epilogue
         const int q = warp;  // TMEM lanes 32q .. 32q+31
-        int uc = 0;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++uc) {
+        uint8_t *so = stage_out + q * 16 * 64;
+        SlotPlan plan;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const Tile tl = p.tiles[u / RB];
             const int rb = u % RB;
             const bool shared = tl.seg >= p.E;
             const int N = round16(tl.n);
-            const int slot = C::ACC_SLOTS == 2 ? (uc & 1) : 0;
-            const uint32_t use = C::ACC_SLOTS == 2 ? (uc >> 1) : uc;
-            if (!mbar_wait(&accf[slot], use & 1, p.err, kErrTimeout)) { ok = false; break; }
+            uint32_t phase[2];
+            const int mask = plan.take(N, phase);
+            for (int s2 = 0; s2 < 2 && ok; ++s2)
+                if (mask >> s2 & 1)
+                    if (!mbar_wait(&accf[s2], phase[s2] & 1, p.err, kErrTimeout)) ok = false;
+            if (!ok) break;
             tc_fence_after();
-            const int row = rb * BM + 32 * q + lane;
-            const bool rv = row < p.rows;
-            const uint32_t tl_addr = tmem + ((uint32_t)(32 * q) << 16) + slot * 256;
+            const int first = (mask == 2) ? 1 : 0;
             for (int c = 0; c < N; c += 16) {
+                const uint32_t col = (c < 256) ? first * 256 + c : 256 + (c - 256);
                 float v[16];
-                tmem_ld16(tl_addr + c, v);
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + col, v);
+                tc_wait_ld();
                 if constexpr (MODE == MODE_GATE_UP) {
-                    float w[16];
-                    tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 256 + c, w);
-                    tc_wait_ld();
+                    // lanes 0-15: gate of intermediate rb*64 + 16q + lane; lanes 16-31: its up
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int n = c + j;
-                        if (rv && n < tl.n)
-                            p.out[(size_t)(tl.p0 + n) * p.rows + row] = f32_to_bf16_bits(silu_ref(v[j]) * w[j]);
+                        const float up = __shfl_down_sync(kFull, v[j], 16);
+                        if (lane < 16)
+                            reinterpret_cast<uint16_t *>(so)[j * 16 + lane] = f32_to_bf16_bits(v[j] / (1.0f + __expf(-v[j])) * up);
                     }
+                    __syncwarp();
+                    // 16 tokens x 16 intermediates (32 bytes): lane -> (token lane/2, half lane%2)
+                    const int tk = lane >> 1, half = lane & 1, n = c + tk;
+                    const int i = rb * 64 + 16 * q + half * 8;
+                    if (n < tl.n && i < p.rows) {
+                        const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 32 + half * 16);
+                        *reinterpret_cast<uint4 *>(p.out + (size_t)(tl.p0 + n) * p.rows + i) = val;
+                    }
+                    __syncwarp();
                 } else {
-                    tc_wait_ld();
+                    // lane holds output dim rb*128 + 32q + lane for 16 tokens
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int n = c + j;
-                        if (rv && n < tl.n) {
+                    for (int j = 0; j < 16; ++j) reinterpret_cast<uint16_t *>(so)[j * 32 + lane] = f32_to_bf16_bits(v[j]);
+                    __syncwarp();
+                    // 16 tokens x 64 bytes = 64 chunks of 16 bytes, two per lane
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
+                        const int d = rb * 128 + 32 * q + part * 8;
+                        if (n < tl.n && d < p.rows) {
+                            const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 64 + part * 16);
                             const int pos = tl.p0 + n;
-                            if (shared) p.out_shared[(size_t)(pos - 8 * p.T) * p.rows + row] = f32_to_bf16_bits(v[j]);
-                            else p.out[(size_t)p.perm_route[pos] * p.rows + row] = f32_to_bf16_bits(v[j]);
+                            uint16_t *dst = shared ? p.out_shared + (size_t)(pos - 8 * p.T) * p.rows
+                                                   : p.out + (size_t)p.perm_route[pos] * p.rows;
+                            *reinterpret_cast<uint4 *>(dst + d) = val;
                         }
                     }
+                    __syncwarp();
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acce[slot]);
+            if (lane == 0)
+                for (int s2 = 0; s2 < 2; ++s2)
+                    if (mask >> s2 & 1) mbar_arrive(&acce[s2]);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 4) {
         tc_fence_after();
-        tmem_dealloc(tmem, C::TMEM_COLS);
+        tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 

@@ -24,8 +24,8 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
-// Canonical dot product of one 8-bit router row with one bf16 activation row, evaluated
-// by a whole warp; returns the same value in every lane.
+// Canonical dot product of one 8-bit router row with one bf16 activation row (in global or
+// shared memory), evaluated by a whole warp; returns the same value in every lane.
 __device__ __forceinline__ float canonical_dot_warp(const QView &m, int row, const uint16_t *x, int D) {
     const uint32_t lane = lane_id();
     const uint32_t *w = m.packed + (size_t)row * m.words_per_row();
@@ -34,7 +34,7 @@ __device__ __forceinline__ float canonical_dot_warp(const QView &m, int row, con
     float acc = 0.0f;
     for (int base = lane * 8; base < D; base += 256) {
         uint2 q = __ldg(reinterpret_cast<const uint2 *>(w + base / 4));
-        uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x + base));
+        const uint4 xv = *reinterpret_cast<const uint4 *>(x + base);  // x may be shared or global
         float s = bf16_bits_to_f32(__ldg(sc + base / 64)), b = bf16_bits_to_f32(__ldg(bi + base / 64));
         uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
@@ -50,16 +50,20 @@ __device__ __forceinline__ float canonical_dot_warp(const QView &m, int row, con
 // ------------------------------------------------------------------ router GEMM (SIMT)
 //
 // logits[t, e] for a tile of 32 tokens x 16 experts per CTA (8 warps: 4 token groups x 2
-// expert groups, 8x8 outputs per warp). Each 256-column block of x and of the 8-bit codes
-// is staged in shared memory (double buffered with cp.async); every lane keeps 64 partial
-// sums in the canonical order and the warp reduces them with the butterfly at the end.
+// expert groups, 8x8 outputs per warp). For every 256-column block, x and the 8-bit codes are
+// staged with cp.async (double buffered); the CTA dequantises the 16 x 256 weights once into
+// f32 shared memory (w = fma(q, s, b)), and every lane accumulates its 64 outputs over its own
+// 8 columns in the canonical order with paired f32 FMAs; the warp butterfly finishes each sum.
 namespace router {
 constexpr int TT = 32, TE = 16, KB = 256, THREADS = 256;
 struct Smem {
     uint16_t x[2][TT][KB];        // 16 KB per stage
-    uint8_t w[2][TE][KB];         // 4 KB per stage
+    uint8_t q[2][TE][KB];         // 4 KB per stage
     uint16_t s[2][TE][KB / 64];
     uint16_t b[2][TE][KB / 64];
+    // dequantised weights of the current block, 16 KB, laid out [expert][half][lane][4] so that
+    // lane l's columns 8l..8l+3 (half 0) and 8l+4..8l+7 (half 1) are contiguous across lanes
+    float w[TE][2][32][4];
 };
 }  // namespace router
 
@@ -80,19 +84,19 @@ router_logits_kernel(const uint16_t *__restrict__ x, int T, int D, QView W, cons
         // x: 32 rows x 512 B = 1024 chunks of 16 B, 4 per thread
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            int c = tid + i * THREADS, r = c >> 5, ch = c & 31;
-            int t = t0 + r;
+            const int c = tid + i * THREADS, r = c >> 5, ch = c & 31;
+            const int t = t0 + r;
             const uint16_t *src = x + (size_t)min(t, T - 1) * D + kb * KB + ch * 8;
             cp_async_16(&sm.x[buf][r][ch * 8], src, t < T);
         }
         // codes: 16 rows x 256 B = 256 chunks, 1 per thread
         {
-            int r = tid >> 4, ch = tid & 15, e = e0 + r;
+            const int r = tid >> 4, ch = tid & 15, e = e0 + r;
             const uint32_t *src = W.packed + (size_t)min(e, E - 1) * wpr + kb * (KB / 4) + ch * 4;
-            cp_async_16(&sm.w[buf][r][ch * 16], src, e < E);
+            cp_async_16(&sm.q[buf][r][ch * 16], src, e < E);
         }
         if (tid < TE) {
-            int e = min(e0 + tid, E - 1);
+            const int e = min(e0 + tid, E - 1);
             const uint16_t *ss = W.scales + (size_t)e * gpr + kb * (KB / 64);
             const uint16_t *bb = W.biases + (size_t)e * gpr + kb * (KB / 64);
 #pragma unroll
@@ -120,43 +124,60 @@ router_logits_kernel(const uint16_t *__restrict__ x, int T, int D, QView W, cons
             cp_async_wait<0>();
         }
         __syncthreads();
+        {
+            // dequantise this block once: thread -> (expert r, 16 columns)
+            const int r = tid >> 4, c0 = (tid & 15) * 16;
+            const float sc = bf16_bits_to_f32(sm.s[buf][r][c0 >> 6]), bi = bf16_bits_to_f32(sm.b[buf][r][c0 >> 6]);
+            const uint4 q = *reinterpret_cast<const uint4 *>(&sm.q[buf][r][c0]);
+            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float4 v;
+                v.x = fmaf(byte_to_f32(qw[i], 0), sc, bi);
+                v.y = fmaf(byte_to_f32(qw[i], 1), sc, bi);
+                v.z = fmaf(byte_to_f32(qw[i], 2), sc, bi);
+                v.w = fmaf(byte_to_f32(qw[i], 3), sc, bi);
+                const int col = c0 + 4 * i;  // columns col..col+3 belong to lane col/8, half (col/4)&1
+                *reinterpret_cast<float4 *>(&sm.w[r][(col >> 2) & 1][col >> 3][0]) = v;
+            }
+        }
+        __syncthreads();
         // x values of this lane's 8 columns for the warp's 8 tokens, as f32 pairs (t, t+1)
         float2 xp[4][8];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-            uint4 a = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p][lane * 8]);
-            uint4 c = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p + 1][lane * 8]);
-            uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
+            const uint4 a = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p][lane * 8]);
+            const uint4 c = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p + 1][lane * 8]);
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
             for (int j = 0; j < 8; ++j)
                 xp[p][j] = make_float2((j & 1) ? bf16_hi(aw[j >> 1]) : bf16_lo(aw[j >> 1]),
                                        (j & 1) ? bf16_hi(cw[j >> 1]) : bf16_lo(cw[j >> 1]));
         }
-        const int g = lane >> 3;  // group of columns 8*lane .. 8*lane+7 within the 256 block
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            uint2 q = *reinterpret_cast<const uint2 *>(&sm.w[buf][we + e][lane * 8]);
-            float s = bf16_bits_to_f32(sm.s[buf][we + e][g]), b = bf16_bits_to_f32(sm.b[buf][we + e][g]);
+            const float4 w0 = *reinterpret_cast<const float4 *>(&sm.w[we + e][0][lane][0]);
+            const float4 w1 = *reinterpret_cast<const float4 *>(&sm.w[we + e][1][lane][0]);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float wv = fmaf(byte_to_f32(j < 4 ? q.x : q.y, j & 3), s, b);
-                float2 w2 = make_float2(wv, wv);
+                const float2 w2 = make_float2(wv[j], wv[j]);
 #pragma unroll
                 for (int p = 0; p < 4; ++p) acc[p][e] = ffma2(xp[p][j], w2, acc[p][e]);
             }
         }
         __syncthreads();
     }
-    // butterfly per output, then lane (e) writes
+    // butterfly per output, then lane e writes
 #pragma unroll
     for (int p = 0; p < 4; ++p)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            float a = warp_sum_butterfly(acc[p][e].x), c = warp_sum_butterfly(acc[p][e].y);
+            const float a = warp_sum_butterfly(acc[p][e].x), c = warp_sum_butterfly(acc[p][e].y);
             if (lane == e) {
-                int ee = e0 + we + e, ta = t0 + wt + 2 * p;
+                const int ee = e0 + we + e, ta = t0 + wt + 2 * p;
                 if (ee < E) {
-                    float bb = bias ? bias[ee] : 0.f;
+                    const float bb = bias ? bias[ee] : 0.f;
                     if (ta < T) logits[(size_t)ta * E + ee] = a + bb;
                     if (ta + 1 < T) logits[(size_t)(ta + 1) * E + ee] = c + bb;
                 }
@@ -184,6 +205,40 @@ __global__ void router_logits_gemv_kernel(const uint16_t *__restrict__ x, int T,
 // 8 chosen logits (Qwen36Model.cs:259-261, :293-298). Non-finite logits set kErrNonFinite.
 // The warp also computes the shared-route gate logit (canonical order). Each CTA owns a
 // contiguous token range and writes the per-expert route counts of that range.
+// 8 rounds of a warp arg-max over (value desc, index asc): the 8 largest logits in descending
+// order with ties to the lower expert id. v[j] is this lane's candidate lane + 32j; all lanes
+// return the same sel/chosen. Non-finite candidates must already be replaced by -inf.
+__device__ __forceinline__ void select_top8(const float *v, int E, int32_t *sel, float *chosen) {
+    const int lane = lane_id();
+    uint32_t used = 0;  // bit j: candidate lane+32j taken
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+        float best = -INFINITY;
+        int bid = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane + 32 * j;
+            const bool ok = e < E && !((used >> j) & 1u);
+            if (ok && (v[j] > best || bid == 0x7fffffff)) {
+                best = v[j];
+                bid = e;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            const float ob = __shfl_xor_sync(kFull, best, off);
+            const int oi = __shfl_xor_sync(kFull, bid, off);
+            if (oi != 0x7fffffff && (bid == 0x7fffffff || ob > best || (ob == best && oi < bid))) {
+                best = ob;
+                bid = oi;
+            }
+        }
+        sel[n] = bid;
+        chosen[n] = best;
+        if ((bid & 31) == lane) used |= 1u << (bid >> 5);
+    }
+}
+
 namespace topk {
 constexpr int WARPS = 8, TOK_PER_WARP = 8, TOK_PER_CTA = WARPS * TOK_PER_WARP;  // 64 tokens = 512 routes
 }
@@ -230,33 +285,7 @@ topk_count_kernel(const float *__restrict__ logits, int T, int E, const uint16_t
                 }
             }
             if (__any_sync(kFull, nonfinite) && lane == 0) atomicOr(err, kErrNonFinite);
-            uint32_t used = 0;  // bit j: candidate lane+32j taken
-#pragma unroll
-            for (int n = 0; n < 8; ++n) {
-                float best = -INFINITY;
-                int bid = 0x7fffffff;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    int e = lane + 32 * j;
-                    bool ok = e < E && !((used >> j) & 1u);
-                    if (ok && (v[j] > best || bid == 0x7fffffff)) {
-                        best = v[j];
-                        bid = e;
-                    }
-                }
-#pragma unroll
-                for (int off = 16; off; off >>= 1) {
-                    float ob = __shfl_xor_sync(kFull, best, off);
-                    int oi = __shfl_xor_sync(kFull, bid, off);
-                    if (oi != 0x7fffffff && (bid == 0x7fffffff || ob > best || (ob == best && oi < bid))) {
-                        best = ob;
-                        bid = oi;
-                    }
-                }
-                sel[n] = bid;
-                chosen[n] = best;
-                if ((bid & 31) == lane) used |= 1u << (bid >> 5);
-            }
+            select_top8(v, E, sel, chosen);
         }
         // softmax over the chosen logits
         float mx = chosen[0];
@@ -294,7 +323,7 @@ topk_count_kernel(const float *__restrict__ logits, int T, int E, const uint16_t
 // Single CTA. For expert e: block_base[blk][e] = routes of e in blocks before blk;
 // counts[e]; segment offsets (exclusive scan over experts). The shared expert is segment E
 // with T rows placed after all routed rows (offset 8T). Emits the work tiles of the
-// grouped GEMMs: (segment, first row, valid rows) with at most `bn` rows each.
+// grouped GEMMs: (segment, first row, valid rows), at most `bn` rows each, balanced.
 struct Tile {
     int32_t seg, p0, n;
 };
@@ -338,8 +367,10 @@ scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int E, 
         seg_off[tid] = off[tid];
         if (toff[E + 1] <= max_tiles)
             for (int i = 0; i < ntile[tid]; ++i) {
-                int p0 = i * bn;
-                tiles[toff[tid] + i] = Tile{tid, off[tid] + p0, min(bn, cnt[tid] - p0)};
+                // balanced split: tile sizes differ by at most one row
+                const int a = (int)((int64_t)i * cnt[tid] / ntile[tid]);
+                const int b = (int)((int64_t)(i + 1) * cnt[tid] / ntile[tid]);
+                tiles[toff[tid] + i] = Tile{tid, off[tid] + a, b - a};
             }
     }
 }
