@@ -140,9 +140,9 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    if world > 1:
-        raise SystemExit("expert-parallel multi-GPU run is not available in this build")
     torch.cuda.set_device(local)
+    if world > 1:
+        return run_expert_parallel(args, di, torch, rank, local, world)
     ctx = di.Context(resident=0)
     layers = [di.MoeLayer.generated(ctx, SEED, l, bits=8) for l in range(LAYERS)]
     norms = torch.ones((LAYERS, D), dtype=torch.float32, device="cuda")
@@ -229,6 +229,89 @@ def run_ours(args):
     for l in layers:
         l.close()
     ctx.close()
+
+
+def run_expert_parallel(args, di, torch, rank, local, world):
+    """configs[2] at N GPUs: 256/N experts per GPU, the 8192 tokens sharded 8192/N per GPU,
+    token dispatch and combine over NCCL inside the library (di_moe_ep_stack)."""
+    import datetime
+
+    import numpy as np
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    ctx = di.Context(resident=0)
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(di.ExpertParallel.unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    ep = di.ExpertParallel(ctx, bytes(uid.cpu().numpy().tobytes()), rank, world)
+    layers = [ep.layer(di.generate_layer_matrices(ctx, SEED, l, 8, E, D, I, shard=(rank, world)))
+              for l in range(LAYERS)]
+    Tl = TOKENS // world
+    norms = torch.ones((LAYERS, D), dtype=torch.float32, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(SEED)
+    x0 = torch.randn((TOKENS, D), generator=gen, device="cuda").to(torch.bfloat16).float()[rank * Tl:(rank + 1) * Tl]
+    x = torch.empty_like(x0)
+    for _ in range(args.warmup):
+        x.copy_(x0)
+        torch.cuda.synchronize()
+        ep.stack(layers, norms, x, Tl, 1e-6, di.DEVICE_IO)
+    total = 0.0
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            x.copy_(x0)
+            torch.cuda.synchronize()
+            dist.barrier()
+            total += ep.stack(layers, norms, x, Tl, 1e-6, di.DEVICE_IO)
+            torch.cuda.synchronize()
+    t = torch.tensor([total], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    value = TOKENS / (ms / 1e3)
+    # end to end through the host-buffer API
+    xh = x0.cpu().pin_memory()
+    xo = torch.empty_like(xh).pin_memory()
+    nh = np.ones((LAYERS, D), np.float32)
+    e2e_total = 0.0
+    for i in range(args.warmup + args.steps):
+        xo.copy_(xh)
+        dist.barrier()
+        t0 = time.perf_counter()
+        ep.stack(layers, nh, xo, Tl, 1e-6, 0)
+        if i >= args.warmup:
+            e2e_total += time.perf_counter() - t0
+    et = torch.tensor([e2e_total], dtype=torch.float64, device="cuda")
+    dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e = TOKENS / (float(et.item()) / args.steps)
+    pk = peaks()
+    total_flops = FLOPS_TOKEN_LAYER * TOKENS * LAYERS
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "prefill 8192 tokens (16 x 512 chunks) x 40 MoE layers, 8-bit g64",
+                   "tokens": TOKENS, "layers": LAYERS, "experts": E, "top_k": 8, "intermediate": I, "hidden": D,
+                   "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)", "tokens_per_gpu": Tl,
+                   "l2": "inputs larger than L2 (34.4 GB of weights per step over the node)"},
+        "tensor_frac_step": total_flops / (ms * 1e-3) / (world * pk["bf16_tflops_sustained"] * 1e12),
+        "roofline": {"kernel": "whole expert-parallel step", "bound": "tensor",
+                     "achieved": total_flops / (ms * 1e-3) / 1e12 / world, "peak": pk["bf16_tflops_sustained"],
+                     "unit": "TFLOP/s per GPU", "frac": total_flops / (ms * 1e-3) / (world * pk["bf16_tflops_sustained"] * 1e12),
+                     "traffic": None, "peak_source": pk["source"] + " sustained bf16"},
+        "cpu_baseline": None,
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": Tl * D * 4 * world + LAYERS * D * 4 * world,
+                "d2h_bytes_per_step": Tl * D * 4 * world},
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps * LAYERS * 12,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for l in layers:
+        l.close()
+    ep.close()
+    ctx.close()
+    dist.destroy_process_group()
 
 
 def e2e_and_decode(args, di, torch, ctx, stack, x0):

@@ -89,9 +89,11 @@ void *di_quant_matrix_device_buffer(void *matrix, int index);
 /* Copies `bytes` from host memory into buffer `index` (bytes must equal the buffer size). */
 int di_quant_matrix_upload(void *matrix, int index, const void *src, uint64_t bytes, char *error, int capacity);
 /* Fills the matrix with synthetic weights ~N(0, stddev) quantised by the min/max affine group-64
-   rule, generated on the device bit-identically to the test oracle (seed, stream). */
-int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, float stddev, char *error,
-                             int capacity);
+   rule, generated on the device bit-identically to the test oracle (seed, stream). Expert e of
+   the matrix receives expert first_expert + e of the stream, so a GPU's expert shard equals the
+   same experts of the full matrix. */
+int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, float stddev, int first_expert,
+                             char *error, int capacity);
 
 /* ------------------------------------------------------------------------------------
  * Part 2. The MoE block.
@@ -133,6 +135,30 @@ int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_layer
    layers) on this context: [router, top8+count, scan, scatter, gate_up, down, combine, rmsnorm];
    returns the number written. */
 int di_moe_last_profile(void *ctx, double *stage_ms, int n);
+
+/* ------------------------------------------------------------------------------------
+ * Part 3. Expert parallelism across the GPUs of one node (no reference counterpart: the
+ * reference has no expert, tensor or collective parallelism, docs/ARCHITECTURE.md:63).
+ * One process per GPU. GPU r of G owns experts [r*E/G, (r+1)*E/G) of every layer and a
+ * contiguous shard of the tokens (shards in rank order); the router, shared expert and its
+ * gate are replicated. Token rows travel to the GPUs that own their experts and partial
+ * expert sums travel back over NCCL (NVLink / NVSwitch). Results equal di_moe_stack on the
+ * concatenated tokens up to f32 summation order; routing ids are identical.
+ * ---------------------------------------------------------------------------------- */
+#define DI_EP_ID_BYTES 128
+/* Fills a 128-byte NCCL unique id on rank 0; the caller broadcasts it to every rank. */
+int di_moe_ep_unique_id(uint8_t *id, char *error, int capacity);
+/* Collective over all ranks (blocks until every rank joins). world in [1, 8]. */
+void *di_moe_ep_create(void *ctx, const uint8_t *id, int rank, int world, char *error, int capacity);
+void di_moe_ep_destroy(void *ep);
+/* Binds one layer's shard: gate/up [E/G, I, D] and down [E/G, D, I] hold this rank's experts;
+   router [1, E, D] and the shared matrices are full. Destroy with di_moe_layer_destroy. */
+void *di_moe_ep_layer_create(void *ep, void *router, void *gate, void *up, void *down, void *shared_gate,
+                             void *shared_up, void *shared_down, void *shared_route, char *error, int capacity);
+/* di_moe_stack semantics on this rank's tokens x [tokens, D] (f32 residual, in/out); every rank
+   calls it with the same layers. Flags: DI_MOE_DEVICE_IO. */
+int di_moe_ep_stack(void *ep, void *const *layers, const float *norms, int n_layers, float eps, float *x, int tokens,
+                    int flags, double *ms, char *error, int capacity);
 
 /* Allocation-free small-batch block. No counterpart in the reference; it exists for callers
    that must not allocate GPU memory once they are running: code recording a CUDA graph

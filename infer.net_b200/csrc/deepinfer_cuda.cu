@@ -2,6 +2,8 @@
 #include "../../include/deepinfer_cuda.h"
 
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -16,6 +18,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "ep.cuh"
 #include "gemv.cuh"
 #include "generate.cuh"
 #include "grouped_gemm.cuh"
@@ -66,6 +69,7 @@ struct Layer {
     float *bias = nullptr;  // device [E] or null
     int E = 0, D = 0, I = 0, bits = 0;
     uint64_t gen = 0;       // unique per layer object, for graph cache keys
+    int E_local = 0, E_off = 0;  // expert-parallel shard: experts [E_off, E_off + E_local) are local
 };
 uint64_t g_layer_gen = 0;
 
@@ -377,7 +381,7 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     }
     if (profile) stage_mark(c, S_SCAN);
     // 3. scan counts, segment offsets, GEMM tile list
-    scan_tiles_kernel<<<1, 1024, 0, st>>>(b.block_counts, b.nblocks, E, T, gg::BN, b.block_base, b.seg_count,
+    scan_tiles_kernel<<<1, 1024, 0, st>>>(b.block_counts, b.nblocks, E, E, T, T, gg::BN, b.block_base, b.seg_count,
                                           b.seg_off, b.tiles, b.n_tiles, b.max_tiles, c->d_err);
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
@@ -386,7 +390,7 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     // 5. grouped gate/up + SwiGLU (routed experts and the shared expert)
     const int grid = c->sms;
     {
-        gg::Params p{G, U, SG, SU, x, b.perm, b.tiles, b.n_tiles, T, D, I, E, b.act, nullptr, c->d_err};
+        gg::Params p{G, U, SG, SU, x, b.perm, b.tiles, b.n_tiles, 8 * T, 0, D, I, E, b.act, nullptr, c->d_err};
         if (L->bits == 8)
             gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
         else
@@ -395,7 +399,7 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_DOWN);
     // 6. grouped down -> expert rows in route order, shared rows
     {
-        gg::Params p{Dn, Dn, SD, SD, b.act, b.perm, b.tiles, b.n_tiles, T, I, D, E, b.yr, b.ys, c->d_err};
+        gg::Params p{Dn, Dn, SD, SD, b.act, b.perm, b.tiles, b.n_tiles, 8 * T, 0, I, D, E, b.yr, b.ys, c->d_err};
         if (L->bits == 8)
             gg::grouped_gemm_kernel<gg::MODE_DOWN, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
         else
@@ -611,9 +615,9 @@ API int di_quant_matrix_upload(void *matrix, int index, const void *src, uint64_
     return 0;
 }
 
-API int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, float stddev, char *error,
-                                 int capacity) {
-    if (!live_matrix(matrix) || !(stddev > 0.0f)) {
+API int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, float stddev, int first_expert,
+                                 char *error, int capacity) {
+    if (!live_matrix(matrix) || !(stddev > 0.0f) || first_expert < 0) {
         set_error(error, capacity, "Invalid synthetic weight request");
         return -1;
     }
@@ -624,8 +628,8 @@ API int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, f
         const int64_t groups = rows * (m->cols / 64);
         const float scale = (1.7320508075688772f / 65536.0f) * stddev;
         gen_quant_kernel<<<(unsigned)((groups + 127) / 128), 128, 0, m->ctx->stream>>>(
-            stream_base(seed, stream), scale, rows, m->cols, m->bits, (uint32_t *)m->d[0], (uint16_t *)m->d[1],
-            (uint16_t *)m->d[2]);
+            stream_base(seed, stream), scale, rows, (int64_t)first_expert * m->rows, m->cols, m->bits,
+            (uint32_t *)m->d[0], (uint16_t *)m->d[1], (uint16_t *)m->d[2]);
         CK(cudaGetLastError());
         CK(cudaStreamSynchronize(m->ctx->stream));
         for (int i = 0; i < 3; ++i) {
@@ -865,6 +869,8 @@ API void *di_moe_layer_create(void *ctx, void *router, void *gate, void *up, voi
     L->I = I;
     L->bits = bits;
     L->gen = ++g_layer_gen;
+    L->E_local = E;
+    L->E_off = 0;
     std::lock_guard<std::mutex> g(g_registry);
     g_layers.insert(L);
     return L;
@@ -1201,6 +1207,398 @@ API int di_moe_last_profile(void *ctx, double *stage_ms, int n) {
     const int k = std::min(n, kProfileSlots);
     for (int i = 0; i < k; ++i) stage_ms[i] = c->last_stage_ms[i];
     return k;
+}
+
+
+// ============================================================================ Part 3: expert parallelism
+
+namespace {
+// NCCL is resolved at run time, only when an expert-parallel group is created: a process that
+// already loaded libnccl.so.2 (e.g. through torch) keeps that copy; otherwise the library named
+// by DEEPINFER_NCCL_LIBRARY or the default libnccl.so.2 is loaded. Single-GPU use never loads it.
+struct NcclApi {
+    ncclResult_t (*getUniqueId)(ncclUniqueId *);
+    ncclResult_t (*commInitRank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*commDestroy)(ncclComm_t);
+    ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*allGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*groupStart)();
+    ncclResult_t (*groupEnd)();
+    const char *(*getErrorString)(ncclResult_t);
+};
+const NcclApi *nccl_api(std::string *why) {
+    static NcclApi api{};
+    static bool tried = false, ok = false;
+    static std::string reason;
+    static std::mutex m;
+    std::lock_guard<std::mutex> g(m);
+    if (!tried) {
+        tried = true;
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) {
+            const char *path = std::getenv("DEEPINFER_NCCL_LIBRARY");
+            h = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        }
+        if (!h) {
+            reason = std::string("cannot load NCCL: ") + dlerror();
+        } else {
+            auto sym = [&](const char *n) { return dlsym(h, n); };
+            api.getUniqueId = (decltype(api.getUniqueId))sym("ncclGetUniqueId");
+            api.commInitRank = (decltype(api.commInitRank))sym("ncclCommInitRank");
+            api.commDestroy = (decltype(api.commDestroy))sym("ncclCommDestroy");
+            api.allReduce = (decltype(api.allReduce))sym("ncclAllReduce");
+            api.allGather = (decltype(api.allGather))sym("ncclAllGather");
+            api.send = (decltype(api.send))sym("ncclSend");
+            api.recv = (decltype(api.recv))sym("ncclRecv");
+            api.groupStart = (decltype(api.groupStart))sym("ncclGroupStart");
+            api.groupEnd = (decltype(api.groupEnd))sym("ncclGroupEnd");
+            api.getErrorString = (decltype(api.getErrorString))sym("ncclGetErrorString");
+            ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.allReduce && api.allGather && api.send &&
+                 api.recv && api.groupStart && api.groupEnd && api.getErrorString;
+            if (!ok) reason = "NCCL library lacks a required entry point";
+        }
+    }
+    if (!ok && why) *why = reason;
+    return ok ? &api : nullptr;
+}
+
+struct Ep {
+    Context *ctx = nullptr;
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1;
+    int32_t *h_counts = nullptr;  // pinned [world*world]
+};
+std::set<Ep *> g_eps;
+bool live_ep(void *p) {
+    std::lock_guard<std::mutex> g(g_registry);
+    return p && g_eps.count(static_cast<Ep *>(p));
+}
+struct NcclFail {
+    std::string what;
+};
+#define NK(call)                                                                                      \
+    do {                                                                                              \
+        ncclResult_t r_ = (call);                                                                     \
+        if (r_ != ncclSuccess) throw NcclFail{std::string(#call) + ": " + nc->getErrorString(r_)};    \
+    } while (0)
+}  // namespace
+
+API int di_moe_ep_unique_id(uint8_t *id, char *error, int capacity) {
+    if (!id) {
+        set_error(error, capacity, "Invalid unique id buffer");
+        return -1;
+    }
+    static_assert(sizeof(ncclUniqueId) == DI_EP_ID_BYTES, "NCCL unique id size");
+    std::string why;
+    const NcclApi *nc = nccl_api(&why);
+    if (!nc) {
+        set_error(error, capacity, "%s", why.c_str());
+        return -1;
+    }
+    ncclUniqueId u;
+    ncclResult_t r = nc->getUniqueId(&u);
+    if (r != ncclSuccess) {
+        set_error(error, capacity, "ncclGetUniqueId: %s", nc->getErrorString(r));
+        return -1;
+    }
+    std::memcpy(id, &u, sizeof(u));
+    return 0;
+}
+
+API void *di_moe_ep_create(void *ctx, const uint8_t *id, int rank, int world, char *error, int capacity) {
+    if (!live_context(ctx) || !id || world < 1 || world > kMaxRanks || rank < 0 || rank >= world) {
+        set_error(error, capacity, "Invalid expert-parallel arguments (world 1..%d)", kMaxRanks);
+        return nullptr;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    std::string why;
+    const NcclApi *nc = nccl_api(&why);
+    if (!nc) {
+        set_error(error, capacity, "%s", why.c_str());
+        return nullptr;
+    }
+    DeviceGuard dg(c->device);
+    Ep *ep = new Ep();
+    ep->ctx = c;
+    ep->rank = rank;
+    ep->world = world;
+    ncclUniqueId u;
+    std::memcpy(&u, id, sizeof(u));
+    ncclResult_t r = nc->commInitRank(&ep->comm, world, u, rank);
+    if (r != ncclSuccess) {
+        set_error(error, capacity, "ncclCommInitRank: %s", nc->getErrorString(r));
+        delete ep;
+        return nullptr;
+    }
+    if (cudaMallocHost(&ep->h_counts, sizeof(int32_t) * kMaxRanks * kMaxRanks) != cudaSuccess) {
+        cudaGetLastError();
+        nc->commDestroy(ep->comm);
+        delete ep;
+        set_error(error, capacity, "Pinned host allocation failed");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> g(g_registry);
+    g_eps.insert(ep);
+    return ep;
+}
+
+API void di_moe_ep_destroy(void *p) {
+    if (!live_ep(p)) return;
+    Ep *ep = static_cast<Ep *>(p);
+    {
+        std::lock_guard<std::mutex> g(g_registry);
+        g_eps.erase(ep);
+    }
+    DeviceGuard dg(ep->ctx->device);
+    cudaStreamSynchronize(ep->ctx->stream);
+    nccl_api(nullptr)->commDestroy(ep->comm);
+    cudaFreeHost(ep->h_counts);
+    delete ep;
+}
+
+API void *di_moe_ep_layer_create(void *ep_, void *router, void *gate, void *up, void *down, void *shared_gate,
+                                 void *shared_up, void *shared_down, void *shared_route, char *error, int capacity) {
+    if (!live_ep(ep_)) {
+        set_error(error, capacity, "Invalid expert-parallel handle");
+        return nullptr;
+    }
+    Ep *ep = static_cast<Ep *>(ep_);
+    void *ptrs[8] = {router, gate, up, down, shared_gate, shared_up, shared_down, shared_route};
+    Matrix *m[8];
+    for (int i = 0; i < 8; ++i) {
+        if (!live_matrix(ptrs[i]) || static_cast<Matrix *>(ptrs[i])->ctx != ep->ctx) {
+            set_error(error, capacity, "MoE layer matrix %d is missing, destroyed or on another device", i);
+            return nullptr;
+        }
+        m[i] = static_cast<Matrix *>(ptrs[i]);
+        for (int j = 0; j < i; ++j)
+            if (m[j] == m[i]) {
+                set_error(error, capacity, "MoE layer matrices must be distinct.");
+                return nullptr;
+            }
+    }
+    const int E = m[0]->rows, D = m[0]->cols, El = m[1]->experts, I = m[1]->rows, bits = m[1]->bits;
+    auto shape = [](Matrix *x, int e, int r, int col) { return x->experts == e && x->rows == r && x->cols == col; };
+    bool ok = m[0]->experts == 1 && m[0]->bits == 8 && E >= 8 && E <= 256 && El * ep->world == E && D % 256 == 0 &&
+              I % 64 == 0 && shape(m[1], El, I, D) && shape(m[2], El, I, D) && shape(m[3], El, D, I) &&
+              shape(m[4], 1, I, D) && shape(m[5], 1, I, D) && shape(m[6], 1, D, I) && shape(m[7], 1, 1, D) &&
+              m[7]->bits == 8;
+    for (int i = 1; i < 7; ++i) ok = ok && m[i]->bits == bits;
+    if (!ok) {
+        set_error(error, capacity,
+                  "Unsupported expert-parallel layer: router [1,E,D] 8-bit with E = world * E_local, expert shards "
+                  "[E_local,I,D]/[E_local,D,I], shared [1,I,D]/[1,D,I], shared_route [1,1,D] 8-bit");
+        return nullptr;
+    }
+    Layer *L = new Layer();
+    L->ctx = ep->ctx;
+    for (int i = 0; i < 8; ++i) {
+        L->m[i] = m[i];
+        m[i]->refs++;
+    }
+    L->E = E;
+    L->D = D;
+    L->I = I;
+    L->bits = bits;
+    L->gen = ++g_layer_gen;
+    L->E_local = El;
+    L->E_off = ep->rank * El;
+    std::lock_guard<std::mutex> g(g_registry);
+    g_layers.insert(L);
+    return L;
+}
+
+API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int n_layers, float eps, float *x,
+                        int tokens, int flags, double *ms, char *error, int capacity) {
+    if (!live_ep(ep_) || !layers || n_layers < 1 || n_layers > 1024 || !norms || !x || tokens < 1 ||
+        tokens > 65536 || !(eps > 0.0f) || (flags & ~DI_MOE_DEVICE_IO)) {
+        set_error(error, capacity, "Invalid expert-parallel stack arguments");
+        return -1;
+    }
+    Ep *ep = static_cast<Ep *>(ep_);
+    Context *c = ep->ctx;
+    const int G = ep->world, rank = ep->rank, T = tokens;
+    int D = -1, E = -1, El = -1, I = -1;
+    for (int l = 0; l < n_layers; ++l) {
+        if (!live_layer(layers[l]) || static_cast<Layer *>(layers[l])->ctx != c) {
+            set_error(error, capacity, "Invalid MoE layer %d", l);
+            return -1;
+        }
+        Layer *L = static_cast<Layer *>(layers[l]);
+        if (l == 0) {
+            D = L->D;
+            E = L->E;
+            El = L->E_local;
+            I = L->I;
+        }
+        if (L->D != D || L->E != E || L->E_local != El || L->I != I || El * G != E || L->E_off != rank * El) {
+            set_error(error, capacity, "Layer %d is not an expert-parallel shard of this rank", l);
+            return -1;
+        }
+        for (int i = 0; i < 8; ++i)
+            if (L->m[i]->destroyed) {
+                set_error(error, capacity, "MoE layer matrix was destroyed");
+                return -1;
+            }
+    }
+    const bool dev_io = flags & DI_MOE_DEVICE_IO;
+    const NcclApi *nc = nccl_api(nullptr);
+    DeviceGuard dg(c->device);
+    cudaStream_t st = c->stream;
+    try {
+        for (int l = 0; l < n_layers; ++l)
+            for (int i = 0; i < 8; ++i) sync_matrix(static_cast<Layer *>(layers[l])->m[i]);
+        // total tokens over the ranks bounds the rows any rank can receive
+        Carve cv0;
+        const size_t o_tok = cv0.take<int32_t>(2);
+        ensure_workspace(c, cv0.off + 256);
+        int32_t *d_tok = at<int32_t>(c, o_tok);
+        CK(cudaMemcpyAsync(d_tok, &T, 4, cudaMemcpyHostToDevice, st));
+        NK(nc->allReduce(d_tok, d_tok + 1, 1, ncclInt32, ncclSum, ep->comm, st));
+        CK(cudaMemcpyAsync(ep->h_counts, d_tok + 1, 4, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        const int Rmax = ep->h_counts[0];
+        const int Smax = T * std::min(8, G);
+        const int nb_l = (T + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA;
+        const int nb_r = (Rmax + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA;
+        const int max_tiles = (8 * Rmax + gg::BN - 1) / gg::BN + El + (T + gg::BN - 1) / gg::BN + 2;
+        Carve cv;
+        cv.take<int32_t>(2);  // keep the token-count words
+        const size_t o_x = dev_io ? 0 : cv.take<float>((size_t)T * D), o_n = dev_io ? 0 : cv.take<float>((size_t)n_layers * D);
+        const size_t o_h = cv.take<uint16_t>((size_t)T * D), o_lg = cv.take<float>((size_t)T * E);
+        const size_t o_ids = cv.take<int32_t>((size_t)T * 8), o_p = cv.take<float>((size_t)T * 8), o_g = cv.take<float>(T);
+        const size_t o_bc = cv.take<int32_t>((size_t)nb_l * E), o_sidx = cv.take<int32_t>((size_t)T * G);
+        const size_t o_sc = cv.take<int32_t>(kMaxRanks), o_so = cv.take<int32_t>(kMaxRanks);
+        const size_t o_all = cv.take<int32_t>(kMaxRanks * kMaxRanks);
+        const size_t o_sx = cv.take<uint16_t>((size_t)Smax * D), o_sm = cv.take<RowMeta>((size_t)Smax);
+        const size_t o_rx = cv.take<uint16_t>((size_t)(Rmax + T) * D), o_rm = cv.take<RowMeta>((size_t)Rmax + 1);
+        const size_t o_il = cv.take<int32_t>((size_t)Rmax * 8 + 8), o_rbc = cv.take<int32_t>((size_t)(nb_r + 1) * (El + 1));
+        const size_t o_rbb = cv.take<int32_t>((size_t)(nb_r + 1) * (El + 1)), o_sgc = cv.take<int32_t>(El + 2);
+        const size_t o_sgo = cv.take<int32_t>(El + 2), o_t = cv.take<Tile>(max_tiles), o_nt = cv.take<int32_t>(1);
+        const size_t o_pm = cv.take<int32_t>((size_t)Rmax * 8 + 8), o_act = cv.take<uint16_t>(((size_t)Rmax * 8 + T) * I);
+        const size_t o_y = cv.take<uint16_t>((size_t)Rmax * 8 * D + 8), o_ys = cv.take<uint16_t>((size_t)T * D);
+        const size_t o_z = cv.take<uint16_t>((size_t)Rmax * D + 8), o_bk = cv.take<uint16_t>((size_t)Smax * D);
+        ensure_workspace(c, cv.off + 256);
+        float *dx = dev_io ? x : at<float>(c, o_x);
+        const float *dn = dev_io ? norms : at<float>(c, o_n);
+        uint16_t *h = at<uint16_t>(c, o_h), *sx = at<uint16_t>(c, o_sx), *rx = at<uint16_t>(c, o_rx);
+        uint16_t *act = at<uint16_t>(c, o_act), *y = at<uint16_t>(c, o_y), *ys = at<uint16_t>(c, o_ys);
+        uint16_t *z = at<uint16_t>(c, o_z), *bk = at<uint16_t>(c, o_bk);
+        float *logits = at<float>(c, o_lg), *probs = at<float>(c, o_p), *gate = at<float>(c, o_g);
+        int32_t *ids = at<int32_t>(c, o_ids), *bc = at<int32_t>(c, o_bc), *sidx = at<int32_t>(c, o_sidx);
+        int32_t *sc = at<int32_t>(c, o_sc), *so = at<int32_t>(c, o_so), *all = at<int32_t>(c, o_all);
+        int32_t *il = at<int32_t>(c, o_il), *rbc = at<int32_t>(c, o_rbc), *rbb = at<int32_t>(c, o_rbb);
+        int32_t *sgc = at<int32_t>(c, o_sgc), *sgo = at<int32_t>(c, o_sgo), *nt = at<int32_t>(c, o_nt);
+        int32_t *perm = at<int32_t>(c, o_pm);
+        RowMeta *smeta = at<RowMeta>(c, o_sm), *rmeta = at<RowMeta>(c, o_rm);
+        Tile *tiles = at<Tile>(c, o_t);
+        CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st));
+        CK(cudaEventRecord(c->ev_start, st));
+        if (!dev_io) {
+            CK(cudaMemcpyAsync(dx, x, (size_t)T * D * 4, cudaMemcpyHostToDevice, st));
+            CK(cudaMemcpyAsync(const_cast<float *>(dn), norms, (size_t)n_layers * D * 4, cudaMemcpyHostToDevice, st));
+        }
+        const int grid = c->sms;
+        for (int l = 0; l < n_layers; ++l) {
+            Layer *L = static_cast<Layer *>(layers[l]);
+            const QView R = L->m[0]->view(), Gm = L->m[1]->view(), U = L->m[2]->view(), Dm = L->m[3]->view();
+            const QView SG = L->m[4]->view(), SU = L->m[5]->view(), SD = L->m[6]->view(), SR = L->m[7]->view();
+            // 1. route the local tokens
+            rmsnorm_kernel<<<T, 256, 0, st>>>(dx, dn + (size_t)l * D, D, eps, h, nullptr);
+            router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
+                                   router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);
+            topk_count_kernel<<<nb_l, topk::WARPS * 32, 0, st>>>(logits, T, E, h, D, SR, nullptr, ids, probs, gate, bc,
+                                                                  c->d_err);
+            // 2. one row per (token, destination GPU), then the counts of every pair of GPUs
+            ep_layout_kernel<<<1, 1024, 0, st>>>(ids, T, El, G, sidx, sc, so);
+            ep_pack_kernel<<<T, 256, 0, st>>>(h, ids, probs, D, G, sidx, so, sx, smeta);
+            NK(nc->allGather(sc, all, G, ncclInt32, ep->comm, st));
+            CK(cudaMemcpyAsync(ep->h_counts, all, sizeof(int32_t) * G * G, cudaMemcpyDeviceToHost, st));
+            CK(cudaStreamSynchronize(st));
+            int scnt[kMaxRanks], rcnt[kMaxRanks], soff[kMaxRanks], roff[kMaxRanks], Rn = 0, Sn = 0;
+            for (int q = 0; q < G; ++q) {
+                scnt[q] = ep->h_counts[rank * G + q];
+                rcnt[q] = ep->h_counts[q * G + rank];
+                soff[q] = Sn;
+                roff[q] = Rn;
+                Sn += scnt[q];
+                Rn += rcnt[q];
+            }
+            if (Rn > Rmax || Sn > Smax) throw CudaFail{"expert-parallel row counts exceed their bound"};
+            // 3. dispatch token rows and their routing metadata
+            NK(nc->groupStart());
+            for (int q = 0; q < G; ++q) {
+                if (scnt[q]) {
+                    NK(nc->send(sx + (size_t)soff[q] * D, (size_t)scnt[q] * D * 2, ncclUint8, q, ep->comm, st));
+                    NK(nc->send(smeta + soff[q], (size_t)scnt[q] * sizeof(RowMeta), ncclUint8, q, ep->comm, st));
+                }
+                if (rcnt[q]) {
+                    NK(nc->recv(rx + (size_t)roff[q] * D, (size_t)rcnt[q] * D * 2, ncclUint8, q, ep->comm, st));
+                    NK(nc->recv(rmeta + roff[q], (size_t)rcnt[q] * sizeof(RowMeta), ncclUint8, q, ep->comm, st));
+                }
+            }
+            NK(nc->groupEnd());
+            // 4. local experts over the received rows, shared expert over the local rows
+            CK(cudaMemcpyAsync(rx + (size_t)Rn * D, h, (size_t)T * D * 2, cudaMemcpyDeviceToDevice, st));
+            const int nbr = std::max(1, (Rn + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA);
+            if (Rn > 0) ep_recv_count_kernel<<<nbr, 256, 0, st>>>(rmeta, Rn, L->E_off, El, il, rbc);
+            else CK(cudaMemsetAsync(rbc, 0, sizeof(int32_t) * (El + 1), st));
+            scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, Rn, T, gg::BN, rbb, sgc, sgo, tiles, nt,
+                                                  max_tiles, c->d_err);
+            if (Rn > 0) scatter_routes_kernel<<<nbr, 32, 0, st>>>(il, Rn, El + 1, rbb, sgo, perm);
+            {
+                gg::Params p{Gm, U, SG, SU, rx, perm, tiles, nt, 8 * Rn, Rn, D, I, El + 1, act, nullptr, c->d_err};
+                if (L->bits == 8) gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+                else gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+            }
+            {
+                gg::Params p{Dm, Dm, SD, SD, act, perm, tiles, nt, 8 * Rn, 0, I, D, El + 1, y, ys, c->d_err};
+                if (L->bits == 8) gg::grouped_gemm_kernel<gg::MODE_DOWN, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+                else gg::grouped_gemm_kernel<gg::MODE_DOWN, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+            }
+            // 5. partial row sums back to the token owners, then the owner's combine
+            if (Rn > 0) {
+                const size_t n = (size_t)Rn * (D / 8);
+                ep_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(y, il, rmeta, Rn, D, El, z);
+            }
+            NK(nc->groupStart());
+            for (int q = 0; q < G; ++q) {
+                if (rcnt[q]) NK(nc->send(z + (size_t)roff[q] * D, (size_t)rcnt[q] * D * 2, ncclUint8, q, ep->comm, st));
+                if (scnt[q]) NK(nc->recv(bk + (size_t)soff[q] * D, (size_t)scnt[q] * D * 2, ncclUint8, q, ep->comm, st));
+            }
+            NK(nc->groupEnd());
+            {
+                const size_t n = (size_t)T * (D / 8);
+                ep_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(bk, sidx, so, G, ys, gate, T, D, dx,
+                                                                                c->d_err);
+            }
+            if (launch_check(error, capacity)) return -1;
+        }
+        CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+        if (dev_io) CK(cudaEventRecord(c->ev_stop, st));
+        CK(cudaStreamSynchronize(st));
+        if (*c->h_err) {
+            set_error(error, capacity, "%s", device_error_text(*c->h_err));
+            return -1;
+        }
+        if (!dev_io) {
+            CK(cudaMemcpyAsync(x, dx, (size_t)T * D * 4, cudaMemcpyDeviceToHost, st));
+            CK(cudaEventRecord(c->ev_stop, st));
+            CK(cudaStreamSynchronize(st));
+        }
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
+        if (ms) *ms = t;
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    } catch (const NcclFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
 }
 
 // ============================================================================ allocation-free block

@@ -24,7 +24,8 @@ __device__ __forceinline__ float normal_sample(uint64_t base, uint64_t index, fl
 }
 
 // One thread per 64-value group of one row.
-__global__ void gen_quant_kernel(uint64_t base, float scale, int64_t total_rows, int cols, int bits,
+// row_offset: stream row of the matrix's first row (expert shards start at first_expert * rows).
+__global__ void gen_quant_kernel(uint64_t base, float scale, int64_t total_rows, int64_t row_offset, int cols, int bits,
                                  uint32_t *__restrict__ packed, uint16_t *__restrict__ scales,
                                  uint16_t *__restrict__ biases) {
     const int groups = cols / 64;
@@ -35,7 +36,7 @@ __global__ void gen_quant_kernel(uint64_t base, float scale, int64_t total_rows,
     float w[64];
     float lo, hi;
 #pragma unroll
-    for (int i = 0; i < 64; ++i) w[i] = normal_sample(base, (uint64_t)(r * cols + g * 64 + i), scale);
+    for (int i = 0; i < 64; ++i) w[i] = normal_sample(base, (uint64_t)((r + row_offset) * cols + g * 64 + i), scale);
     lo = hi = w[0];
 #pragma unroll
     for (int i = 1; i < 64; ++i) {

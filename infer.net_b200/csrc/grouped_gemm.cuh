@@ -51,7 +51,9 @@ struct Params {
     const int32_t *perm_route; // [8T] route id of each permuted position
     const Tile *tiles;
     const int32_t *n_tiles;
-    int T, K, rows, E;         // rows: I (GATE_UP) or D (DOWN)
+    int shared_pos0;           // first permuted position of the shared-expert segment
+    int shared_src0;           // GATE_UP: source row of that first shared position
+    int K, rows, E;            // rows: I (GATE_UP) or D (DOWN); segments >= E are the shared expert
     uint16_t *out;             // GATE_UP: act [P, rows]; DOWN: y [8T, rows]
     uint16_t *out_shared;      // DOWN: ys [T, rows]
     uint32_t *err;
@@ -308,7 +310,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
                     const int n = g8 * 8 + lane;
                     const int pos = tl.p0 + min(n, tl.n - 1);
                     int row;
-                    if constexpr (MODE == MODE_GATE_UP) row = shared ? pos - 8 * p.T : (p.perm_route[pos] >> 3);
+                    if constexpr (MODE == MODE_GATE_UP) row = shared ? p.shared_src0 + (pos - p.shared_pos0) : (p.perm_route[pos] >> 3);
                     else row = pos;
                     tok_table[n] = row;
                 }
@@ -435,7 +437,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
                         if (n < tl.n && d < p.rows) {
                             const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 64 + part * 16);
                             const int pos = tl.p0 + n;
-                            uint16_t *dst = shared ? p.out_shared + (size_t)(pos - 8 * p.T) * p.rows
+                            uint16_t *dst = shared ? p.out_shared + (size_t)(pos - p.shared_pos0) * p.rows
                                                    : p.out + (size_t)p.perm_route[pos] * p.rows;
                             *reinterpret_cast<uint4 *>(dst + d) = val;
                         }

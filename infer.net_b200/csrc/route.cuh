@@ -320,41 +320,46 @@ topk_count_kernel(const float *__restrict__ logits, int T, int E, const uint16_t
 
 // ------------------------------------------------------------------ scan + tile list
 //
-// Single CTA. For expert e: block_base[blk][e] = routes of e in blocks before blk;
-// counts[e]; segment offsets (exclusive scan over experts). The shared expert is segment E
-// with T rows placed after all routed rows (offset 8T). Emits the work tiles of the
-// grouped GEMMs: (segment, first row, valid rows), at most `bn` rows each, balanced.
+// Single CTA. Histogram buckets e < n_hist (routed experts, plus optionally a bucket for
+// routes that belong to another GPU): block_base[blk][e] = routes of e in blocks before blk;
+// counts; segment offsets (exclusive scan over buckets). The shared expert is segment n_hist
+// with `shared_count` rows placed after all routed positions (offset 8*rows). Emits the work
+// tiles of the grouped GEMMs for buckets e < n_tiled and the shared segment: (segment, first
+// position, rows), at most `bn` rows each, balanced.
 struct Tile {
     int32_t seg, p0, n;
 };
 
+constexpr int kMaxBuckets = 260;
+
 __global__ void __launch_bounds__(1024)
-scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int E, int T, int bn,
-                  int32_t *__restrict__ block_base, int32_t *__restrict__ seg_count, int32_t *__restrict__ seg_off,
-                  Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles, int max_tiles, uint32_t *__restrict__ err) {
-    __shared__ int32_t cnt[257], ntile[257], toff[258], off[258];
-    const int tid = threadIdx.x;
-    if (tid < E) {
+scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int n_hist, int n_tiled, int rows,
+                  int shared_count, int bn, int32_t *__restrict__ block_base, int32_t *__restrict__ seg_count,
+                  int32_t *__restrict__ seg_off, Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles, int max_tiles,
+                  uint32_t *__restrict__ err) {
+    __shared__ int32_t cnt[kMaxBuckets], ntile[kMaxBuckets], toff[kMaxBuckets + 1], off[kMaxBuckets + 1];
+    const int tid = threadIdx.x, S = n_hist;  // segment S = shared expert
+    if (tid < n_hist) {
         int run = 0;
         for (int b = 0; b < nblocks; ++b) {
-            block_base[(size_t)b * E + tid] = run;
-            run += block_counts[(size_t)b * E + tid];
+            block_base[(size_t)b * n_hist + tid] = run;
+            run += block_counts[(size_t)b * n_hist + tid];
         }
         cnt[tid] = run;
     }
-    if (tid == 0) cnt[E] = T;
+    if (tid == 0) cnt[S] = shared_count;
     __syncthreads();
-    if (tid <= E) ntile[tid] = (cnt[tid] + bn - 1) / bn;
+    if (tid <= S) ntile[tid] = (tid < n_tiled || tid == S) ? (cnt[tid] + bn - 1) / bn : 0;
     __syncthreads();
     if (tid == 0) {
         int run = 0, tr = 0;
-        for (int e = 0; e <= E; ++e) {
-            off[e] = (e == E) ? 8 * T : run;
-            run += (e < E) ? cnt[e] : 0;
+        for (int e = 0; e <= S; ++e) {
+            off[e] = (e == S) ? 8 * rows : run;
+            run += (e < S) ? cnt[e] : 0;
             toff[e] = tr;
             tr += ntile[e];
         }
-        toff[E + 1] = tr;
+        toff[S + 1] = tr;
         if (tr > max_tiles) {
             atomicOr(err, kErrCapacity);
             tr = 0;
@@ -362,10 +367,10 @@ scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int E, 
         *n_tiles = tr;
     }
     __syncthreads();
-    if (tid <= E) {
+    if (tid <= S) {
         seg_count[tid] = cnt[tid];
         seg_off[tid] = off[tid];
-        if (toff[E + 1] <= max_tiles)
+        if (toff[S + 1] <= max_tiles)
             for (int i = 0; i < ntile[tid]; ++i) {
                 // balanced split: tile sizes differ by at most one row
                 const int a = (int)((int64_t)i * cnt[tid] / ntile[tid]);
@@ -383,7 +388,7 @@ scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int E, 
 __global__ void __launch_bounds__(32)
 scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32_t *__restrict__ block_base,
                       const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route) {
-    __shared__ int32_t run[256];
+    __shared__ int32_t run[kMaxBuckets];
     const int lane = threadIdx.x;
     for (int i = lane; i < E; i += 32) run[i] = 0;
     __syncwarp();

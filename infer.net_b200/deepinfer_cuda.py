@@ -56,7 +56,8 @@ SIGNATURES = {
     "di_quant_embedding": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
     "di_quant_matrix_device_buffer": (C.c_void_p, [C.c_void_p, C.c_int]),
     "di_quant_matrix_upload": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_uint64, C.c_char_p, C.c_int]),
-    "di_quant_matrix_generate": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_float, C.c_char_p, C.c_int]),
+    "di_quant_matrix_generate": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_float, C.c_int, C.c_char_p,
+                                           C.c_int]),
     "di_moe_layer_create": (C.c_void_p, [C.c_void_p] * 9 + [C.c_char_p, C.c_int]),
     "di_moe_layer_destroy": (None, [C.c_void_p]),
     "di_moe_layer_set_router_bias": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_int]),
@@ -65,6 +66,12 @@ SIGNATURES = {
     "di_moe_stack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_int,
                                C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
     "di_moe_last_profile": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.c_int]),
+    "di_moe_ep_unique_id": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
+    "di_moe_ep_create": (C.c_void_p, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.c_int]),
+    "di_moe_ep_destroy": (None, [C.c_void_p]),
+    "di_moe_ep_layer_create": (C.c_void_p, [C.c_void_p] * 9 + [C.c_char_p, C.c_int]),
+    "di_moe_ep_stack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_int,
+                                  C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
     "di_moe_block_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
 }
@@ -205,9 +212,9 @@ class Matrix:
         self.upload(2, q.biases)
         return self
 
-    def generate(self, seed, stream, stddev=0.02):
+    def generate(self, seed, stream, stddev=0.02, first_expert=0):
         err = C.create_string_buffer(2048)
-        if lib().di_quant_matrix_generate(self.h, seed, stream, stddev, err, 2048):
+        if lib().di_quant_matrix_generate(self.h, seed, stream, stddev, first_expert, err, 2048):
             raise DeepInferError(err.value.decode())
         return self
 
@@ -264,14 +271,7 @@ class MoeLayer:
     @classmethod
     def generated(cls, ctx: Context, seed: int, layer: int, bits: int = 8, E=256, D=2048, I=512, stddev=0.02):
         """Synthetic weights generated on the device (same bits as oracle.Layer(seed, layer, ...))."""
-        shapes = {"router": (1, E, D, 8), "gate": (E, I, D, bits), "up": (E, I, D, bits), "down": (E, D, I, bits),
-                  "shared_gate": (1, I, D, bits), "shared_up": (1, I, D, bits), "shared_down": (1, D, I, bits),
-                  "shared_route": (1, 1, D, 8)}
-        mats = {}
-        for k, n in enumerate(LAYER_ORDER):
-            e, r, c, b = shapes[n]
-            mats[n] = Matrix(ctx, e, r, c, b).generate(seed, layer * 16 + k, stddev)
-        return cls(ctx, mats)
+        return cls(ctx, generate_layer_matrices(ctx, seed, layer, bits, E, D, I, stddev))
 
     def set_router_bias(self, bias):
         err = C.create_string_buffer(2048)
@@ -295,6 +295,65 @@ class MoeLayer:
         if matrices:
             for m in self.mats.values():
                 m.close()
+
+
+def generate_layer_matrices(ctx, seed, layer, bits=8, E=256, D=2048, I=512, stddev=0.02, shard=(0, 1)):
+    """Device-generated matrices of one layer; with shard=(rank, world) the routed experts are the
+    rank's contiguous share [rank*E/world, (rank+1)*E/world) of the same full layer."""
+    rank, world = shard
+    El = E // world
+    shapes = {"router": (1, E, D, 8, 0), "gate": (El, I, D, bits, rank * El), "up": (El, I, D, bits, rank * El),
+              "down": (El, D, I, bits, rank * El), "shared_gate": (1, I, D, bits, 0),
+              "shared_up": (1, I, D, bits, 0), "shared_down": (1, D, I, bits, 0), "shared_route": (1, 1, D, 8, 0)}
+    mats = {}
+    for k, n in enumerate(LAYER_ORDER):
+        e, r, c, b, first = shapes[n]
+        mats[n] = Matrix(ctx, e, r, c, b).generate(seed, layer * 16 + k, stddev, first)
+    return mats
+
+
+class ExpertParallel:
+    """NCCL expert-parallel group of one process per GPU (di_moe_ep_*)."""
+
+    def __init__(self, ctx: Context, unique_id: bytes, rank: int, world: int):
+        err = C.create_string_buffer(2048)
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        h = lib().di_moe_ep_create(ctx.h, buf, rank, world, err, 2048)
+        if not h:
+            raise DeepInferError(err.value.decode())
+        self.ctx, self.h, self.rank, self.world = ctx, h, rank, world
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * 128)()
+        err = C.create_string_buffer(2048)
+        if lib().di_moe_ep_unique_id(buf, err, 2048):
+            raise DeepInferError(err.value.decode())
+        return bytes(buf)
+
+    def layer(self, mats: dict) -> "MoeLayer":
+        err = C.create_string_buffer(2048)
+        h = lib().di_moe_ep_layer_create(self.h, *[mats[n].h for n in LAYER_ORDER], err, 2048)
+        if not h:
+            raise DeepInferError(err.value.decode())
+        obj = MoeLayer.__new__(MoeLayer)
+        obj.ctx, obj.h, obj.mats = self.ctx, h, mats
+        return obj
+
+    def stack(self, layers, norms, x, tokens, eps=1e-6, flags=0):
+        arr = (C.c_void_p * len(layers))(*[l.h for l in layers])
+        ms = C.c_double()
+        err = C.create_string_buffer(2048)
+        rc = lib().di_moe_ep_stack(self.h, C.cast(arr, C.c_void_p), _p(norms), len(layers), eps, _p(x), tokens,
+                                   flags, C.byref(ms), err, 2048)
+        if rc:
+            raise DeepInferError(err.value.decode())
+        return ms.value
+
+    def close(self):
+        if self.h:
+            lib().di_moe_ep_destroy(self.h)
+            self.h = None
 
 
 def moe_block(layer: MoeLayer, x_bf16: np.ndarray, flags: int = 0, forced: np.ndarray | None = None):

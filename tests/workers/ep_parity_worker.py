@@ -1,0 +1,54 @@
+"""Worker of tests/test_gpu_ep.py (run under torchrun, one process per GPU).
+
+Builds a small model twice -- full layers on every rank and the rank's expert shard -- runs the
+expert-parallel stack on uneven contiguous token shards and compares the rows against the
+single-GPU stack on all tokens. Exits non-zero on a mismatch.
+"""
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.join(ROOT, "infer.net_b200"))
+import deepinfer_cuda as di  # noqa: E402
+
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+local = int(os.environ.get("LOCAL_RANK", rank))
+torch.cuda.set_device(local)
+dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+E, D, I, L, SEED = 64, 256, 128, 3, 77
+bits = int(os.environ.get("EP_BITS", "8"))
+sizes = [40 + 16 * r for r in range(world)]  # uneven shards, in rank order
+T = sum(sizes)
+ctx = di.Context(resident=0)
+uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+if rank == 0:
+    uid.copy_(torch.frombuffer(bytearray(di.ExpertParallel.unique_id()), dtype=torch.uint8))
+dist.broadcast(uid, 0)
+ep = di.ExpertParallel(ctx, bytes(uid.cpu().numpy().tobytes()), rank, world)
+shards = [ep.layer(di.generate_layer_matrices(ctx, SEED, l, bits, E, D, I, shard=(rank, world))) for l in range(L)]
+full = [di.MoeLayer(ctx, di.generate_layer_matrices(ctx, SEED, l, bits, E, D, I)) for l in range(L)]
+rng = np.random.default_rng(5)
+x = rng.standard_normal((T, D)).astype(np.float32)
+norms = (1.0 + 0.1 * np.cos(np.arange(L * D))).astype(np.float32).reshape(L, D)
+lo = sum(sizes[:rank])
+xs = x[lo:lo + sizes[rank]].copy()
+ep.stack(shards, norms, xs, sizes[rank], 1e-6, 0)
+ref, _, _, _ = di.moe_stack(ctx, full, norms, x, 1e-6, di.PATH_GROUPED)
+ref = ref[lo:lo + sizes[rank]]
+err = np.abs(xs.astype(np.float64) - ref)
+rel = np.linalg.norm(xs - ref) / np.linalg.norm(ref)
+ok = float(err.max()) <= 2e-2 and rel <= 5e-3
+print(f"rank {rank}: rows {sizes[rank]} max_abs {err.max():.3e} rel_l2 {rel:.3e} ok {ok}", flush=True)
+flag = torch.tensor([0 if ok else 1], device="cuda")
+dist.all_reduce(flag)
+for l in shards + full:
+    l.close()
+ep.close()
+ctx.close()
+dist.destroy_process_group()
+sys.exit(int(flag.item() != 0))
