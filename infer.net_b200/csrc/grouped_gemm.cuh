@@ -28,17 +28,19 @@ namespace gg {
 
 constexpr int MODE_GATE_UP = 0, MODE_DOWN = 1;
 constexpr int BM = 128;          // A rows per unit (one MMA M)
-constexpr int BN = 512;          // max tokens per unit (two accumulators of 256 columns)
+constexpr int BN = 256;          // max tokens per unit (one 256-column accumulator slot)
 constexpr int BK = 32;           // K per pipeline stage: 64-byte rows
-constexpr int STAGES = 5;
-constexpr int LOAD_DEPTH = 3;   // B-loader stages in flight (< STAGES)
+constexpr int STAGES = 7;
+constexpr int RING = 4;         // dequantiser code ring: own stages in flight per thread
+constexpr int kRingSlot = 48;   // bytes per thread per slot: 32 code bytes + 2 scale words + 2 bias words
 constexpr int THREADS = 512;
 constexpr int kA = BM * 64;      // bytes of one A stage tile
 constexpr int kB = BN * 64;      // bytes of one B stage tile
 constexpr int STAGE_BYTES = kA + kB;
 constexpr int kTable = BN * 4;   // token row table of the B loaders
 constexpr int kStageOut = 4 * 16 * 64;  // epilogue staging: 4 warps x 16 tokens x 64 bytes
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + kTable + kStageOut + 256;
+constexpr int kRing = 256 * RING * kRingSlot;
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + kTable + kStageOut + kRing + 256;
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int MODE>
@@ -227,7 +229,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
     uint8_t *smem = smem_raw + pad;
     int32_t *tok_table = reinterpret_cast<int32_t *>(smem + STAGES * STAGE_BYTES);
     uint8_t *stage_out = reinterpret_cast<uint8_t *>(tok_table + BN);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
+    uint8_t *ring = stage_out + kStageOut;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kRing);
     uint64_t *full = bars, *empty = bars + STAGES;
     uint64_t *accf = bars + 2 * STAGES, *acce = accf + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 4 + 3);  // one dequant group (4 warps) + 3 loader warps
+            mbar_init(&full[s], 4 + 96);  // one dequant group (4 warp arrivals) + 96 loader threads' copies
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -264,42 +267,106 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
     // Flat pipeline index `it`: unit u = blockIdx.x + (it / nk) * gridDim.x, k-block it % nk.
     if (warp >= 8) {
         // ---------------------------------------------------------------- A dequantisers
-        // group g (warps 8-11 or 12-15) fills the stages it with it % 2 == g. Each thread keeps
-        // the codes of its next two stages in flight in a 3-deep register ring.
+        // group g (warps 8-11 or 12-15) fills the stages it with it % 2 == g. Each thread streams
+        // its own codes, scale and bias words with cp.async into a private RING-deep slot ring
+        // (layout [slot][field][thread], conflict-free), RING own stages ahead of their use.
         const int g = (warp - 8) >> 2, tid = threadIdx.x - 256 - 128 * g;  // 0..127
+        const int rt = threadIdx.x - 256;                                    // ring column 0..255
         const int total = (int)blockIdx.x < n_units ? ((n_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1) * nk : 0;
-        Fetch<BITS> ring[3];
-        auto fetch = [&](int it, Fetch<BITS> &f) {
-            f.valid = it < total;
-            if (!f.valid) return;
-            const int u = blockIdx.x + (it / nk) * gridDim.x, kb = it % nk;
-            const Tile tl = p.tiles[u / RB];
-            f.template load<MODE>(p, tl, u % RB, kb, tid);
+        constexpr int JOBS = BITS == 8 ? 2 : 1;
+        auto slot_codes = [&](int sl, int j) { return ring + (size_t)sl * 256 * kRingSlot + ((size_t)j * 256 + rt) * 16; };
+        auto slot_word = [&](int sl, int f) {  // f: 0,1 scale words of jobs 0,1; 2,3 bias words
+            return ring + (size_t)sl * 256 * kRingSlot + 2 * 256 * 16 + ((size_t)f * 256 + rt) * 4;
         };
-        fetch(g, ring[0]);
-        fetch(g + 2, ring[1]);
-        for (int it = g; it < total && ok; it += 6) {
+        int cached_tile = -1, cached_expert = 0;
+        bool cached_shared = false;
+        uint32_t parity = 0;  // bit (slot*2 + job): the group's bf16 is the high half of its copied word
+        auto issue = [&](int it, int sl) {
+            if (it < total) {
+                const int u = blockIdx.x + (it / nk) * gridDim.x, kb = it % nk, rb = u % RB;
+                if (u / RB != cached_tile) {
+                    cached_tile = u / RB;
+                    const int seg = p.tiles[cached_tile].seg;
+                    cached_shared = seg >= p.E;
+                    cached_expert = cached_shared ? 0 : seg;
+                }
 #pragma unroll
-            for (int r = 0; r < 3; ++r) {
-                const int cur = it + 2 * r;
-                if (cur >= total || !ok) break;
-                fetch(cur + 4, ring[(r + 2) % 3]);
-                const int s = cur % STAGES;
-                const uint32_t ph = (cur / STAGES) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeout)) { ok = false; break; }
-                ring[r].template store<MODE>(a_tile(s), tid);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[s]);
+                for (int j = 0; j < JOBS; ++j) {
+                    const int job = j * 128 + tid;
+                    const int m = BITS == 8 ? (job >> 1) : job, part = BITS == 8 ? (job & 1) : 0;
+                    int mat, row;
+                    a_row<MODE>(m, rb, mat, row);
+                    const QView W = mat ? (cached_shared ? p.s2 : p.w2) : (cached_shared ? p.s1 : p.w1);
+                    const size_t ridx = (size_t)cached_expert * W.rows + min(row, p.rows - 1);
+                    const uint32_t *src = W.packed + ridx * W.words_per_row();
+                    if constexpr (BITS == 8) {
+                        cp_async_16(slot_codes(sl, j), src + kb * 8 + part * 4, true);
+                    } else {
+                        // words 0-3 in this thread's first 16-byte field, word 4 in its second
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) cp_async_4(slot_codes(sl, 0) + 4 * w, src + kb * 5 + w);
+                        cp_async_4(slot_codes(sl, 1), src + kb * 5 + 4);
+                    }
+                    const size_t gi = ridx * W.groups_per_row() + (kb >> 1);
+                    cp_async_4(slot_word(sl, j), W.scales + (gi & ~(size_t)1));
+                    cp_async_4(slot_word(sl, 2 + j), W.biases + (gi & ~(size_t)1));
+                    const uint32_t bit = 1u << (sl * 2 + j);
+                    parity = (gi & 1) ? (parity | bit) : (parity & ~bit);
+                }
             }
+            cp_async_commit();  // one group per own stage, empty at the end of the sequence
+        };
+        // prologue: own stages 0 .. RING-1
+#pragma unroll
+        for (int k = 0; k < RING; ++k) issue(g + 2 * k, k);
+        for (int k = 0;; ++k) {
+            const int cur = g + 2 * k;
+            if (cur >= total || !ok) break;
+            const int sl = k % RING;
+            cp_async_wait<RING - 1>();  // own stage k has landed in slot sl
+            Fetch<BITS> f;
+            {
+                const int u = blockIdx.x + (cur / nk) * gridDim.x, rb = u % RB;
+#pragma unroll
+                for (int j = 0; j < JOBS; ++j) {
+                    const int job = j * 128 + tid;
+                    const int m = BITS == 8 ? (job >> 1) : job;
+                    int mat, row;
+                    a_row<MODE>(m, rb, mat, row);
+                    f.live[j] = row < p.rows;
+                    if constexpr (BITS == 8) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(slot_codes(sl, j));
+                        f.q[j][0] = v.x; f.q[j][1] = v.y; f.q[j][2] = v.z; f.q[j][3] = v.w;
+                    } else {
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) f.q[j][w] = *reinterpret_cast<const uint32_t *>(slot_codes(sl, 0) + 4 * w);
+                        f.q[j][4] = *reinterpret_cast<const uint32_t *>(slot_codes(sl, 1));
+                    }
+                    // the group's bf16 sits in the low or high half of the copied word
+                    const uint32_t odd = (parity >> (sl * 2 + j)) & 1u;
+                    const uint32_t sw = *reinterpret_cast<const uint32_t *>(slot_word(sl, j));
+                    const uint32_t bw = *reinterpret_cast<const uint32_t *>(slot_word(sl, 2 + j));
+                    f.s[j] = bf16_bits_to_f32(odd ? (sw >> 16) : (sw & 0xffffu));
+                    f.b[j] = bf16_bits_to_f32(odd ? (bw >> 16) : (bw & 0xffffu));
+                }
+            }
+            issue(cur + 2 * RING, sl);  // the slot is free again: fetch own stage k + RING into it
+            const int s = cur % STAGES;
+            const uint32_t ph = (cur / STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeout)) { ok = false; break; }
+            f.template store<MODE>(a_tile(s), tid);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[s]);
         }
+        cp_async_wait<0>();
     } else if (warp >= 5) {
         // ---------------------------------------------------------------- B loaders
         // loader warp w owns the 8-row groups g with g % 3 == w: it alone writes and reads
         // their table entries, so only __syncwarp is needed. Per group, lane l copies 16-byte
         // chunk l % 4 of row 8g + l / 4.
         const int w = warp - 5;
-        int it = 0, done = 0;  // stages issued / stages published
+        int it = 0;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const Tile tl = p.tiles[u / RB];
             const bool shared = tl.seg >= p.E;
@@ -326,22 +393,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
                     const int n = g8 * 8 + (lane >> 2), ch = lane & 3;
                     cp_async_16(bt + sw64_offset(n, ch), base + (size_t)tok_table[n] * p.K + ch * 8, n < tl.n);
                 }
-                cp_async_commit();
-                // keep LOAD_DEPTH stages in flight; publish the oldest once its copies landed
-                if (it - done >= LOAD_DEPTH) {
-                    cp_async_wait<LOAD_DEPTH>();
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&full[done % STAGES]);
-                    ++done;
-                }
+                // the stage is published when this thread's copies land (no wait here)
+                cp_async_arrive_noinc(&full[s]);
             }
         }
         cp_async_wait<0>();
-        fence_proxy_async_smem();
-        __syncwarp();
-        for (; done < it && ok; ++done)
-            if (lane == 0) mbar_arrive(&full[done % STAGES]);
     } else if (warp == 4) {
         // ---------------------------------------------------------------- MMA issue
         if (lane == 0) {
@@ -402,18 +458,41 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
             if (!ok) break;
             tc_fence_after();
             const int first = (mask == 2) ? 1 : 0;
+            auto col_of = [&](int c) -> uint32_t { return (c < 256) ? first * 256 + c : 256 + (c - 256); };
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+            // software pipeline: the TMEM columns (and, for down, the output rows) of chunk c + 16
+            // are requested while chunk c is processed
+            float v[16], vn[16];
+            int rid = 0, rid_next = 0;  // DOWN: output row of token (c + lane) for lanes < 16
+            auto route_of = [&](int c) -> int {
+                const int n = c + (lane & 15);
+                if (n >= tl.n) return 0;
+                const int pos = tl.p0 + n;
+                return shared ? -1 - (pos - p.shared_pos0) : p.perm_route[pos];
+            };
+            tmem_ld16(lane_base + col_of(0), vn);
+            if constexpr (MODE == MODE_DOWN) rid_next = route_of(0);
             for (int c = 0; c < N; c += 16) {
-                const uint32_t col = (c < 256) ? first * 256 + c : 256 + (c - 256);
-                float v[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + col, v);
                 tc_wait_ld();
-                if constexpr (MODE == MODE_GATE_UP) {
-                    // lanes 0-15: gate of intermediate rb*64 + 16q + lane; lanes 16-31: its up
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float up = __shfl_down_sync(kFull, v[j], 16);
-                        if (lane < 16)
-                            reinterpret_cast<uint16_t *>(so)[j * 16 + lane] = f32_to_bf16_bits(v[j] / (1.0f + __expf(-v[j])) * up);
+                for (int j = 0; j < 16; ++j) v[j] = vn[j];
+                rid = rid_next;
+                if (c + 16 < N) {
+                    tmem_ld16(lane_base + col_of(c + 16), vn);
+                    if constexpr (MODE == MODE_DOWN) rid_next = route_of(c + 16);
+                }
+                if constexpr (MODE == MODE_GATE_UP) {
+                    // lanes 0-15 hold the gate rows of intermediates rb*64 + 16q + (lane & 15), lanes
+                    // 16-31 their up rows; branch-free: lanes 0-15 finish tokens 0-7 of the chunk,
+                    // lanes 16-31 tokens 8-15
+                    const bool lo = lane < 16;
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const float a = v[jj], b = v[jj + 8];
+                        const float oa = __shfl_xor_sync(kFull, a, 16), ob = __shfl_xor_sync(kFull, b, 16);
+                        const float gt = lo ? a : ob, up = lo ? oa : b;
+                        const float act = __fdividef(gt, 1.0f + __expf(-gt)) * up;
+                        reinterpret_cast<uint16_t *>(so)[(jj + (lo ? 0 : 8)) * 16 + (lane & 15)] = f32_to_bf16_bits(act);
                     }
                     __syncwarp();
                     // 16 tokens x 16 intermediates (32 bytes): lane -> (token lane/2, half lane%2)
@@ -434,11 +513,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
                     for (int h = 0; h < 2; ++h) {
                         const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
                         const int d = rb * 128 + 32 * q + part * 8;
+                        const int r = __shfl_sync(kFull, rid, tk);
                         if (n < tl.n && d < p.rows) {
                             const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 64 + part * 16);
-                            const int pos = tl.p0 + n;
-                            uint16_t *dst = shared ? p.out_shared + (size_t)(pos - p.shared_pos0) * p.rows
-                                                   : p.out + (size_t)p.perm_route[pos] * p.rows;
+                            uint16_t *dst = r >= 0 ? p.out + (size_t)r * p.rows : p.out_shared + (size_t)(-1 - r) * p.rows;
                             *reinterpret_cast<uint4 *>(dst + d) = val;
                         }
                     }
