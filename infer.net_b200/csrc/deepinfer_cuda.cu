@@ -1,6 +1,8 @@
 // deepinfer_cuda: C ABI of the B200 MoE block backend (see include/deepinfer_cuda.h).
 #include "../../include/deepinfer_cuda.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -233,6 +235,90 @@ void configure_kernels() {
     kernels_configured = true;
 }
 
+// ------------------------------------------------------------------------ tensor maps
+
+// The driver's tensor-map encoder, resolved once through the runtime (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) throw CudaFail{"cuTensorMapEncodeTiled is not available from the driver"};
+    return fn;
+}
+
+// Row-major 2-D map: dim0 contiguous elements, dim1 rows `stride` bytes apart, box b0 x b1.
+void encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t dim0, uint64_t dim1,
+               uint64_t stride, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
+    const cuuint64_t dims[2] = {dim0, dim1};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(m, dt, 2, const_cast<void *>(base), dims, strides, box, es,
+                                            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw CudaFail{"cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")"};
+}
+
+// Grouped-GEMM geometry limits beyond the layer's own: at most 32 scale groups per row (the
+// per-unit scale buffer) and 16-byte rows of 5-bit codes for the tensor copies.
+const char *grouped_geometry_error(const Layer *L) {
+    if (L->D > 2048 || L->I > 2048) return "The grouped path supports hidden and intermediate sizes up to 2048.";
+    if (L->bits == 5 && L->I % 128 != 0) return "The 5-bit grouped path needs an intermediate size divisible by 128.";
+    return nullptr;
+}
+
+// Launch parameters of one grouped GEMM. mode GATE_UP: w = {gate, up, shared gate, shared
+// up}, src = the permuted routed rows xp [src_rows, K], shared_src = x [shared_rows, K];
+// DOWN: w = {down, down, shared down, shared down}, src = act [src_rows, K].
+gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QView &s0, const QView &s1,
+                          const uint16_t *src, int src_rows, const uint16_t *shared_src, int shared_rows,
+                          const int32_t *perm, const Tile *tiles,
+                          const int32_t *n_tiles, int shared_pos0, int shared_src0, int K, int rows, int E,
+                          uint16_t *out, uint16_t *out_shared, uint32_t *err) {
+    gg::Params p;
+    std::memset(&p, 0, sizeof(p));
+    const QView ws[4] = {w0, w1, s0, s1};
+    const uint32_t rpu = mode == gg::MODE_GATE_UP ? gg::rows_per_unit<gg::MODE_GATE_UP>()
+                                                  : gg::rows_per_unit<gg::MODE_DOWN>();
+    for (int i = 0; i < 4; ++i) {
+        p.w[i] = ws[i];
+        const uint64_t row_bytes = (uint64_t)ws[i].cols * ws[i].bits / 8;
+        encode_2d(&p.code[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, ws[i].packed, row_bytes,
+                  (uint64_t)ws[i].experts * ws[i].rows, row_bytes, 32, rpu, CU_TENSOR_MAP_SWIZZLE_32B);
+    }
+    for (int i = 0; i < gg::kBoxes; ++i) {
+        encode_2d(&p.bmap[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, src, (uint64_t)K, (uint64_t)std::max(src_rows, 1),
+                  (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (shared_src)
+            encode_2d(&p.smap[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, shared_src, (uint64_t)K,
+                      (uint64_t)std::max(shared_rows, 1), (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_64B);
+    }
+    p.perm_route = perm;
+    p.tiles = tiles;
+    p.n_tiles = n_tiles;
+    p.shared_pos0 = shared_pos0;
+    p.shared_src0 = shared_src0;
+    p.K = K;
+    p.rows = rows;
+    p.E = E;
+    p.out = out;
+    p.out_shared = out_shared;
+    p.err = err;
+    return p;
+}
+
+template <int MODE>
+void launch_grouped(const gg::Params &p, int bits, int grid, cudaStream_t st) {
+    if (bits == 8) gg::grouped_gemm_kernel<MODE, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+    else gg::grouped_gemm_kernel<MODE, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+}
+
 // ------------------------------------------------------------------------ the block
 
 struct BlockBuffers {
@@ -240,7 +326,7 @@ struct BlockBuffers {
     float *logits, *probs, *gate;
     int32_t *ids, *block_counts, *block_base, *seg_count, *seg_off, *n_tiles, *perm;
     Tile *tiles;
-    uint16_t *act, *yr, *ys;
+    uint16_t *act, *yr, *ys, *xp;
     float *act32;
     uint32_t *counter;  // last-CTA ticket of decode_route_kernel (kept at zero between launches)
     int nblocks, max_tiles;
@@ -266,6 +352,7 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     size_t o_a = gemv ? 0 : cv.take<uint16_t>((size_t)T * 9 * I);
     size_t o_yr = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
     size_t o_ys = gemv ? 0 : cv.take<uint16_t>((size_t)T * D);
+    size_t o_xp = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
     size_t o_a32 = gemv ? cv.take<float>((size_t)T * 9 * I) : 0;
     size_t o_ctr = cv.take<uint32_t>(1);
     size_t need = cv.off + 256;
@@ -286,6 +373,7 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     b.act = gemv ? nullptr : at<uint16_t>(c, o_a);
     b.yr = gemv ? nullptr : at<uint16_t>(c, o_yr);
     b.ys = gemv ? nullptr : at<uint16_t>(c, o_ys);
+    b.xp = gemv ? nullptr : at<uint16_t>(c, o_xp);
     b.act32 = gemv ? at<float>(c, o_a32) : nullptr;
     b.counter = at<uint32_t>(c, o_ctr);
     return need;
@@ -389,22 +477,15 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_GATE_UP);
     // 5. grouped gate/up + SwiGLU (routed experts and the shared expert)
     const int grid = c->sms;
-    {
-        gg::Params p{G, U, SG, SU, x, b.perm, b.tiles, b.n_tiles, 8 * T, 0, D, I, E, b.act, nullptr, c->d_err};
-        if (L->bits == 8)
-            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-        else
-            gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-    }
+    permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(x, b.perm, b.seg_off + E, D, b.xp);
+    launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, G, U, SG, SU, b.xp, 8 * T, x, T, b.perm,
+                                                    b.tiles, b.n_tiles, 8 * T, 0, D, I, E, b.act, nullptr, c->d_err),
+                                     L->bits, grid, st);
     if (profile) stage_mark(c, S_DOWN);
     // 6. grouped down -> expert rows in route order, shared rows
-    {
-        gg::Params p{Dn, Dn, SD, SD, b.act, b.perm, b.tiles, b.n_tiles, 8 * T, 0, I, D, E, b.yr, b.ys, c->d_err};
-        if (L->bits == 8)
-            gg::grouped_gemm_kernel<gg::MODE_DOWN, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-        else
-            gg::grouped_gemm_kernel<gg::MODE_DOWN, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-    }
+    launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dn, Dn, SD, SD, b.act, 9 * T, nullptr, 0, b.perm,
+                                                 b.tiles, b.n_tiles, 8 * T, 0, I, D, E, b.yr, b.ys, c->d_err),
+                                  L->bits, grid, st);
     if (profile) stage_mark(c, S_COMBINE);
     // 7. combine
     {
@@ -962,6 +1043,11 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
         set_error(error, capacity, "Decode path supports T*D <= %d; use the grouped path", kDecodeSmemMax / 2);
         return -1;
     }
+    if (!gemv)
+        if (const char *why = grouped_geometry_error(L)) {
+            set_error(error, capacity, "%s", why);
+            return -1;
+        }
     DeviceGuard dg(c->device);
     try {
         for (int i = 0; i < 8; ++i) sync_matrix(L->m[i]);
@@ -1062,6 +1148,12 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
         set_error(error, capacity, "Decode path supports T*D <= %d; use the grouped path", kDecodeSmemMax / 2);
         return -1;
     }
+    if (!gemv)
+        for (int l = 0; l < n_layers; ++l)
+            if (const char *why = grouped_geometry_error(static_cast<Layer *>(layers[l]))) {
+                set_error(error, capacity, "%s", why);
+                return -1;
+            }
     DeviceGuard dg(c->device);
     try {
         const size_t need_events = profile ? (size_t)n_layers * (S_N + 2) : 0;
@@ -1442,6 +1534,10 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                 set_error(error, capacity, "MoE layer matrix was destroyed");
                 return -1;
             }
+        if (const char *why = grouped_geometry_error(L)) {
+            set_error(error, capacity, "%s", why);
+            return -1;
+        }
     }
     const bool dev_io = flags & DI_MOE_DEVICE_IO;
     const NcclApi *nc = nccl_api(nullptr);
@@ -1480,12 +1576,13 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         const size_t o_pm = cv.take<int32_t>((size_t)Rmax * 8 + 8), o_act = cv.take<uint16_t>(((size_t)Rmax * 8 + T) * I);
         const size_t o_y = cv.take<uint16_t>((size_t)Rmax * 8 * D + 8), o_ys = cv.take<uint16_t>((size_t)T * D);
         const size_t o_z = cv.take<uint16_t>((size_t)Rmax * D + 8), o_bk = cv.take<uint16_t>((size_t)Smax * D);
+        const size_t o_xp = cv.take<uint16_t>((size_t)Rmax * 8 * D + 8);
         ensure_workspace(c, cv.off + 256);
         float *dx = dev_io ? x : at<float>(c, o_x);
         const float *dn = dev_io ? norms : at<float>(c, o_n);
         uint16_t *h = at<uint16_t>(c, o_h), *sx = at<uint16_t>(c, o_sx), *rx = at<uint16_t>(c, o_rx);
         uint16_t *act = at<uint16_t>(c, o_act), *y = at<uint16_t>(c, o_y), *ys = at<uint16_t>(c, o_ys);
-        uint16_t *z = at<uint16_t>(c, o_z), *bk = at<uint16_t>(c, o_bk);
+        uint16_t *z = at<uint16_t>(c, o_z), *bk = at<uint16_t>(c, o_bk), *xp = at<uint16_t>(c, o_xp);
         float *logits = at<float>(c, o_lg), *probs = at<float>(c, o_p), *gate = at<float>(c, o_g);
         int32_t *ids = at<int32_t>(c, o_ids), *bc = at<int32_t>(c, o_bc), *sidx = at<int32_t>(c, o_sidx);
         int32_t *sc = at<int32_t>(c, o_sc), *so = at<int32_t>(c, o_so), *all = at<int32_t>(c, o_all);
@@ -1548,16 +1645,14 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, Rn, T, gg::BN, rbb, sgc, sgo, tiles, nt,
                                                   max_tiles, c->d_err);
             if (Rn > 0) scatter_routes_kernel<<<nbr, 32, 0, st>>>(il, Rn, El + 1, rbb, sgo, perm);
-            {
-                gg::Params p{Gm, U, SG, SU, rx, perm, tiles, nt, 8 * Rn, Rn, D, I, El + 1, act, nullptr, c->d_err};
-                if (L->bits == 8) gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-                else gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-            }
-            {
-                gg::Params p{Dm, Dm, SD, SD, act, perm, tiles, nt, 8 * Rn, 0, I, D, El + 1, y, ys, c->d_err};
-                if (L->bits == 8) gg::grouped_gemm_kernel<gg::MODE_DOWN, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-                else gg::grouped_gemm_kernel<gg::MODE_DOWN, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-            }
+            if (Rn > 0) permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(rx, perm, sgo + El, D, xp);
+            launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, Gm, U, SG, SU, xp, 8 * Rn, rx, Rn + T,
+                                                            perm, tiles, nt, 8 * Rn, Rn, D, I, El + 1, act, nullptr,
+                                                            c->d_err),
+                                             L->bits, grid, st);
+            launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dm, Dm, SD, SD, act, 8 * Rn + T, nullptr, 0,
+                                                         perm, tiles, nt, 8 * Rn, 0, I, D, El + 1, y, ys, c->d_err),
+                                          L->bits, grid, st);
             // 5. partial row sums back to the token owners, then the owner's combine
             if (Rn > 0) {
                 const size_t n = (size_t)Rn * (D / 8);

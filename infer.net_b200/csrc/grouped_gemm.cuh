@@ -9,17 +9,28 @@
 //   MODE_GATE_UP: the 128 A rows of a unit interleave 16 gate rows and the 16 up rows of the
 //                 same intermediate indices in every 32-lane TMEM quadrant, so the SwiGLU
 //                 epilogue pairs them with one warp shuffle; a unit covers 64 intermediate
-//                 indices and up to 512 tokens (two 256-column accumulators), so at 8K tokens
-//                 every expert's weights are dequantised once. act = silu(gate) * up -> bf16
-//                 act[p, i] (quantized.mm:148-189; prefill_moe.mm:23-53 semantics)
+//                 indices and up to 256 tokens. act = silu(gate) * up -> bf16 act[p, i]
+//                 (quantized.mm:148-189; prefill_moe.mm:23-53 semantics)
 //   MODE_DOWN:    128 rows of the down matrix; the epilogue writes each bf16 expert row to its
 //                 route slot y[r, d] (r = t*8 + slot) or the shared row ys[t, d]
 //                 (prefill_moe.mm:54-78 semantics)
 //
+// Data movement is asynchronous and issued by one producer warp: per pipeline stage a tensor
+// copy of the stage's code bytes (32 K-columns of every A row) and the stage's B rows, which
+// are contiguous for every unit (gate/up reads the token rows already permuted into expert
+// order, down the activation rows), as at most five boxes of 16 << i rows issued by as many
+// lanes at once; per unit one bulk copy each of the scales and biases of the unit's rows.
+// (Row gathers at 64-byte granularity -- cp.async or tile::gather4 -- run at a fraction of the
+// L2 bandwidth that large tiled boxes reach, and gate/up re-reads its B rows once per block
+// of 64 intermediates.) The dequantiser warps only read shared memory, convert and write the
+// swizzled bf16 A tile.
+//
 // Warp roles (512 threads): 0-3 epilogue (one TMEM lane quadrant each), 4 MMA issue + TMEM
-// owner, 5-7 B loaders (cp.async), 8-15 A dequantisers in two groups of 4 warps that take
-// alternate pipeline stages.
+// owner, 5 producer, 6-7 idle, 8-15 A dequantisers in two groups of 4 warps that take
+// alternate pairs of pipeline stages (one quantisation group of 64 codes per pair).
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 #include "route.cuh"
 
@@ -29,27 +40,28 @@ namespace gg {
 constexpr int MODE_GATE_UP = 0, MODE_DOWN = 1;
 constexpr int BM = 128;          // A rows per unit (one MMA M)
 constexpr int BN = 256;          // max tokens per unit (one 256-column accumulator slot)
-constexpr int BK = 32;           // K per pipeline stage: 64-byte rows
-constexpr int STAGES = 7;
-constexpr int RING = 4;         // dequantiser code ring: own stages in flight per thread
-constexpr int kRingSlot = 48;   // bytes per thread per slot: 32 code bytes + 2 scale words + 2 bias words
+constexpr int BK = 32;           // K per pipeline stage: 64-byte bf16 rows, 32 code columns
+constexpr int STAGES = 6;
 constexpr int THREADS = 512;
-constexpr int kA = BM * 64;      // bytes of one A stage tile
-constexpr int kB = BN * 64;      // bytes of one B stage tile
-constexpr int STAGE_BYTES = kA + kB;
-constexpr int kTable = BN * 4;   // token row table of the B loaders
+constexpr int kA = BM * 64;      // bytes of one A stage tile (bf16)
+constexpr int kB = BN * 64;      // bytes of one B stage tile (bf16)
+constexpr int kCode = BM * 32;   // bytes of one stage's code window (32 bytes per A row)
+constexpr int STAGE_BYTES = kA + kB + kCode;
+constexpr int kScaleBuf = 16384; // scales + biases of one unit's rows (<= 32 groups per row)
 constexpr int kStageOut = 4 * 16 * 64;  // epilogue staging: 4 warps x 16 tokens x 64 bytes
-constexpr int kRing = 256 * RING * kRingSlot;
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + kTable + kStageOut + kRing + 256;
+constexpr int kBoxes = 5;               // down B boxes of 16 << i rows, i < kBoxes
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 2 * kScaleBuf + kStageOut + 512;
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int MODE>
 __host__ __device__ constexpr int rows_per_unit() { return MODE == MODE_GATE_UP ? 64 : 128; }
 
+// Tensor maps: index = matrix (0 gate / down, 1 up) + 2 * shared-expert.
 struct Params {
-    QView w1, w2;              // routed experts: gate, up (GATE_UP) or down (DOWN)
-    QView s1, s2;              // shared expert:  gate, up (GATE_UP) or down (DOWN)
-    const uint16_t *src;       // GATE_UP: x [T, K]; DOWN: act [P, K]
+    CUtensorMap code[4];       // uint8 [experts*rows, row bytes], box 32 bytes x rows_per_unit, 32B swizzle
+    CUtensorMap bmap[kBoxes];  // B rows by position: GATE_UP xp [8T, K], DOWN act [P, K]; box 32 x (16 << i)
+    CUtensorMap smap[kBoxes];  // GATE_UP shared-expert B rows: x [rows, K]; same boxes
+    QView w[4];                // the same matrices: scales / biases (bulk copies), geometry
     const int32_t *perm_route; // [8T] route id of each permuted position
     const Tile *tiles;
     const int32_t *n_tiles;
@@ -67,6 +79,11 @@ __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
 // (address bits [7,9) XOR-ed into bits [4,6)).
 __device__ __forceinline__ uint32_t sw64_offset(uint32_t r, uint32_t c) {
     return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4);
+}
+// Byte offset of 16-byte chunk c (0..1) of row r in a 32B-swizzled tile of 32-byte rows
+// (address bit 7 XOR-ed into bit 4).
+__device__ __forceinline__ uint32_t sw32_offset(uint32_t r, uint32_t c) {
+    return r * 32u + ((c ^ ((r >> 2) & 1u)) << 4);
 }
 
 // Shared-memory descriptor: K-major, 64-byte swizzle, 8-row atoms 512 bytes apart.
@@ -125,130 +142,74 @@ __device__ __forceinline__ void dequant32_5bit(const uint32_t *w, float s, float
     }
 }
 
-// A-tile row m of a unit -> weight row. GATE_UP: in quadrant q = m/32, lanes 0-15 are gate rows
-// and lanes 16-31 the up rows of intermediates rb*64 + 16q + (m & 15).
+// A-tile row m of a unit -> (matrix, row within the unit's block of that matrix). GATE_UP: in
+// quadrant q = m/32, lanes 0-15 are gate rows and lanes 16-31 the up rows of intermediates
+// rb*64 + 16q + (m & 15).
 template <int MODE>
-__device__ __forceinline__ void a_row(int m, int rb, int &mat, int &row) {
+__device__ __forceinline__ void a_row(int m, int &mat, int &r) {
     if constexpr (MODE == MODE_GATE_UP) {
         mat = (m >> 4) & 1;
-        row = rb * 64 + (m >> 5) * 16 + (m & 15);
+        r = (m >> 5) * 16 + (m & 15);
     } else {
         mat = 0;
-        row = rb * 128 + m;
+        r = m;
     }
 }
 
-// Accumulator slots: a unit with N <= 256 takes one 256-column slot (alternating), a larger
-// unit takes both. Every role derives the same assignment from the unit sequence.
+// Byte offset of the stage's code window for K-block kb: 8-bit rows hold 32 code bytes per
+// block (aligned); 5-bit blocks are 20 bytes, fetched as the 16-byte-aligned 32-byte window
+// that contains them (the tensor copy's x coordinate must be 16-byte aligned).
+template <int BITS>
+__device__ __forceinline__ int code_x(int kb) { return BITS == 8 ? kb * 32 : ((kb * 20) & ~15); }
+
+// Accumulator slots alternate between units; every role derives the same assignment.
 struct SlotPlan {
     int next = 0;
     uint32_t uses[2] = {0, 0};
-    // returns a bitmask of slots; phase[s] = completed fills of slot s before this unit
-    __device__ __forceinline__ int take(int N, uint32_t *phase) {
-        const int mask = N <= 256 ? (1 << next) : 3;
-        if (N <= 256) next ^= 1;
-        for (int s = 0; s < 2; ++s) {
-            phase[s] = uses[s];
-            if (mask >> s & 1) uses[s]++;
-        }
-        return mask;
-    }
-};
-
-// Codes, scale and bias of one dequantiser thread's share of one stage (2 jobs of 16 codes
-// for 8-bit, 1 job of 32 codes for 5-bit), loaded ahead of use.
-template <int BITS>
-struct Fetch {
-    static constexpr int JOBS = BITS == 8 ? 2 : 1, WORDS = BITS == 8 ? 4 : 5;
-    uint32_t q[JOBS][WORDS];
-    float s[JOBS], b[JOBS];
-    bool live[JOBS];
-    bool valid;
-
-    template <int MODE>
-    __device__ __forceinline__ void load(const Params &p, const Tile &tl, int rb, int kb, int tid) {
-        const bool shared = tl.seg >= p.E;
-        const int expert = shared ? 0 : tl.seg;
-#pragma unroll
-        for (int j = 0; j < JOBS; ++j) {
-            const int job = j * 128 + tid;
-            // 8-bit: job = (m, part), 2 parts of 16 codes per 32-wide row; 5-bit: job = m
-            const int m = BITS == 8 ? (job >> 1) : job, part = BITS == 8 ? (job & 1) : 0;
-            int mat, row;
-            a_row<MODE>(m, rb, mat, row);
-            const QView W = mat ? (shared ? p.s2 : p.w2) : (shared ? p.s1 : p.w1);
-            live[j] = row < p.rows;
-            const size_t ridx = (size_t)expert * W.rows + min(row, p.rows - 1);
-            const uint32_t *src = W.packed + ridx * W.words_per_row();
-            if constexpr (BITS == 8) {
-                const uint4 v = ldg_nc_v4(src + kb * 8 + part * 4);
-                q[j][0] = v.x; q[j][1] = v.y; q[j][2] = v.z; q[j][3] = v.w;
-            } else {
-#pragma unroll
-                for (int w = 0; w < 5; ++w) q[j][w] = ldg_nc_u32(src + kb * 5 + w);
-            }
-            s[j] = bf16_bits_to_f32(__ldg(W.scales + ridx * W.groups_per_row() + (kb >> 1)));
-            b[j] = bf16_bits_to_f32(__ldg(W.biases + ridx * W.groups_per_row() + (kb >> 1)));
-        }
-    }
-
-    template <int MODE>
-    __device__ __forceinline__ void store(uint8_t *t, int tid) const {
-#pragma unroll
-        for (int j = 0; j < JOBS; ++j) {
-            const int job = j * 128 + tid;
-            if constexpr (BITS == 8) {
-                const int m = job >> 1, part = job & 1;
-                uint32_t o[8];
-                if (live[j]) dequant16_8bit(make_uint4(q[j][0], q[j][1], q[j][2], q[j][3]), s[j], b[j], o);
-                else
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) o[i] = 0;
-                *reinterpret_cast<uint4 *>(t + sw64_offset(m, 2 * part)) = make_uint4(o[0], o[1], o[2], o[3]);
-                *reinterpret_cast<uint4 *>(t + sw64_offset(m, 2 * part + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-            } else {
-                const int m = job;
-                uint32_t o[16];
-                if (live[j]) dequant32_5bit(q[j], s[j], b[j], o);
-                else
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o[i] = 0;
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    *reinterpret_cast<uint4 *>(t + sw64_offset(m, c)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-            }
-        }
+    // returns the slot; phase = completed fills of that slot before this unit
+    __device__ __forceinline__ int take(uint32_t &phase) {
+        const int s = next;
+        next ^= 1;
+        phase = uses[s]++;
+        return s;
     }
 };
 
 template <int MODE, int BITS>
-__global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
+__global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
     uint8_t *smem = smem_raw + pad;
-    int32_t *tok_table = reinterpret_cast<int32_t *>(smem + STAGES * STAGE_BYTES);
-    uint8_t *stage_out = reinterpret_cast<uint8_t *>(tok_table + BN);
-    uint8_t *ring = stage_out + kStageOut;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kRing);
-    uint64_t *full = bars, *empty = bars + STAGES;
-    uint64_t *accf = bars + 2 * STAGES, *acce = accf + 2;
+    uint8_t *scale_buf = smem + STAGES * STAGE_BYTES;
+    uint8_t *stage_out = scale_buf + 2 * kScaleBuf;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
+    uint64_t *full = bars, *bfull = bars + STAGES, *cfull = bars + 2 * STAGES, *empty = bars + 3 * STAGES;
+    uint64_t *sfull = bars + 4 * STAGES, *sempty = sfull + 2;
+    uint64_t *accf = sempty + 2, *acce = accf + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
     auto a_tile = [&](int s) { return smem + s * STAGE_BYTES; };
     auto b_tile = [&](int s) { return smem + s * STAGE_BYTES + kA; };
+    auto c_tile = [&](int s) { return smem + s * STAGE_BYTES + kA + kB; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int RPU = rows_per_unit<MODE>();
+    constexpr int NMAT = MODE == MODE_GATE_UP ? 2 : 1;
     const int RB = (p.rows + RPU - 1) / RPU;
-    const int nk = p.K / BK;
+    const int nk = p.K / BK;  // even (K is a multiple of 64)
+    const int gpr = p.K / 64;
     const int n_units = (*p.n_tiles) * RB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 4 + 96);  // one dequant group (4 warp arrivals) + 96 loader threads' copies
-            mbar_init(&empty[s], 1);
+            mbar_init(&full[s], 4);   // the dequantiser warps of the stage's group
+            mbar_init(&bfull[s], 1);  // producer arrive + B bytes
+            mbar_init(&cfull[s], 1);  // producer arrive + code bytes
+            mbar_init(&empty[s], 1);  // MMA commit
         }
         for (int a = 0; a < 2; ++a) {
+            mbar_init(&sfull[a], 1);
+            mbar_init(&sempty[a], 8);
             mbar_init(&accf[a], 1);
             mbar_init(&acce[a], 4);
         }
@@ -258,146 +219,156 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
         tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
+    if (warp == 5 && lane == 0) {
+        for (int i = 0; i < kBoxes; ++i) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&p.bmap[i]) : "memory");
+            if constexpr (MODE == MODE_GATE_UP) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.smap[i]) : "memory");
+        }
+        for (int i = 0; i < 4; ++i) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.code[i]) : "memory");
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
 
-    // Flat pipeline index `it`: unit u = blockIdx.x + (it / nk) * gridDim.x, k-block it % nk.
+    // Flat pipeline index `it` = ul * nk + kb over this CTA's units ul (unit u = blockIdx.x +
+    // ul * gridDim.x) and K-blocks kb. Stage s = it % STAGES, phase (it / STAGES) & 1.
     if (warp >= 8) {
         // ---------------------------------------------------------------- A dequantisers
-        // group g (warps 8-11 or 12-15) fills the stages it with it % 2 == g. Each thread streams
-        // its own codes, scale and bias words with cp.async into a private RING-deep slot ring
-        // (layout [slot][field][thread], conflict-free), RING own stages ahead of their use.
-        const int g = (warp - 8) >> 2, tid = threadIdx.x - 256 - 128 * g;  // 0..127
-        const int rt = threadIdx.x - 256;                                    // ring column 0..255
-        const int total = (int)blockIdx.x < n_units ? ((n_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1) * nk : 0;
-        constexpr int JOBS = BITS == 8 ? 2 : 1;
-        auto slot_codes = [&](int sl, int j) { return ring + (size_t)sl * 256 * kRingSlot + ((size_t)j * 256 + rt) * 16; };
-        auto slot_word = [&](int sl, int f) {  // f: 0,1 scale words of jobs 0,1; 2,3 bias words
-            return ring + (size_t)sl * 256 * kRingSlot + 2 * 256 * 16 + ((size_t)f * 256 + rt) * 4;
-        };
-        int cached_tile = -1, cached_expert = 0;
-        bool cached_shared = false;
-        uint32_t parity = 0;  // bit (slot*2 + job): the group's bf16 is the high half of its copied word
-        auto issue = [&](int it, int sl) {
-            if (it < total) {
-                const int u = blockIdx.x + (it / nk) * gridDim.x, kb = it % nk, rb = u % RB;
-                if (u / RB != cached_tile) {
-                    cached_tile = u / RB;
-                    const int seg = p.tiles[cached_tile].seg;
-                    cached_shared = seg >= p.E;
-                    cached_expert = cached_shared ? 0 : seg;
+        // group g takes the stage pairs (2j, 2j+1) of the flat index with j % 2 == g; both
+        // stages of a pair use the same quantisation group. Thread m of the group converts A
+        // row m.
+        const int g = (warp - 8) >> 2, m = threadIdx.x - 256 - 128 * g;  // 0..127
+        int mat, r;
+        a_row<MODE>(m, mat, r);
+        const bool fast_scales = (gpr & 7) == 0;  // rows of scales are 16-byte aligned
+        int it0 = 0;                              // flat index of the unit's first stage
+        for (int ul = 0, u = blockIdx.x; u < n_units && ok; ++ul, u += gridDim.x, it0 += nk) {
+            const int rb = u % RB, sb = ul & 1;
+            const bool live = rb * RPU + r < p.rows;
+            if (!mbar_wait(&sfull[sb], (ul >> 1) & 1, p.err, kErrTimeout)) { ok = false; break; }
+            const uint16_t *s_row =
+                reinterpret_cast<const uint16_t *>(scale_buf + sb * kScaleBuf) + ((mat * 2) * RPU + r) * gpr;
+            const uint16_t *b_row = s_row + RPU * gpr;
+            uint4 swin = make_uint4(0, 0, 0, 0), bwin = swin;
+            int win = -1;
+            // first own pair of this unit: pairs j = (it0 + kb) / 2 with j % 2 == g
+            for (int kb = 2 * ((g - (it0 >> 1)) & 1); kb < nk && ok; kb += 4) {
+                const int gi = kb >> 1;
+                float sc, bi;
+                if (fast_scales) {
+                    if ((gi >> 3) != win) {
+                        win = gi >> 3;
+                        swin = *reinterpret_cast<const uint4 *>(s_row + 8 * win);
+                        bwin = *reinterpret_cast<const uint4 *>(b_row + 8 * win);
+                    }
+                    const int e = gi & 7;
+                    const uint32_t sw = e < 2 ? swin.x : e < 4 ? swin.y : e < 6 ? swin.z : swin.w;
+                    const uint32_t bw = e < 2 ? bwin.x : e < 4 ? bwin.y : e < 6 ? bwin.z : bwin.w;
+                    sc = (e & 1) ? bf16_hi(sw) : bf16_lo(sw);
+                    bi = (e & 1) ? bf16_hi(bw) : bf16_lo(bw);
+                } else {
+                    sc = bf16_bits_to_f32(s_row[gi]);
+                    bi = bf16_bits_to_f32(b_row[gi]);
                 }
 #pragma unroll
-                for (int j = 0; j < JOBS; ++j) {
-                    const int job = j * 128 + tid;
-                    const int m = BITS == 8 ? (job >> 1) : job, part = BITS == 8 ? (job & 1) : 0;
-                    int mat, row;
-                    a_row<MODE>(m, rb, mat, row);
-                    const QView W = mat ? (cached_shared ? p.s2 : p.w2) : (cached_shared ? p.s1 : p.w1);
-                    const size_t ridx = (size_t)cached_expert * W.rows + min(row, p.rows - 1);
-                    const uint32_t *src = W.packed + ridx * W.words_per_row();
+                for (int h = 0; h < 2; ++h) {
+                    const int it = it0 + kb + h, s = it % STAGES;
+                    if (!mbar_wait(&cfull[s], (it / STAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
+                    const uint8_t *crow = c_tile(s) + mat * (RPU * 32);
+                    const uint4 c0 = *reinterpret_cast<const uint4 *>(crow + sw32_offset(r, 0));
+                    const uint4 c1 = *reinterpret_cast<const uint4 *>(crow + sw32_offset(r, 1));
+                    uint32_t o[16];
                     if constexpr (BITS == 8) {
-                        cp_async_16(slot_codes(sl, j), src + kb * 8 + part * 4, true);
+                        dequant16_8bit(c0, sc, bi, o);
+                        dequant16_8bit(c1, sc, bi, o + 8);
                     } else {
-                        // words 0-3 in this thread's first 16-byte field, word 4 in its second
+                        const uint32_t win8[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                        const int off = (((kb + h) * 20) & 15) >> 2;  // word offset of the block
+                        uint32_t w5[5];
 #pragma unroll
-                        for (int w = 0; w < 4; ++w) cp_async_4(slot_codes(sl, 0) + 4 * w, src + kb * 5 + w);
-                        cp_async_4(slot_codes(sl, 1), src + kb * 5 + 4);
+                        for (int i = 0; i < 5; ++i)
+                            w5[i] = off == 0 ? win8[i] : off == 1 ? win8[i + 1] : off == 2 ? win8[i + 2] : win8[i + 3];
+                        dequant32_5bit(w5, sc, bi, o);
                     }
-                    const size_t gi = ridx * W.groups_per_row() + (kb >> 1);
-                    cp_async_4(slot_word(sl, j), W.scales + (gi & ~(size_t)1));
-                    cp_async_4(slot_word(sl, 2 + j), W.biases + (gi & ~(size_t)1));
-                    const uint32_t bit = 1u << (sl * 2 + j);
-                    parity = (gi & 1) ? (parity | bit) : (parity & ~bit);
+                    if (!live)
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) o[i] = 0;
+                    uint8_t *t = a_tile(s);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4 *>(t + sw64_offset(m, c)) =
+                            make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[s]);
                 }
             }
-            cp_async_commit();  // one group per own stage, empty at the end of the sequence
-        };
-        // prologue: own stages 0 .. RING-1
-#pragma unroll
-        for (int k = 0; k < RING; ++k) issue(g + 2 * k, k);
-        for (int k = 0;; ++k) {
-            const int cur = g + 2 * k;
-            if (cur >= total || !ok) break;
-            const int sl = k % RING;
-            cp_async_wait<RING - 1>();  // own stage k has landed in slot sl
-            Fetch<BITS> f;
-            {
-                const int u = blockIdx.x + (cur / nk) * gridDim.x, rb = u % RB;
-#pragma unroll
-                for (int j = 0; j < JOBS; ++j) {
-                    const int job = j * 128 + tid;
-                    const int m = BITS == 8 ? (job >> 1) : job;
-                    int mat, row;
-                    a_row<MODE>(m, rb, mat, row);
-                    f.live[j] = row < p.rows;
-                    if constexpr (BITS == 8) {
-                        const uint4 v = *reinterpret_cast<const uint4 *>(slot_codes(sl, j));
-                        f.q[j][0] = v.x; f.q[j][1] = v.y; f.q[j][2] = v.z; f.q[j][3] = v.w;
-                    } else {
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) f.q[j][w] = *reinterpret_cast<const uint32_t *>(slot_codes(sl, 0) + 4 * w);
-                        f.q[j][4] = *reinterpret_cast<const uint32_t *>(slot_codes(sl, 1));
-                    }
-                    // the group's bf16 sits in the low or high half of the copied word
-                    const uint32_t odd = (parity >> (sl * 2 + j)) & 1u;
-                    const uint32_t sw = *reinterpret_cast<const uint32_t *>(slot_word(sl, j));
-                    const uint32_t bw = *reinterpret_cast<const uint32_t *>(slot_word(sl, 2 + j));
-                    f.s[j] = bf16_bits_to_f32(odd ? (sw >> 16) : (sw & 0xffffu));
-                    f.b[j] = bf16_bits_to_f32(odd ? (bw >> 16) : (bw & 0xffffu));
-                }
-            }
-            issue(cur + 2 * RING, sl);  // the slot is free again: fetch own stage k + RING into it
-            const int s = cur % STAGES;
-            const uint32_t ph = (cur / STAGES) & 1;
-            if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeout)) { ok = false; break; }
-            f.template store<MODE>(a_tile(s), tid);
-            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&full[s]);
+            if (lane == 0) mbar_arrive(&sempty[sb]);
         }
-        cp_async_wait<0>();
-    } else if (warp >= 5) {
-        // ---------------------------------------------------------------- B loaders
-        // loader warp w owns the 8-row groups g with g % 3 == w: it alone writes and reads
-        // their table entries, so only __syncwarp is needed. Per group, lane l copies 16-byte
-        // chunk l % 4 of row 8g + l / 4.
-        const int w = warp - 5;
-        int it = 0;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    } else if (warp == 5) {
+        // ---------------------------------------------------------------- producer
+        int it = 0, ul = 0;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ul) {
             const Tile tl = p.tiles[u / RB];
+            const int rb = u % RB, sb = ul & 1;
             const bool shared = tl.seg >= p.E;
+            const int expert = shared ? 0 : tl.seg;
             const int N = round16(tl.n);
-            __syncwarp();
-            for (int g8 = w; g8 < N / 8; g8 += 3) {
-                if (lane < 8) {
-                    const int n = g8 * 8 + lane;
-                    const int pos = tl.p0 + min(n, tl.n - 1);
-                    int row;
-                    if constexpr (MODE == MODE_GATE_UP) row = shared ? p.shared_src0 + (pos - p.shared_pos0) : (p.perm_route[pos] >> 3);
-                    else row = pos;
-                    tok_table[n] = row;
+            // scales and biases of the unit's rows
+            if (lane == 0) {
+                ok = mbar_wait(&sempty[sb], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeout);
+                if (ok) {
+                    const int nrows = min(RPU, p.rows - rb * RPU);
+                    const uint32_t bytes = (uint32_t)(nrows * gpr * 2);
+                    mbar_arrive_expect_tx(&sfull[sb], bytes * 2 * NMAT);
+                    for (int mt = 0; mt < NMAT; ++mt) {
+                        const QView &W = p.w[mt + 2 * shared];
+                        const size_t r0 = (size_t)expert * W.rows + rb * RPU;
+                        uint8_t *dst = scale_buf + sb * kScaleBuf + (size_t)(mt * 2) * RPU * gpr * 2;
+                        bulk_load(dst, W.scales + r0 * gpr, bytes, &sfull[sb]);
+                        bulk_load(dst + RPU * gpr * 2, W.biases + r0 * gpr, bytes, &sfull[sb]);
+                    }
                 }
             }
-            __syncwarp();
-            for (int kb = 0; kb < nk && ok; ++kb, ++it) {
+            ok = __shfl_sync(kFull, ok, 0);
+            if (!ok) break;
+            // B boxes of this unit: lane i < kBoxes copies 16 << i rows when bit i of N/16 is set,
+            // larger boxes first
+            const int nb16 = N >> 4;
+            const bool box_mine = lane < kBoxes && ((nb16 >> lane) & 1);
+            const int box_off = box_mine ? 16 * ((nb16 >> (lane + 1)) << (lane + 1)) : 0;
+            const bool shared_src = MODE == MODE_GATE_UP && shared;
+            const int row0 = (shared_src ? p.shared_src0 + (tl.p0 - p.shared_pos0) : tl.p0) + box_off;
+            const CUtensorMap *bm = shared_src ? &p.smap[box_mine ? lane : 0] : &p.bmap[box_mine ? lane : 0];
+            for (int kb = 0; kb < nk; ++kb, ++it) {
                 const int s = it % STAGES;
-                const uint32_t ph = (it / STAGES) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrTimeout)) { ok = false; break; }
-                uint8_t *bt = b_tile(s);
-                const uint16_t *base = p.src + kb * BK;
-                for (int g8 = w; g8 < N / 8; g8 += 3) {
-                    const int n = g8 * 8 + (lane >> 2), ch = lane & 3;
-                    cp_async_16(bt + sw64_offset(n, ch), base + (size_t)tok_table[n] * p.K + ch * 8, n < tl.n);
+                if (lane == 0) {
+                    ok = mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.err, kErrTimeout);
+                    if (ok) {
+                        mbar_arrive_expect_tx(&cfull[s], kCode);
+                        mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 64u);
+                    }
                 }
-                // the stage is published when this thread's copies land (no wait here)
-                cp_async_arrive_noinc(&full[s]);
+                ok = __shfl_sync(kFull, ok, 0);
+                if (!ok) break;
+                if (lane < NMAT)
+                    tma_load_2d(c_tile(s) + lane * (RPU * 32), &p.code[lane + 2 * shared], code_x<BITS>(kb),
+                                expert * p.w[lane + 2 * shared].rows + rb * RPU, &cfull[s]);
+                if (box_mine) tma_load_2d(b_tile(s) + box_off * 64, bm, kb * BK, row0, &bfull[s]);
             }
         }
-        cp_async_wait<0>();
+        if (!ok && lane == 0) {
+            // copies still in flight must land before the CTA's shared memory is released
+            for (int k = max(0, it - STAGES); k < it; ++k) {
+                const int s = k % STAGES;
+                mbar_wait(&cfull[s], (k / STAGES) & 1, p.err, kErrTimeout);
+                mbar_wait(&bfull[s], (k / STAGES) & 1, p.err, kErrTimeout);
+            }
+            for (int k = max(0, ul - 1); k <= ul; ++k) mbar_wait(&sfull[k & 1], (k >> 1) & 1, p.err, kErrTimeout);
+        }
     } else if (warp == 4) {
         // ---------------------------------------------------------------- MMA issue
         if (lane == 0) {
@@ -406,41 +377,32 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const Tile tl = p.tiles[u / RB];
                 const int N = round16(tl.n);
-                uint32_t phase[2];
-                const int mask = plan.take(N, phase);
-                for (int s2 = 0; s2 < 2 && ok; ++s2)
-                    if (mask >> s2 & 1)
-                        if (!mbar_wait(&acce[s2], (phase[s2] & 1) ^ 1, p.err, kErrTimeout)) ok = false;
-                if (!ok) break;
+                uint32_t phase;
+                const int slot = plan.take(phase);
+                if (!mbar_wait(&acce[slot], (phase & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
                 tc_fence_after();
-                // tokens [0, n0) accumulate in the first slot of the mask, [256, N) in slot 1
-                const int first = (mask == 2) ? 1 : 0;
-                const int n0 = N < 256 ? N : 256, n1 = N - n0;
-                const uint32_t d0 = tmem + first * 256, d1 = tmem + 256;
-                const uint32_t id0 = idesc_bf16_f32(BM, n0), id1 = n1 > 0 ? idesc_bf16_f32(BM, n1) : 0;
+                const uint32_t d = tmem + slot * 256;
+                const uint32_t id = idesc_bf16_f32(BM, N);
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&full[s], ph, p.err, kErrTimeout)) { ok = false; break; }
+                    if (!mbar_wait(&bfull[s], ph, p.err, kErrTimeout) || !mbar_wait(&full[s], ph, p.err, kErrTimeout)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint64_t adesc = smem_desc_sw64(smem_u32(a_tile(s)));
                     const uint64_t bdesc = smem_desc_sw64(smem_u32(b_tile(s)));
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        const uint32_t acc = (kb | k) != 0;
-                        tc_mma_bf16(d0, adesc + 2 * k, bdesc + 2 * k, id0, acc);
-                        // second accumulator: B rows from 256 on start 256 x 64 bytes further
-                        if (n1 > 0) tc_mma_bf16(d1, adesc + 2 * k, bdesc + ((256 * 64) >> 4) + 2 * k, id1, acc);
-                    }
+                    for (int k = 0; k < BK / 16; ++k) tc_mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, id, (kb | k) != 0);
                     tc_commit(&empty[s]);
                 }
                 if (!ok) break;
-                for (int s2 = 0; s2 < 2; ++s2)
-                    if (mask >> s2 & 1) tc_commit(&accf[s2]);
+                tc_commit(&accf[slot]);
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp < 4) {
         // ---------------------------------------------------------------- epilogue
         const int q = warp;  // TMEM lanes 32q .. 32q+31
         uint8_t *so = stage_out + q * 16 * 64;
@@ -450,16 +412,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
             const int rb = u % RB;
             const bool shared = tl.seg >= p.E;
             const int N = round16(tl.n);
-            uint32_t phase[2];
-            const int mask = plan.take(N, phase);
-            for (int s2 = 0; s2 < 2 && ok; ++s2)
-                if (mask >> s2 & 1)
-                    if (!mbar_wait(&accf[s2], phase[s2] & 1, p.err, kErrTimeout)) ok = false;
-            if (!ok) break;
+            uint32_t phase;
+            const int slot = plan.take(phase);
+            if (!mbar_wait(&accf[slot], phase & 1, p.err, kErrTimeout)) { ok = false; break; }
             tc_fence_after();
-            const int first = (mask == 2) ? 1 : 0;
-            auto col_of = [&](int c) -> uint32_t { return (c < 256) ? first * 256 + c : 256 + (c - 256); };
-            const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + slot * 256;
             // software pipeline: the TMEM columns (and, for down, the output rows) of chunk c + 16
             // are requested while chunk c is processed
             float v[16], vn[16];
@@ -470,7 +427,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
                 const int pos = tl.p0 + n;
                 return shared ? -1 - (pos - p.shared_pos0) : p.perm_route[pos];
             };
-            tmem_ld16(lane_base + col_of(0), vn);
+            tmem_ld16(lane_base, vn);
             if constexpr (MODE == MODE_DOWN) rid_next = route_of(0);
             for (int c = 0; c < N; c += 16) {
                 tc_wait_ld();
@@ -478,7 +435,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
                 for (int j = 0; j < 16; ++j) v[j] = vn[j];
                 rid = rid_next;
                 if (c + 16 < N) {
-                    tmem_ld16(lane_base + col_of(c + 16), vn);
+                    tmem_ld16(lane_base + c + 16, vn);
                     if constexpr (MODE == MODE_DOWN) rid_next = route_of(c + 16);
                 }
                 if constexpr (MODE == MODE_GATE_UP) {
@@ -513,10 +470,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
                     for (int h = 0; h < 2; ++h) {
                         const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
                         const int d = rb * 128 + 32 * q + part * 8;
-                        const int r = __shfl_sync(kFull, rid, tk);
+                        const int rr = __shfl_sync(kFull, rid, tk);
                         if (n < tl.n && d < p.rows) {
                             const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 64 + part * 16);
-                            uint16_t *dst = r >= 0 ? p.out + (size_t)r * p.rows : p.out_shared + (size_t)(-1 - r) * p.rows;
+                            uint16_t *dst = rr >= 0 ? p.out + (size_t)rr * p.rows : p.out_shared + (size_t)(-1 - rr) * p.rows;
                             *reinterpret_cast<uint4 *>(dst + d) = val;
                         }
                     }
@@ -525,9 +482,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(Params p) {
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0)
-                for (int s2 = 0; s2 < 2; ++s2)
-                    if (mask >> s2 & 1) mbar_arrive(&acce[s2]);
+            if (lane == 0) mbar_arrive(&acce[slot]);
         }
     }
     tc_fence_before();

@@ -411,6 +411,36 @@ scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32
     }
 }
 
+// ------------------------------------------------------------------ permuted token rows
+//
+// xp[pos] = src[perm_route[pos] / 8] for the routed positions pos < *count (expert order), so
+// the grouped gate/up GEMM reads each expert's tokens as contiguous rows. One warp per row,
+// 16 bytes per lane per step; D % 256 == 0.
+__global__ void __launch_bounds__(256)
+permute_rows_kernel(const uint16_t *__restrict__ src, const int32_t *__restrict__ perm_route,
+                    const int32_t *__restrict__ count, int D, uint16_t *__restrict__ dst) {
+    const int lane = threadIdx.x & 31;
+    const int n = *count;
+    const int chunks = D / 8;  // 16-byte chunks per row
+    for (int pos = blockIdx.x * 8 + (threadIdx.x >> 5); pos < n; pos += gridDim.x * 8) {
+        const uint4 *s = reinterpret_cast<const uint4 *>(src + (size_t)(perm_route[pos] >> 3) * D);
+        uint4 *d = reinterpret_cast<uint4 *>(dst + (size_t)pos * D);
+        for (int c0 = 0; c0 < chunks; c0 += 256) {
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = c0 + j * 32 + lane;
+                if (c < chunks) v[j] = s[c];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = c0 + j * 32 + lane;
+                if (c < chunks) d[c] = v[j];
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ combine
 //
 // out[t] = sigmoid(gate_t) * shared[t] + sum_j p[t,j] * y[8t+j]   (Qwen36Model.cs:242-244),
