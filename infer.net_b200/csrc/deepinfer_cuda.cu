@@ -290,14 +290,14 @@ gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QVie
         p.w[i] = ws[i];
         const uint64_t row_bytes = (uint64_t)ws[i].cols * ws[i].bits / 8;
         encode_2d(&p.code[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, ws[i].packed, row_bytes,
-                  (uint64_t)ws[i].experts * ws[i].rows, row_bytes, 32, rpu, CU_TENSOR_MAP_SWIZZLE_32B);
+                  (uint64_t)ws[i].experts * ws[i].rows, row_bytes, 64, rpu, CU_TENSOR_MAP_SWIZZLE_64B);
     }
     for (int i = 0; i < gg::kBoxes; ++i) {
         encode_2d(&p.bmap[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, src, (uint64_t)K, (uint64_t)std::max(src_rows, 1),
-                  (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_64B);
+                  (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_128B);
         if (shared_src)
             encode_2d(&p.smap[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, shared_src, (uint64_t)K,
-                      (uint64_t)std::max(shared_rows, 1), (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_64B);
+                      (uint64_t)std::max(shared_rows, 1), (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     p.perm_route = perm;
     p.tiles = tiles;
@@ -474,10 +474,11 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
     scatter_routes_kernel<<<b.nblocks, 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm);
+    // token rows in expert order for the gate/up B operand (timed with the scatter)
+    permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(x, b.perm, b.seg_off + E, D, b.xp);
     if (profile) stage_mark(c, S_GATE_UP);
     // 5. grouped gate/up + SwiGLU (routed experts and the shared expert)
     const int grid = c->sms;
-    permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(x, b.perm, b.seg_off + E, D, b.xp);
     launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, G, U, SG, SU, b.xp, 8 * T, x, T, b.perm,
                                                     b.tiles, b.n_tiles, 8 * T, 0, D, I, E, b.act, nullptr, c->d_err),
                                      L->bits, grid, st);

@@ -3,7 +3,7 @@
 // D[m, n] = sum_k A[m, k] * B[n, k] for every work unit (a token tile of one expert segment
 // x a block of weight rows). A is dequantised in shared memory from the affine-quantised MLX
 // codes; B rows are the tokens routed to the expert (gathered from x for gate/up, contiguous
-// activation rows for down). Both operands are K-major bf16 tiles with the 64-byte swizzle;
+// activation rows for down). Both operands are K-major bf16 tiles with the 128-byte swizzle;
 // the f32 accumulators live in tensor memory.
 //
 //   MODE_GATE_UP: the 128 A rows of a unit interleave 16 gate rows and the 16 up rows of the
@@ -15,8 +15,8 @@
 //                 route slot y[r, d] (r = t*8 + slot) or the shared row ys[t, d]
 //                 (prefill_moe.mm:54-78 semantics)
 //
-// Data movement is asynchronous and issued by one producer warp: per pipeline stage a tensor
-// copy of the stage's code bytes (32 K-columns of every A row) and the stage's B rows, which
+// Data movement is asynchronous and issued by one producer warp: per pipeline stage (64
+// K-columns, one quantisation group) a tensor copy of the stage's code bytes and B rows, which
 // are contiguous for every unit (gate/up reads the token rows already permuted into expert
 // order, down the activation rows), as at most five boxes of 16 << i rows issued by as many
 // lanes at once; per unit one bulk copy each of the scales and biases of the unit's rows.
@@ -27,7 +27,11 @@
 //
 // Warp roles (512 threads): 0-3 epilogue (one TMEM lane quadrant each), 4 MMA issue + TMEM
 // owner, 5 producer, 6-7 idle, 8-15 A dequantisers in two groups of 4 warps that take
-// alternate pairs of pipeline stages (one quantisation group of 64 codes per pair).
+// alternate pipeline stages.
+//
+// Stage size: every stage costs a fixed round trip (MMA commit -> producer -> tensor copy ->
+// dequantiser -> MMA issue, several hundred cycles on B200) and fixed issue work, so stages
+// carry 64 K-columns (four K=16 MMAs per commit) rather than 32.
 #pragma once
 #include <cuda.h>
 
@@ -40,12 +44,12 @@ namespace gg {
 constexpr int MODE_GATE_UP = 0, MODE_DOWN = 1;
 constexpr int BM = 128;          // A rows per unit (one MMA M)
 constexpr int BN = 256;          // max tokens per unit (one 256-column accumulator slot)
-constexpr int BK = 32;           // K per pipeline stage: 64-byte bf16 rows, 32 code columns
-constexpr int STAGES = 6;
+constexpr int BK = 64;           // K per pipeline stage: 128-byte bf16 rows, one group of 64 codes
+constexpr int STAGES = 3;
 constexpr int THREADS = 512;
-constexpr int kA = BM * 64;      // bytes of one A stage tile (bf16)
-constexpr int kB = BN * 64;      // bytes of one B stage tile (bf16)
-constexpr int kCode = BM * 32;   // bytes of one stage's code window (32 bytes per A row)
+constexpr int kA = BM * 128;     // bytes of one A stage tile (bf16)
+constexpr int kB = BN * 128;     // bytes of one B stage tile (bf16)
+constexpr int kCode = BM * 64;   // bytes of one stage's code window (64 bytes per A row)
 constexpr int STAGE_BYTES = kA + kB + kCode;
 constexpr int kScaleBuf = 16384; // scales + biases of one unit's rows (<= 32 groups per row)
 constexpr int kStageOut = 4 * 16 * 64;  // epilogue staging: 4 warps x 16 tokens x 64 bytes
@@ -58,8 +62,8 @@ __host__ __device__ constexpr int rows_per_unit() { return MODE == MODE_GATE_UP 
 
 // Tensor maps: index = matrix (0 gate / down, 1 up) + 2 * shared-expert.
 struct Params {
-    CUtensorMap code[4];       // uint8 [experts*rows, row bytes], box 32 bytes x rows_per_unit, 32B swizzle
-    CUtensorMap bmap[kBoxes];  // B rows by position: GATE_UP xp [8T, K], DOWN act [P, K]; box 32 x (16 << i)
+    CUtensorMap code[4];       // uint8 [experts*rows, row bytes], box 64 bytes x rows_per_unit, 64B swizzle
+    CUtensorMap bmap[kBoxes];  // B rows by position: GATE_UP xp [8T, K], DOWN act [P, K]; box 64 x (16 << i), 128B swizzle
     CUtensorMap smap[kBoxes];  // GATE_UP shared-expert B rows: x [rows, K]; same boxes
     QView w[4];                // the same matrices: scales / biases (bulk copies), geometry
     const int32_t *perm_route; // [8T] route id of each permuted position
@@ -79,22 +83,6 @@ __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
 // (address bits [7,9) XOR-ed into bits [4,6)).
 __device__ __forceinline__ uint32_t sw64_offset(uint32_t r, uint32_t c) {
     return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4);
-}
-// Byte offset of 16-byte chunk c (0..1) of row r in a 32B-swizzled tile of 32-byte rows
-// (address bit 7 XOR-ed into bit 4).
-__device__ __forceinline__ uint32_t sw32_offset(uint32_t r, uint32_t c) {
-    return r * 32u + ((c ^ ((r >> 2) & 1u)) << 4);
-}
-
-// Shared-memory descriptor: K-major, 64-byte swizzle, 8-row atoms 512 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1u << 16;             // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(512u >> 4) << 32;    // stride byte offset between 8-row groups
-    d |= (uint64_t)1u << 46;             // descriptor version for tcgen05
-    d |= (uint64_t)4u << 61;             // SWIZZLE_64B
-    return d;
 }
 
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
@@ -156,11 +144,11 @@ __device__ __forceinline__ void a_row(int m, int &mat, int &r) {
     }
 }
 
-// Byte offset of the stage's code window for K-block kb: 8-bit rows hold 32 code bytes per
-// block (aligned); 5-bit blocks are 20 bytes, fetched as the 16-byte-aligned 32-byte window
+// Byte offset of the stage's code window for K-block kb: 8-bit rows hold 64 code bytes per
+// block (aligned); 5-bit blocks are 40 bytes, fetched as the 16-byte-aligned 64-byte window
 // that contains them (the tensor copy's x coordinate must be 16-byte aligned).
 template <int BITS>
-__device__ __forceinline__ int code_x(int kb) { return BITS == 8 ? kb * 32 : ((kb * 20) & ~15); }
+__device__ __forceinline__ int code_x(int kb) { return BITS == 8 ? kb * 64 : ((kb * 40) & ~15); }
 
 // Accumulator slots alternate between units; every role derives the same assignment.
 struct SlotPlan {
@@ -196,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     constexpr int RPU = rows_per_unit<MODE>();
     constexpr int NMAT = MODE == MODE_GATE_UP ? 2 : 1;
     const int RB = (p.rows + RPU - 1) / RPU;
-    const int nk = p.K / BK;  // even (K is a multiple of 64)
+    const int nk = p.K / BK;  // K is a multiple of 64
     const int gpr = p.K / 64;
     const int n_units = (*p.n_tiles) * RB;
 
@@ -236,9 +224,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     // ul * gridDim.x) and K-blocks kb. Stage s = it % STAGES, phase (it / STAGES) & 1.
     if (warp >= 8) {
         // ---------------------------------------------------------------- A dequantisers
-        // group g takes the stage pairs (2j, 2j+1) of the flat index with j % 2 == g; both
-        // stages of a pair use the same quantisation group. Thread m of the group converts A
-        // row m.
+        // group g takes the stages of the flat index with it % 2 == g (each stage is one
+        // quantisation group); thread m of the group converts A row m.
         const int g = (warp - 8) >> 2, m = threadIdx.x - 256 - 128 * g;  // 0..127
         int mat, r;
         a_row<MODE>(m, mat, r);
@@ -253,57 +240,54 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             const uint16_t *b_row = s_row + RPU * gpr;
             uint4 swin = make_uint4(0, 0, 0, 0), bwin = swin;
             int win = -1;
-            // first own pair of this unit: pairs j = (it0 + kb) / 2 with j % 2 == g
-            for (int kb = 2 * ((g - (it0 >> 1)) & 1); kb < nk && ok; kb += 4) {
-                const int gi = kb >> 1;
+            for (int kb = (g - it0) & 1; kb < nk; kb += 2) {
                 float sc, bi;
                 if (fast_scales) {
-                    if ((gi >> 3) != win) {
-                        win = gi >> 3;
+                    if ((kb >> 3) != win) {
+                        win = kb >> 3;
                         swin = *reinterpret_cast<const uint4 *>(s_row + 8 * win);
                         bwin = *reinterpret_cast<const uint4 *>(b_row + 8 * win);
                     }
-                    const int e = gi & 7;
+                    const int e = kb & 7;
                     const uint32_t sw = e < 2 ? swin.x : e < 4 ? swin.y : e < 6 ? swin.z : swin.w;
                     const uint32_t bw = e < 2 ? bwin.x : e < 4 ? bwin.y : e < 6 ? bwin.z : bwin.w;
                     sc = (e & 1) ? bf16_hi(sw) : bf16_lo(sw);
                     bi = (e & 1) ? bf16_hi(bw) : bf16_lo(bw);
                 } else {
-                    sc = bf16_bits_to_f32(s_row[gi]);
-                    bi = bf16_bits_to_f32(b_row[gi]);
+                    sc = bf16_bits_to_f32(s_row[kb]);
+                    bi = bf16_bits_to_f32(b_row[kb]);
                 }
+                const int it = it0 + kb, s = it % STAGES;
+                if (!mbar_wait(&cfull[s], (it / STAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
+                const uint8_t *crow = c_tile(s) + mat * (RPU * 64);
+                uint4 cw[4];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int it = it0 + kb + h, s = it % STAGES;
-                    if (!mbar_wait(&cfull[s], (it / STAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
-                    const uint8_t *crow = c_tile(s) + mat * (RPU * 32);
-                    const uint4 c0 = *reinterpret_cast<const uint4 *>(crow + sw32_offset(r, 0));
-                    const uint4 c1 = *reinterpret_cast<const uint4 *>(crow + sw32_offset(r, 1));
-                    uint32_t o[16];
-                    if constexpr (BITS == 8) {
-                        dequant16_8bit(c0, sc, bi, o);
-                        dequant16_8bit(c1, sc, bi, o + 8);
-                    } else {
-                        const uint32_t win8[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                        const int off = (((kb + h) * 20) & 15) >> 2;  // word offset of the block
-                        uint32_t w5[5];
+                for (int c = 0; c < 4; ++c) cw[c] = *reinterpret_cast<const uint4 *>(crow + sw64_offset(r, c));
+                uint32_t o[32];
+                if constexpr (BITS == 8) {
 #pragma unroll
-                        for (int i = 0; i < 5; ++i)
-                            w5[i] = off == 0 ? win8[i] : off == 1 ? win8[i + 1] : off == 2 ? win8[i + 2] : win8[i + 3];
-                        dequant32_5bit(w5, sc, bi, o);
-                    }
-                    if (!live)
+                    for (int c = 0; c < 4; ++c) dequant16_8bit(cw[c], sc, bi, o + 8 * c);
+                } else {
+                    const uint32_t w16[16] = {cw[0].x, cw[0].y, cw[0].z, cw[0].w, cw[1].x, cw[1].y, cw[1].z, cw[1].w,
+                                              cw[2].x, cw[2].y, cw[2].z, cw[2].w, cw[3].x, cw[3].y, cw[3].z, cw[3].w};
+                    const bool odd = ((kb * 40) & 15) != 0;  // the block starts 8 bytes into the window
+                    uint32_t w10[10];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) o[i] = 0;
-                    uint8_t *t = a_tile(s);
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        *reinterpret_cast<uint4 *>(t + sw64_offset(m, c)) =
-                            make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&full[s]);
+                    for (int i = 0; i < 10; ++i) w10[i] = odd ? w16[i + 2] : w16[i];
+                    dequant32_5bit(w10, sc, bi, o);
+                    dequant32_5bit(w10 + 5, sc, bi, o + 16);
                 }
+                if (!live)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = 0;
+                uint8_t *t = a_tile(s);
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4 *>(t + sw128_offset(m, c)) =
+                        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[sb]);
@@ -349,15 +333,15 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                     ok = mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.err, kErrTimeout);
                     if (ok) {
                         mbar_arrive_expect_tx(&cfull[s], kCode);
-                        mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 64u);
+                        mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u);
                     }
                 }
                 ok = __shfl_sync(kFull, ok, 0);
                 if (!ok) break;
                 if (lane < NMAT)
-                    tma_load_2d(c_tile(s) + lane * (RPU * 32), &p.code[lane + 2 * shared], code_x<BITS>(kb),
+                    tma_load_2d(c_tile(s) + lane * (RPU * 64), &p.code[lane + 2 * shared], code_x<BITS>(kb),
                                 expert * p.w[lane + 2 * shared].rows + rb * RPU, &cfull[s]);
-                if (box_mine) tma_load_2d(b_tile(s) + box_off * 64, bm, kb * BK, row0, &bfull[s]);
+                if (box_mine) tma_load_2d(b_tile(s) + box_off * 128, bm, kb * BK, row0, &bfull[s]);
             }
         }
         if (!ok && lane == 0) {
@@ -391,8 +375,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw64(smem_u32(a_tile(s)));
-                    const uint64_t bdesc = smem_desc_sw64(smem_u32(b_tile(s)));
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(a_tile(s)));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(b_tile(s)));
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) tc_mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, id, (kb | k) != 0);
                     tc_commit(&empty[s]);
