@@ -49,21 +49,24 @@ __device__ __forceinline__ float canonical_dot_warp(const QView &m, int row, con
 
 // ------------------------------------------------------------------ router GEMM (SIMT)
 //
-// logits[t, e] for a tile of 32 tokens x 16 experts per CTA (8 warps: 4 token groups x 2
-// expert groups, 8x8 outputs per warp). For every 256-column block, x and the 8-bit codes are
-// staged with cp.async (double buffered); the CTA dequantises the 16 x 256 weights once into
-// f32 shared memory (w = fma(q, s, b)), and every lane accumulates its 64 outputs over its own
-// 8 columns in the canonical order with paired f32 FMAs; the warp butterfly finishes each sum.
+// logits[t, e] for a tile of 64 tokens x 16 experts per CTA (16 warps: 8 token groups x 2
+// expert groups, 8x8 outputs per warp). 256-column blocks of x and the 8-bit codes are staged
+// with cp.async three deep; one barrier per block. After it, the CTA dequantises the next
+// block's 16 x 256 weights once into f32 shared memory (w = fma(q, s, b), double buffered)
+// while every lane accumulates its 64 outputs over its own 8 columns of the current block in
+// the canonical order with paired f32 FMAs (pairs of tokens). The 32-lane reduction is a
+// reduce-scatter whose every partial sum is the one the xor butterfly 16,8,4,2,1 forms
+// (a + b == b + a exactly), so each logit is bit-identical to the butterfly's.
 namespace router {
-constexpr int TT = 32, TE = 16, KB = 256, THREADS = 256;
+constexpr int TT = 64, TE = 16, KB = 256, THREADS = 512, XS = 3;
 struct Smem {
-    uint16_t x[2][TT][KB];        // 16 KB per stage
-    uint8_t q[2][TE][KB];         // 4 KB per stage
-    uint16_t s[2][TE][KB / 64];
-    uint16_t b[2][TE][KB / 64];
-    // dequantised weights of the current block, 16 KB, laid out [expert][half][lane][4] so that
-    // lane l's columns 8l..8l+3 (half 0) and 8l+4..8l+7 (half 1) are contiguous across lanes
-    float w[TE][2][32][4];
+    uint16_t x[XS][TT][KB];       // 32 KB per stage
+    uint8_t q[XS][TE][KB];        // 4 KB per stage
+    uint16_t s[XS][TE][KB / 64];
+    uint16_t b[XS][TE][KB / 64];
+    // dequantised weights of a block, laid out [expert][half][lane][4] so that lane l's
+    // columns 8l..8l+3 (half 0) and 8l+4..8l+7 (half 1) are contiguous across lanes
+    float w[2][TE][2][32][4];
 };
 }  // namespace router
 
@@ -76,12 +79,13 @@ router_logits_kernel(const uint16_t *__restrict__ x, int T, int D, QView W, cons
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
     const int E = W.rows;
-    const int wt = (warp & 3) * 8, we = (warp >> 2) * 8;  // warp's token / expert offsets in the tile
+    const int wt = (warp & 7) * 8, we = (warp >> 3) * 8;  // warp's token / expert offsets in the tile
     const int nkb = D / KB;
     const int wpr = W.words_per_row(), gpr = W.groups_per_row();
 
-    auto stage = [&](int kb, int buf) {
-        // x: 32 rows x 512 B = 1024 chunks of 16 B, 4 per thread
+    auto stage = [&](int kb) {
+        const int buf = kb % XS;
+        // x: 64 rows x 512 B = 2048 chunks of 16 B, 4 per thread
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int c = tid + i * THREADS, r = c >> 5, ch = c & 31;
@@ -89,23 +93,33 @@ router_logits_kernel(const uint16_t *__restrict__ x, int T, int D, QView W, cons
             const uint16_t *src = x + (size_t)min(t, T - 1) * D + kb * KB + ch * 8;
             cp_async_16(&sm.x[buf][r][ch * 8], src, t < T);
         }
-        // codes: 16 rows x 256 B = 256 chunks, 1 per thread
-        {
+        if (tid < 256) {  // codes: 16 rows x 256 B = 256 chunks
             const int r = tid >> 4, ch = tid & 15, e = e0 + r;
             const uint32_t *src = W.packed + (size_t)min(e, E - 1) * wpr + kb * (KB / 4) + ch * 4;
             cp_async_16(&sm.q[buf][r][ch * 16], src, e < E);
-        }
-        if (tid < TE) {
-            const int e = min(e0 + tid, E - 1);
-            const uint16_t *ss = W.scales + (size_t)e * gpr + kb * (KB / 64);
-            const uint16_t *bb = W.biases + (size_t)e * gpr + kb * (KB / 64);
-#pragma unroll
-            for (int g = 0; g < KB / 64; ++g) {
-                sm.s[buf][tid][g] = __ldg(ss + g);
-                sm.b[buf][tid][g] = __ldg(bb + g);
-            }
+        } else if (tid < 256 + 2 * TE) {  // scales / biases: 4 groups (8 bytes) per expert row
+            const int i = tid - 256, r = i >> 1, e = min(e0 + r, E - 1);
+            const uint16_t *src = ((i & 1) ? W.biases : W.scales) + (size_t)e * gpr + kb * (KB / 64);
+            cp_async_8((i & 1) ? (void *)sm.b[buf][r] : (void *)sm.s[buf][r], src);
         }
         cp_async_commit();
+    };
+    // thread -> (expert tid / 32, lane tid % 32's 8 columns) of a block
+    auto dequant = [&](int kb) {
+        const int buf = kb % XS, r = tid >> 5, l = tid & 31;
+        const float sc = bf16_bits_to_f32(sm.s[buf][r][l >> 3]), bi = bf16_bits_to_f32(sm.b[buf][r][l >> 3]);
+        const uint2 q = *reinterpret_cast<const uint2 *>(&sm.q[buf][r][l * 8]);
+        float4 v0, v1;
+        v0.x = fmaf(byte_to_f32(q.x, 0), sc, bi);
+        v0.y = fmaf(byte_to_f32(q.x, 1), sc, bi);
+        v0.z = fmaf(byte_to_f32(q.x, 2), sc, bi);
+        v0.w = fmaf(byte_to_f32(q.x, 3), sc, bi);
+        v1.x = fmaf(byte_to_f32(q.y, 0), sc, bi);
+        v1.y = fmaf(byte_to_f32(q.y, 1), sc, bi);
+        v1.z = fmaf(byte_to_f32(q.y, 2), sc, bi);
+        v1.w = fmaf(byte_to_f32(q.y, 3), sc, bi);
+        *reinterpret_cast<float4 *>(&sm.w[kb & 1][r][0][l][0]) = v0;
+        *reinterpret_cast<float4 *>(&sm.w[kb & 1][r][1][l][0]) = v1;
     };
 
     float2 acc[4][8];  // [token pair][expert]: (token 2p, token 2p+1)
@@ -114,75 +128,70 @@ router_logits_kernel(const uint16_t *__restrict__ x, int T, int D, QView W, cons
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[p][e] = make_float2(0.f, 0.f);
 
-    stage(0, 0);
+    stage(0);
+    cp_async_wait<0>();
+    __syncthreads();
+    if (nkb > 1) stage(1);
+    dequant(0);
     for (int kb = 0; kb < nkb; ++kb) {
-        const int buf = kb & 1;
-        if (kb + 1 < nkb) {
-            stage(kb + 1, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        {
-            // dequantise this block once: thread -> (expert r, 16 columns)
-            const int r = tid >> 4, c0 = (tid & 15) * 16;
-            const float sc = bf16_bits_to_f32(sm.s[buf][r][c0 >> 6]), bi = bf16_bits_to_f32(sm.b[buf][r][c0 >> 6]);
-            const uint4 q = *reinterpret_cast<const uint4 *>(&sm.q[buf][r][c0]);
-            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        cp_async_wait<0>();  // block kb + 1 (this thread's copies)
+        __syncthreads();     // every copy of kb + 1, w of kb, and the reads of block kb - 1 are done
+        if (kb + 2 < nkb) stage(kb + 2);
+        if (kb + 1 < nkb) dequant(kb + 1);
+        const int xb = kb % XS, wb = kb & 1;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float4 v;
-                v.x = fmaf(byte_to_f32(qw[i], 0), sc, bi);
-                v.y = fmaf(byte_to_f32(qw[i], 1), sc, bi);
-                v.z = fmaf(byte_to_f32(qw[i], 2), sc, bi);
-                v.w = fmaf(byte_to_f32(qw[i], 3), sc, bi);
-                const int col = c0 + 4 * i;  // columns col..col+3 belong to lane col/8, half (col/4)&1
-                *reinterpret_cast<float4 *>(&sm.w[r][(col >> 2) & 1][col >> 3][0]) = v;
+        for (int h = 0; h < 2; ++h) {
+            // x of this lane's columns 8l + 4h .. +3 for the warp's 8 tokens, as f32 pairs (t, t+1)
+            float2 xp[4][4];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const uint2 a = *reinterpret_cast<const uint2 *>(&sm.x[xb][wt + 2 * p][lane * 8 + 4 * h]);
+                const uint2 c = *reinterpret_cast<const uint2 *>(&sm.x[xb][wt + 2 * p + 1][lane * 8 + 4 * h]);
+                xp[p][0] = make_float2(bf16_lo(a.x), bf16_lo(c.x));
+                xp[p][1] = make_float2(bf16_hi(a.x), bf16_hi(c.x));
+                xp[p][2] = make_float2(bf16_lo(a.y), bf16_lo(c.y));
+                xp[p][3] = make_float2(bf16_hi(a.y), bf16_hi(c.y));
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float4 wv = *reinterpret_cast<const float4 *>(&sm.w[wb][we + e][h][lane][0]);
+                const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 w2 = make_float2(w4[j], w4[j]);
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) acc[p][e] = ffma2(xp[p][j], w2, acc[p][e]);
+                }
             }
         }
-        __syncthreads();
-        // x values of this lane's 8 columns for the warp's 8 tokens, as f32 pairs (t, t+1)
-        float2 xp[4][8];
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const uint4 a = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p][lane * 8]);
-            const uint4 c = *reinterpret_cast<const uint4 *>(&sm.x[buf][wt + 2 * p + 1][lane * 8]);
-            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                xp[p][j] = make_float2((j & 1) ? bf16_hi(aw[j >> 1]) : bf16_lo(aw[j >> 1]),
-                                       (j & 1) ? bf16_hi(cw[j >> 1]) : bf16_lo(cw[j >> 1]));
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float4 w0 = *reinterpret_cast<const float4 *>(&sm.w[we + e][0][lane][0]);
-            const float4 w1 = *reinterpret_cast<const float4 *>(&sm.w[we + e][1][lane][0]);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float2 w2 = make_float2(wv[j], wv[j]);
-#pragma unroll
-                for (int p = 0; p < 4; ++p) acc[p][e] = ffma2(xp[p][j], w2, acc[p][e]);
-            }
-        }
-        __syncthreads();
     }
-    // butterfly per output, then lane e writes
+    // reduce-scatter over the 32 lanes: outputs o = p*16 + e*2 + k (token 2p+k, expert e);
+    // at mask m the lane keeps the upper or lower half of its list and adds the partner's
+    // partial of the same outputs; lane l ends with outputs 2l and 2l + 1
+    float v[64];
 #pragma unroll
     for (int p = 0; p < 4; ++p)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const float a = warp_sum_butterfly(acc[p][e].x), c = warp_sum_butterfly(acc[p][e].y);
-            if (lane == e) {
-                const int ee = e0 + we + e, ta = t0 + wt + 2 * p;
-                if (ee < E) {
-                    const float bb = bias ? bias[ee] : 0.f;
-                    if (ta < T) logits[(size_t)ta * E + ee] = a + bb;
-                    if (ta + 1 < T) logits[(size_t)(ta + 1) * E + ee] = c + bb;
-                }
-            }
+            v[p * 16 + e * 2] = acc[p][e].x;
+            v[p * 16 + e * 2 + 1] = acc[p][e].y;
         }
+#pragma unroll
+    for (int m = 16, n = 64; m >= 1; m >>= 1, n >>= 1) {
+        const bool high = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = high ? v[i] : v[i + n / 2];
+            const float keep = high ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(kFull, send, m);
+        }
+    }
+    const int p = lane >> 3, ee = e0 + we + (lane & 7), ta = t0 + wt + 2 * p;
+    if (ee < E) {
+        const float bb = bias ? bias[ee] : 0.f;
+        if (ta < T) logits[(size_t)ta * E + ee] = v[0] + bb;
+        if (ta + 1 < T) logits[(size_t)(ta + 1) * E + ee] = v[1] + bb;
+    }
 }
 
 // Decode-sized router: one warp per expert row, all T (<= 8) tokens per warp.
