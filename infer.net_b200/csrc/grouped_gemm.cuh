@@ -15,8 +15,10 @@
 //                 route slot y[r, d] (r = t*8 + slot) or the shared row ys[t, d]
 //                 (prefill_moe.mm:54-78 semantics)
 //
-// Data movement is asynchronous and issued by one producer warp: per pipeline stage (64
-// K-columns, one quantisation group) a tensor copy of the stage's code bytes and B rows, which
+// Data movement is asynchronous and issued by two producer warps: per pipeline stage (64
+// K-columns, one quantisation group) a tensor copy of the stage's code bytes (into a code ring
+// of its own, released as soon as the dequantisers hold the codes in registers, so code
+// fetches run ahead of the MMA) and of its B rows, which
 // are contiguous for every unit (gate/up reads the token rows already permuted into expert
 // order, down the activation rows), as at most five boxes of 16 << i rows issued by as many
 // lanes at once; per unit one bulk copy each of the scales and biases of the unit's rows.
@@ -26,8 +28,8 @@
 // swizzled bf16 A tile.
 //
 // Warp roles (512 threads): 0-3 epilogue (one TMEM lane quadrant each), 4 MMA issue + TMEM
-// owner, 5 producer, 6-7 idle, 8-15 A dequantisers in two groups of 4 warps that take
-// alternate pipeline stages.
+// owner, 5 code and scale producer, 6 B producer, 7 idle, 8-15 A dequantisers in two groups
+// of 4 warps that take alternate pipeline stages.
 //
 // Stage size: every stage costs a fixed round trip (MMA commit -> producer -> tensor copy ->
 // dequantiser -> MMA issue, several hundred cycles on B200) and fixed issue work, so stages
@@ -50,11 +52,12 @@ constexpr int THREADS = 512;
 constexpr int kA = BM * 128;     // bytes of one A stage tile (bf16)
 constexpr int kB = BN * 128;     // bytes of one B stage tile (bf16)
 constexpr int kCode = BM * 64;   // bytes of one stage's code window (64 bytes per A row)
-constexpr int STAGE_BYTES = kA + kB + kCode;
+constexpr int STAGE_BYTES = kA + kB;
+constexpr int CSTAGES = 4;       // code ring slots
 constexpr int kScaleBuf = 16384; // scales + biases of one unit's rows (<= 32 groups per row)
 constexpr int kStageOut = 4 * 16 * 64;  // epilogue staging: 4 warps x 16 tokens x 64 bytes
 constexpr int kBoxes = 5;               // down B boxes of 16 << i rows, i < kBoxes
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 2 * kScaleBuf + kStageOut + 512;
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + CSTAGES * kCode + 2 * kScaleBuf + kStageOut + 512;
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int MODE>
@@ -169,16 +172,18 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
     uint8_t *smem = smem_raw + pad;
-    uint8_t *scale_buf = smem + STAGES * STAGE_BYTES;
+    uint8_t *code_ring = smem + STAGES * STAGE_BYTES;
+    uint8_t *scale_buf = code_ring + CSTAGES * kCode;
     uint8_t *stage_out = scale_buf + 2 * kScaleBuf;
     uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
-    uint64_t *full = bars, *bfull = bars + STAGES, *cfull = bars + 2 * STAGES, *empty = bars + 3 * STAGES;
-    uint64_t *sfull = bars + 4 * STAGES, *sempty = sfull + 2;
+    uint64_t *full = bars, *bfull = bars + STAGES, *empty = bars + 2 * STAGES;
+    uint64_t *cfull = bars + 3 * STAGES, *cempty = cfull + CSTAGES;
+    uint64_t *sfull = cempty + CSTAGES, *sempty = sfull + 2;
     uint64_t *accf = sempty + 2, *acce = accf + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
     auto a_tile = [&](int s) { return smem + s * STAGE_BYTES; };
     auto b_tile = [&](int s) { return smem + s * STAGE_BYTES + kA; };
-    auto c_tile = [&](int s) { return smem + s * STAGE_BYTES + kA + kB; };
+    auto c_tile = [&](int cs) { return code_ring + cs * kCode; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int RPU = rows_per_unit<MODE>();
@@ -191,9 +196,12 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 4);   // the dequantiser warps of the stage's group
-            mbar_init(&bfull[s], 1);  // producer arrive + B bytes
-            mbar_init(&cfull[s], 1);  // producer arrive + code bytes
+            mbar_init(&bfull[s], 1);  // B producer arrive + B bytes
             mbar_init(&empty[s], 1);  // MMA commit
+        }
+        for (int c = 0; c < CSTAGES; ++c) {
+            mbar_init(&cfull[c], 1);   // code producer arrive + code bytes
+            mbar_init(&cempty[c], 4);  // the dequantiser warps holding the codes in registers
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&sfull[a], 1);
@@ -207,13 +215,14 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
-    if (warp == 5 && lane == 0) {
+    if (warp == 6 && lane == 0) {
         for (int i = 0; i < kBoxes; ++i) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&p.bmap[i]) : "memory");
             if constexpr (MODE == MODE_GATE_UP) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.smap[i]) : "memory");
         }
-        for (int i = 0; i < 4; ++i) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.code[i]) : "memory");
     }
+    if (warp == 5 && lane == 0)
+        for (int i = 0; i < 4; ++i) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.code[i]) : "memory");
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -257,12 +266,14 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                     sc = bf16_bits_to_f32(s_row[kb]);
                     bi = bf16_bits_to_f32(b_row[kb]);
                 }
-                const int it = it0 + kb, s = it % STAGES;
-                if (!mbar_wait(&cfull[s], (it / STAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
-                const uint8_t *crow = c_tile(s) + mat * (RPU * 64);
+                const int it = it0 + kb, s = it % STAGES, cs = it % CSTAGES;
+                if (!mbar_wait(&cfull[cs], (it / CSTAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
+                const uint8_t *crow = c_tile(cs) + mat * (RPU * 64);
                 uint4 cw[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) cw[c] = *reinterpret_cast<const uint4 *>(crow + sw64_offset(r, c));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&cempty[cs]);  // the code slot may be refilled
                 uint32_t o[32];
                 if constexpr (BITS == 8) {
 #pragma unroll
@@ -280,6 +291,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 if (!live)
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[i] = 0;
+                // the A tile is free once the MMA of the stage's previous use has completed
+                if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
                 uint8_t *t = a_tile(s);
 #pragma unroll
                 for (int c = 0; c < 8; ++c)
@@ -293,14 +306,13 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             if (lane == 0) mbar_arrive(&sempty[sb]);
         }
     } else if (warp == 5) {
-        // ---------------------------------------------------------------- producer
+        // ---------------------------------------------------------------- code and scale producer
         int it = 0, ul = 0;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ul) {
             const Tile tl = p.tiles[u / RB];
             const int rb = u % RB, sb = ul & 1;
             const bool shared = tl.seg >= p.E;
             const int expert = shared ? 0 : tl.seg;
-            const int N = round16(tl.n);
             // scales and biases of the unit's rows
             if (lane == 0) {
                 ok = mbar_wait(&sempty[sb], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeout);
@@ -319,8 +331,34 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             }
             ok = __shfl_sync(kFull, ok, 0);
             if (!ok) break;
-            // B boxes of this unit: lane i < kBoxes copies 16 << i rows when bit i of N/16 is set,
-            // larger boxes first
+            const int row0 = expert * p.w[(lane & 1) + 2 * shared].rows + rb * RPU;
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                const int cs = it % CSTAGES;
+                if (lane == 0) {
+                    ok = mbar_wait(&cempty[cs], ((it / CSTAGES) & 1) ^ 1, p.err, kErrTimeout);
+                    if (ok) mbar_arrive_expect_tx(&cfull[cs], kCode);
+                }
+                ok = __shfl_sync(kFull, ok, 0);
+                if (!ok) break;
+                if (lane < NMAT)
+                    tma_load_2d(c_tile(cs) + lane * (RPU * 64), &p.code[lane + 2 * shared], code_x<BITS>(kb), row0,
+                                &cfull[cs]);
+            }
+        }
+        if (!ok && lane == 0) {
+            // copies still in flight must land before the CTA's shared memory is released
+            for (int k = max(0, it - CSTAGES); k < it; ++k)
+                mbar_wait(&cfull[k % CSTAGES], (k / CSTAGES) & 1, p.err, kErrTimeout);
+            for (int k = max(0, ul - 1); k <= ul; ++k) mbar_wait(&sfull[k & 1], (k >> 1) & 1, p.err, kErrTimeout);
+        }
+    } else if (warp == 6) {
+        // ---------------------------------------------------------------- B producer
+        int it = 0;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            const Tile tl = p.tiles[u / RB];
+            const bool shared = tl.seg >= p.E;
+            const int N = round16(tl.n);
+            // lane i < kBoxes copies 16 << i rows when bit i of N/16 is set, larger boxes first
             const int nb16 = N >> 4;
             const bool box_mine = lane < kBoxes && ((nb16 >> lane) & 1);
             const int box_off = box_mine ? 16 * ((nb16 >> (lane + 1)) << (lane + 1)) : 0;
@@ -331,28 +369,16 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 const int s = it % STAGES;
                 if (lane == 0) {
                     ok = mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.err, kErrTimeout);
-                    if (ok) {
-                        mbar_arrive_expect_tx(&cfull[s], kCode);
-                        mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u);
-                    }
+                    if (ok) mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u);
                 }
                 ok = __shfl_sync(kFull, ok, 0);
                 if (!ok) break;
-                if (lane < NMAT)
-                    tma_load_2d(c_tile(s) + lane * (RPU * 64), &p.code[lane + 2 * shared], code_x<BITS>(kb),
-                                expert * p.w[lane + 2 * shared].rows + rb * RPU, &cfull[s]);
                 if (box_mine) tma_load_2d(b_tile(s) + box_off * 128, bm, kb * BK, row0, &bfull[s]);
             }
         }
-        if (!ok && lane == 0) {
-            // copies still in flight must land before the CTA's shared memory is released
-            for (int k = max(0, it - STAGES); k < it; ++k) {
-                const int s = k % STAGES;
-                mbar_wait(&cfull[s], (k / STAGES) & 1, p.err, kErrTimeout);
-                mbar_wait(&bfull[s], (k / STAGES) & 1, p.err, kErrTimeout);
-            }
-            for (int k = max(0, ul - 1); k <= ul; ++k) mbar_wait(&sfull[k & 1], (k >> 1) & 1, p.err, kErrTimeout);
-        }
+        if (!ok && lane == 0)
+            for (int k = max(0, it - STAGES); k < it; ++k)
+                mbar_wait(&bfull[k % STAGES], (k / STAGES) & 1, p.err, kErrTimeout);
     } else if (warp == 4) {
         // ---------------------------------------------------------------- MMA issue
         if (lane == 0) {
