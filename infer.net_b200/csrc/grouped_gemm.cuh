@@ -56,8 +56,9 @@ constexpr int STAGE_BYTES = kA + kB;
 constexpr int CSTAGES = 4;       // code ring slots
 constexpr int kScaleBuf = 16384; // scales + biases of one unit's rows (<= 32 groups per row)
 constexpr int kStageOut = 4 * 16 * 64;  // epilogue staging: 4 warps x 16 tokens x 64 bytes
+constexpr int kRouteTab = 4 * 2 * BN * 4;  // DOWN epilogue: output rows of this and the next unit, per warp
 constexpr int kBoxes = 5;               // down B boxes of 16 << i rows, i < kBoxes
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + CSTAGES * kCode + 2 * kScaleBuf + kStageOut + 512;
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + CSTAGES * kCode + 2 * kScaleBuf + kStageOut + kRouteTab + 512;
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int MODE>
@@ -175,7 +176,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     uint8_t *code_ring = smem + STAGES * STAGE_BYTES;
     uint8_t *scale_buf = code_ring + CSTAGES * kCode;
     uint8_t *stage_out = scale_buf + 2 * kScaleBuf;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
+    int32_t *route_tab = reinterpret_cast<int32_t *>(stage_out + kStageOut);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut + kRouteTab);
     uint64_t *full = bars, *bfull = bars + STAGES, *empty = bars + 2 * STAGES;
     uint64_t *cfull = bars + 3 * STAGES, *cempty = cfull + CSTAGES;
     uint64_t *sfull = cempty + CSTAGES, *sempty = sfull + 2;
@@ -416,38 +418,53 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         // ---------------------------------------------------------------- epilogue
         const int q = warp;  // TMEM lanes 32q .. 32q+31
         uint8_t *so = stage_out + q * 16 * 64;
+        // DOWN: output row of every token of a unit (route id, or -1 - t for shared rows), in a
+        // per-warp table; the next unit's rows are loaded while this unit is written out
+        int32_t *rtab = route_tab + q * 2 * BN;
+        int rnext[BN / 32];
+        auto load_routes = [&](const Tile &t2) {
+            const bool sh2 = t2.seg >= p.E;
+#pragma unroll
+            for (int k = 0; k < BN / 32; ++k) {
+                const int n = lane + 32 * k, pos = t2.p0 + n;
+                rnext[k] = n < t2.n ? (sh2 ? -1 - (pos - p.shared_pos0) : p.perm_route[pos]) : 0;
+            }
+        };
+        auto store_routes = [&](int buf) {
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < BN / 32; ++k) rtab[buf * BN + lane + 32 * k] = rnext[k];
+            __syncwarp();
+        };
+        if constexpr (MODE == MODE_DOWN)
+            if ((int)blockIdx.x < n_units) {
+                load_routes(p.tiles[blockIdx.x / RB]);
+                store_routes(0);
+            }
         SlotPlan plan;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        int ul = 0;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ul) {
             const Tile tl = p.tiles[u / RB];
             const int rb = u % RB;
-            const bool shared = tl.seg >= p.E;
             const int N = round16(tl.n);
             uint32_t phase;
             const int slot = plan.take(phase);
             if (!mbar_wait(&accf[slot], phase & 1, p.err, kErrTimeout)) { ok = false; break; }
             tc_fence_after();
+            const bool has_next = u + (int)gridDim.x < n_units;
+            if constexpr (MODE == MODE_DOWN)
+                if (has_next) load_routes(p.tiles[(u + gridDim.x) / RB]);
+            const int32_t *rcur = rtab + (ul & 1) * BN;
             const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + slot * 256;
-            // software pipeline: the TMEM columns (and, for down, the output rows) of chunk c + 16
-            // are requested while chunk c is processed
+            // software pipeline: the TMEM columns of chunk c + 16 are requested while chunk c is
+            // processed
             float v[16], vn[16];
-            int rid = 0, rid_next = 0;  // DOWN: output row of token (c + lane) for lanes < 16
-            auto route_of = [&](int c) -> int {
-                const int n = c + (lane & 15);
-                if (n >= tl.n) return 0;
-                const int pos = tl.p0 + n;
-                return shared ? -1 - (pos - p.shared_pos0) : p.perm_route[pos];
-            };
             tmem_ld16(lane_base, vn);
-            if constexpr (MODE == MODE_DOWN) rid_next = route_of(0);
             for (int c = 0; c < N; c += 16) {
                 tc_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = vn[j];
-                rid = rid_next;
-                if (c + 16 < N) {
-                    tmem_ld16(lane_base + c + 16, vn);
-                    if constexpr (MODE == MODE_DOWN) rid_next = route_of(c + 16);
-                }
+                if (c + 16 < N) tmem_ld16(lane_base + c + 16, vn);
                 if constexpr (MODE == MODE_GATE_UP) {
                     // lanes 0-15 hold the gate rows of intermediates rb*64 + 16q + (lane & 15), lanes
                     // 16-31 their up rows; branch-free: lanes 0-15 finish tokens 0-7 of the chunk,
@@ -480,7 +497,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                     for (int h = 0; h < 2; ++h) {
                         const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
                         const int d = rb * 128 + 32 * q + part * 8;
-                        const int rr = __shfl_sync(kFull, rid, tk);
+                        const int rr = rcur[n];
                         if (n < tl.n && d < p.rows) {
                             const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 64 + part * 16);
                             uint16_t *dst = rr >= 0 ? p.out + (size_t)rr * p.rows : p.out_shared + (size_t)(-1 - rr) * p.rows;
@@ -493,6 +510,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[slot]);
+            if constexpr (MODE == MODE_DOWN)
+                if (has_next) store_routes((ul + 1) & 1);
         }
     }
     tc_fence_before();
