@@ -280,7 +280,7 @@ gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QVie
                           const uint16_t *src, int src_rows, const uint16_t *shared_src, int shared_rows,
                           const int32_t *perm, const Tile *tiles,
                           const int32_t *n_tiles, int shared_pos0, int shared_src0, int K, int rows, int E,
-                          uint16_t *out, uint16_t *out_shared, uint32_t *err) {
+                          uint16_t *out, int out_rows, uint32_t *err) {
     gg::Params p;
     std::memset(&p, 0, sizeof(p));
     const QView ws[4] = {w0, w1, s0, s1};
@@ -307,8 +307,10 @@ gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QVie
     p.K = K;
     p.rows = rows;
     p.E = E;
+    if (mode == gg::MODE_DOWN)
+        encode_2d(&p.ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, (uint64_t)rows, (uint64_t)std::max(out_rows, 1),
+                  (uint64_t)rows * 2, 32, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
     p.out = out;
-    p.out_shared = out_shared;
     p.err = err;
     return p;
 }
@@ -324,7 +326,7 @@ void launch_grouped(const gg::Params &p, int bits, int grid, cudaStream_t st) {
 struct BlockBuffers {
     uint16_t *x, *y;
     float *logits, *probs, *gate;
-    int32_t *ids, *block_counts, *block_base, *seg_count, *seg_off, *n_tiles, *perm;
+    int32_t *ids, *block_counts, *block_base, *seg_count, *seg_off, *n_tiles, *perm, *route_pos;
     Tile *tiles;
     uint16_t *act, *yr, *ys, *xp;
     float *act32;
@@ -348,10 +350,10 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     size_t o_so = cv.take<int32_t>(E + 1);
     size_t o_nt = cv.take<int32_t>(1);
     size_t o_pm = cv.take<int32_t>((size_t)T * 8);
+    size_t o_rp = cv.take<int32_t>((size_t)T * 8);
     size_t o_t = cv.take<Tile>((size_t)b.max_tiles);
     size_t o_a = gemv ? 0 : cv.take<uint16_t>((size_t)T * 9 * I);
-    size_t o_yr = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
-    size_t o_ys = gemv ? 0 : cv.take<uint16_t>((size_t)T * D);
+    size_t o_yp = gemv ? 0 : cv.take<uint16_t>((size_t)T * 9 * D);  // expert rows by position, shared rows last
     size_t o_xp = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
     size_t o_a32 = gemv ? cv.take<float>((size_t)T * 9 * I) : 0;
     size_t o_ctr = cv.take<uint32_t>(1);
@@ -369,10 +371,11 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     b.seg_off = at<int32_t>(c, o_so);
     b.n_tiles = at<int32_t>(c, o_nt);
     b.perm = at<int32_t>(c, o_pm);
+    b.route_pos = at<int32_t>(c, o_rp);
     b.tiles = at<Tile>(c, o_t);
     b.act = gemv ? nullptr : at<uint16_t>(c, o_a);
-    b.yr = gemv ? nullptr : at<uint16_t>(c, o_yr);
-    b.ys = gemv ? nullptr : at<uint16_t>(c, o_ys);
+    b.yr = gemv ? nullptr : at<uint16_t>(c, o_yp);
+    b.ys = gemv ? nullptr : b.yr + (size_t)T * 8 * D;
     b.xp = gemv ? nullptr : at<uint16_t>(c, o_xp);
     b.act32 = gemv ? at<float>(c, o_a32) : nullptr;
     b.counter = at<uint32_t>(c, o_ctr);
@@ -473,25 +476,25 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
                                           b.seg_off, b.tiles, b.n_tiles, b.max_tiles, c->d_err);
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
-    scatter_routes_kernel<<<b.nblocks, 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm);
+    scatter_routes_kernel<<<b.nblocks, 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos);
     // token rows in expert order for the gate/up B operand (timed with the scatter)
     permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(x, b.perm, b.seg_off + E, D, b.xp);
     if (profile) stage_mark(c, S_GATE_UP);
     // 5. grouped gate/up + SwiGLU (routed experts and the shared expert)
     const int grid = c->sms;
     launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, G, U, SG, SU, b.xp, 8 * T, x, T, b.perm,
-                                                    b.tiles, b.n_tiles, 8 * T, 0, D, I, E, b.act, nullptr, c->d_err),
+                                                    b.tiles, b.n_tiles, 8 * T, 0, D, I, E, b.act, 9 * T, c->d_err),
                                      L->bits, grid, st);
     if (profile) stage_mark(c, S_DOWN);
     // 6. grouped down -> expert rows in route order, shared rows
     launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dn, Dn, SD, SD, b.act, 9 * T, nullptr, 0, b.perm,
-                                                 b.tiles, b.n_tiles, 8 * T, 0, I, D, E, b.yr, b.ys, c->d_err),
+                                                 b.tiles, b.n_tiles, 8 * T, 0, I, D, E, b.yr, 9 * T, c->d_err),
                                   L->bits, grid, st);
     if (profile) stage_mark(c, S_COMBINE);
     // 7. combine
     {
         const size_t n = (size_t)T * (D / 8);
-        combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(b.yr, b.ys, b.gate, probs, T, D, y, resid,
+        combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(b.yr, b.route_pos, b.ys, b.gate, probs, T, D, y, resid,
                                                                      c->d_err);
     }
     if (profile) stage_mark(c, S_N);
@@ -1575,14 +1578,15 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         const size_t o_rbb = cv.take<int32_t>((size_t)(nb_r + 1) * (El + 1)), o_sgc = cv.take<int32_t>(El + 2);
         const size_t o_sgo = cv.take<int32_t>(El + 2), o_t = cv.take<Tile>(max_tiles), o_nt = cv.take<int32_t>(1);
         const size_t o_pm = cv.take<int32_t>((size_t)Rmax * 8 + 8), o_act = cv.take<uint16_t>(((size_t)Rmax * 8 + T) * I);
-        const size_t o_y = cv.take<uint16_t>((size_t)Rmax * 8 * D + 8), o_ys = cv.take<uint16_t>((size_t)T * D);
+        const size_t o_y = cv.take<uint16_t>(((size_t)Rmax * 8 + T) * D + 8), o_rp = cv.take<int32_t>((size_t)Rmax * 8 + 8);
         const size_t o_z = cv.take<uint16_t>((size_t)Rmax * D + 8), o_bk = cv.take<uint16_t>((size_t)Smax * D);
         const size_t o_xp = cv.take<uint16_t>((size_t)Rmax * 8 * D + 8);
         ensure_workspace(c, cv.off + 256);
         float *dx = dev_io ? x : at<float>(c, o_x);
         const float *dn = dev_io ? norms : at<float>(c, o_n);
         uint16_t *h = at<uint16_t>(c, o_h), *sx = at<uint16_t>(c, o_sx), *rx = at<uint16_t>(c, o_rx);
-        uint16_t *act = at<uint16_t>(c, o_act), *y = at<uint16_t>(c, o_y), *ys = at<uint16_t>(c, o_ys);
+        uint16_t *act = at<uint16_t>(c, o_act), *y = at<uint16_t>(c, o_y);
+        int32_t *rpos = at<int32_t>(c, o_rp);
         uint16_t *z = at<uint16_t>(c, o_z), *bk = at<uint16_t>(c, o_bk), *xp = at<uint16_t>(c, o_xp);
         float *logits = at<float>(c, o_lg), *probs = at<float>(c, o_p), *gate = at<float>(c, o_g);
         int32_t *ids = at<int32_t>(c, o_ids), *bc = at<int32_t>(c, o_bc), *sidx = at<int32_t>(c, o_sidx);
@@ -1645,19 +1649,20 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             else CK(cudaMemsetAsync(rbc, 0, sizeof(int32_t) * (El + 1), st));
             scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, Rn, T, gg::BN, rbb, sgc, sgo, tiles, nt,
                                                   max_tiles, c->d_err);
-            if (Rn > 0) scatter_routes_kernel<<<nbr, 32, 0, st>>>(il, Rn, El + 1, rbb, sgo, perm);
+            if (Rn > 0) scatter_routes_kernel<<<nbr, 32, 0, st>>>(il, Rn, El + 1, rbb, sgo, perm, rpos);
             if (Rn > 0) permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(rx, perm, sgo + El, D, xp);
             launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, Gm, U, SG, SU, xp, 8 * Rn, rx, Rn + T,
-                                                            perm, tiles, nt, 8 * Rn, Rn, D, I, El + 1, act, nullptr,
-                                                            c->d_err),
+                                                            perm, tiles, nt, 8 * Rn, Rn, D, I, El + 1, act,
+                                                            8 * Rn + T, c->d_err),
                                              L->bits, grid, st);
             launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dm, Dm, SD, SD, act, 8 * Rn + T, nullptr, 0,
-                                                         perm, tiles, nt, 8 * Rn, 0, I, D, El + 1, y, ys, c->d_err),
+                                                         perm, tiles, nt, 8 * Rn, 0, I, D, El + 1, y, 8 * Rn + T,
+                                                         c->d_err),
                                           L->bits, grid, st);
             // 5. partial row sums back to the token owners, then the owner's combine
             if (Rn > 0) {
                 const size_t n = (size_t)Rn * (D / 8);
-                ep_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(y, il, rmeta, Rn, D, El, z);
+                ep_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(y, rpos, il, rmeta, Rn, D, El, z);
             }
             NK(nc->groupStart());
             for (int q = 0; q < G; ++q) {
@@ -1667,7 +1672,8 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             NK(nc->groupEnd());
             {
                 const size_t n = (size_t)T * (D / 8);
-                ep_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(bk, sidx, so, G, ys, gate, T, D, dx,
+                ep_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(bk, sidx, so, G, y + (size_t)8 * Rn * D, gate, T,
+                                                                                D, dx,
                                                                                 c->d_err);
             }
             if (launch_check(error, capacity)) return -1;

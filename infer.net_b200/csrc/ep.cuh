@@ -107,8 +107,10 @@ ep_recv_count_kernel(const RowMeta *__restrict__ meta, int R, int E_off, int E_l
     for (int i = threadIdx.x; i <= E_l; i += blockDim.x) block_counts[(size_t)blockIdx.x * (E_l + 1) + i] = hist[i];
 }
 
-// Receiver: z[i] = sum over local slots j (slot order) of p[i,j] * y[8i+j], f32 then bf16.
-__global__ void ep_reduce_kernel(const uint16_t *__restrict__ y, const int32_t *__restrict__ ids_local,
+// Receiver: z[i] = sum over local slots j (slot order) of p[i,j] * y[8i+j], f32 then bf16; the
+// expert rows are stored in expert order, y[8i+j] = yp[route_pos[8i+j]].
+__global__ void ep_reduce_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__ route_pos,
+                                 const int32_t *__restrict__ ids_local,
                                  const RowMeta *__restrict__ meta, int R, int D, int E_l, uint16_t *__restrict__ z) {
     const int per_row = D / 8;
     const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -119,7 +121,7 @@ __global__ void ep_reduce_kernel(const uint16_t *__restrict__ y, const int32_t *
     for (int j = 0; j < 8; ++j) {
         if (ids_local[(size_t)i * 8 + j] >= E_l) continue;
         const float p = meta[i].probs[j];
-        const uint4 v = *reinterpret_cast<const uint4 *>(y + ((size_t)i * 8 + j) * D + c);
+        const uint4 v = *reinterpret_cast<const uint4 *>(yp + (size_t)route_pos[(size_t)i * 8 + j] * D + c);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int k = 0; k < 8; ++k) {

@@ -11,8 +11,9 @@
 //                 epilogue pairs them with one warp shuffle; a unit covers 64 intermediate
 //                 indices and up to 256 tokens. act = silu(gate) * up -> bf16 act[p, i]
 //                 (quantized.mm:148-189; prefill_moe.mm:23-53 semantics)
-//   MODE_DOWN:    128 rows of the down matrix; the epilogue writes each bf16 expert row to its
-//                 route slot y[r, d] (r = t*8 + slot) or the shared row ys[t, d]
+//   MODE_DOWN:    128 rows of the down matrix; the epilogue writes the bf16 expert rows in
+//                 expert order, yp[position, d] (the combine finds route r's row through the
+//                 inverse permutation), as 16-token x 32-dim tensor stores
 //                 (prefill_moe.mm:54-78 semantics)
 //
 // Data movement is asynchronous and issued by two producer warps: per pipeline stage (64
@@ -55,10 +56,9 @@ constexpr int kCode = BM * 64;   // bytes of one stage's code window (64 bytes p
 constexpr int STAGE_BYTES = kA + kB;
 constexpr int CSTAGES = 4;       // code ring slots
 constexpr int kScaleBuf = 16384; // scales + biases of one unit's rows (<= 32 groups per row)
-constexpr int kStageOut = 4 * 16 * 64;  // epilogue staging: 4 warps x 16 tokens x 64 bytes
-constexpr int kRouteTab = 4 * 2 * BN * 4;  // DOWN epilogue: output rows of this and the next unit, per warp
+constexpr int kStageOut = 4 * 2 * 16 * 64;  // epilogue staging: 4 warps x 2 buffers x 16 tokens x 64 bytes
 constexpr int kBoxes = 5;               // down B boxes of 16 << i rows, i < kBoxes
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + CSTAGES * kCode + 2 * kScaleBuf + kStageOut + kRouteTab + 512;
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + CSTAGES * kCode + 2 * kScaleBuf + kStageOut + 512;
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int MODE>
@@ -69,6 +69,7 @@ struct Params {
     CUtensorMap code[4];       // uint8 [experts*rows, row bytes], box 64 bytes x rows_per_unit, 64B swizzle
     CUtensorMap bmap[kBoxes];  // B rows by position: GATE_UP xp [8T, K], DOWN act [P, K]; box 64 x (16 << i), 128B swizzle
     CUtensorMap smap[kBoxes];  // GATE_UP shared-expert B rows: x [rows, K]; same boxes
+    CUtensorMap ymap;          // DOWN output yp [P, rows] bf16, box 32 x 16, no swizzle
     QView w[4];                // the same matrices: scales / biases (bulk copies), geometry
     const int32_t *perm_route; // [8T] route id of each permuted position
     const Tile *tiles;
@@ -76,8 +77,7 @@ struct Params {
     int shared_pos0;           // first permuted position of the shared-expert segment
     int shared_src0;           // GATE_UP: source row of that first shared position
     int K, rows, E;            // rows: I (GATE_UP) or D (DOWN); segments >= E are the shared expert
-    uint16_t *out;             // GATE_UP: act [P, rows]; DOWN: y [8T, rows]
-    uint16_t *out_shared;      // DOWN: ys [T, rows]
+    uint16_t *out;             // GATE_UP: act [P, rows]; DOWN: yp [P, rows] (written through ymap)
     uint32_t *err;
 };
 
@@ -176,8 +176,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     uint8_t *code_ring = smem + STAGES * STAGE_BYTES;
     uint8_t *scale_buf = code_ring + CSTAGES * kCode;
     uint8_t *stage_out = scale_buf + 2 * kScaleBuf;
-    int32_t *route_tab = reinterpret_cast<int32_t *>(stage_out + kStageOut);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut + kRouteTab);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
     uint64_t *full = bars, *bfull = bars + STAGES, *empty = bars + 2 * STAGES;
     uint64_t *cfull = bars + 3 * STAGES, *cempty = cfull + CSTAGES;
     uint64_t *sfull = cempty + CSTAGES, *sempty = sfull + 2;
@@ -417,33 +416,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     } else if (warp < 4) {
         // ---------------------------------------------------------------- epilogue
         const int q = warp;  // TMEM lanes 32q .. 32q+31
-        uint8_t *so = stage_out + q * 16 * 64;
-        // DOWN: output row of every token of a unit (route id, or -1 - t for shared rows), in a
-        // per-warp table; the next unit's rows are loaded while this unit is written out
-        int32_t *rtab = route_tab + q * 2 * BN;
-        int rnext[BN / 32];
-        auto load_routes = [&](const Tile &t2) {
-            const bool sh2 = t2.seg >= p.E;
-#pragma unroll
-            for (int k = 0; k < BN / 32; ++k) {
-                const int n = lane + 32 * k, pos = t2.p0 + n;
-                rnext[k] = n < t2.n ? (sh2 ? -1 - (pos - p.shared_pos0) : p.perm_route[pos]) : 0;
-            }
-        };
-        auto store_routes = [&](int buf) {
-            __syncwarp();
-#pragma unroll
-            for (int k = 0; k < BN / 32; ++k) rtab[buf * BN + lane + 32 * k] = rnext[k];
-            __syncwarp();
-        };
-        if constexpr (MODE == MODE_DOWN)
-            if ((int)blockIdx.x < n_units) {
-                load_routes(p.tiles[blockIdx.x / RB]);
-                store_routes(0);
-            }
+        uint8_t *so = stage_out + q * 2 * 16 * 64;
+        int chunk_no = 0;  // DOWN: staging buffer of a chunk = chunk_no & 1
         SlotPlan plan;
-        int ul = 0;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ul) {
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const Tile tl = p.tiles[u / RB];
             const int rb = u % RB;
             const int N = round16(tl.n);
@@ -451,10 +427,6 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             const int slot = plan.take(phase);
             if (!mbar_wait(&accf[slot], phase & 1, p.err, kErrTimeout)) { ok = false; break; }
             tc_fence_after();
-            const bool has_next = u + (int)gridDim.x < n_units;
-            if constexpr (MODE == MODE_DOWN)
-                if (has_next) load_routes(p.tiles[(u + gridDim.x) / RB]);
-            const int32_t *rcur = rtab + (ul & 1) * BN;
             const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + slot * 256;
             // software pipeline: the TMEM columns of chunk c + 16 are requested while chunk c is
             // processed
@@ -488,31 +460,41 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                     }
                     __syncwarp();
                 } else {
-                    // lane holds output dim rb*128 + 32q + lane for 16 tokens
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) reinterpret_cast<uint16_t *>(so)[j * 32 + lane] = f32_to_bf16_bits(v[j]);
+                    // lane holds output dim rb*128 + 32q + lane for 16 tokens: stage [token][dim]
+                    // and store the 16 x 32 tile with one tensor store (the tail rows of a tile,
+                    // which must not spill into the next tile's positions, with plain stores)
+                    uint8_t *sb = so + (chunk_no & 1) * 1024;
+                    ++chunk_no;
+                    if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done
                     __syncwarp();
-                    // 16 tokens x 64 bytes = 64 chunks of 16 bytes, two per lane
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
-                        const int d = rb * 128 + 32 * q + part * 8;
-                        const int rr = rcur[n];
-                        if (n < tl.n && d < p.rows) {
-                            const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 64 + part * 16);
-                            uint16_t *dst = rr >= 0 ? p.out + (size_t)rr * p.rows : p.out_shared + (size_t)(-1 - rr) * p.rows;
-                            *reinterpret_cast<uint4 *>(dst + d) = val;
+                    for (int j = 0; j < 16; ++j) reinterpret_cast<uint16_t *>(sb)[j * 32 + lane] = f32_to_bf16_bits(v[j]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    const int d0 = rb * 128 + 32 * q;
+                    if (tl.n - c >= 16) {
+                        if (lane == 0) {
+                            tma_store_2d(&p.ymap, sb, d0, tl.p0 + c);
+                            bulk_commit();
+                        }
+                    } else {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
+                            const int d = d0 + part * 8;
+                            if (n < tl.n && d < p.rows)
+                                *reinterpret_cast<uint4 *>(p.out + (size_t)(tl.p0 + n) * p.rows + d) =
+                                    *reinterpret_cast<const uint4 *>(sb + tk * 64 + part * 16);
                         }
                     }
-                    __syncwarp();
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[slot]);
-            if constexpr (MODE == MODE_DOWN)
-                if (has_next) store_routes((ul + 1) & 1);
         }
+        if constexpr (MODE == MODE_DOWN)
+            if (lane == 0) bulk_wait<0>();  // tensor stores complete before the CTA exits
     }
     tc_fence_before();
     __syncthreads();

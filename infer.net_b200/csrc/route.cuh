@@ -396,7 +396,8 @@ scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int n_h
 // routes of e in this block): the stable counting sort (prefill_moe.mm:12-14 order).
 __global__ void __launch_bounds__(32)
 scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32_t *__restrict__ block_base,
-                      const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route) {
+                      const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route,
+                      int32_t *__restrict__ route_pos) {
     __shared__ int32_t run[kMaxBuckets];
     const int lane = threadIdx.x;
     for (int i = lane; i < E; i += 32) run[i] = 0;
@@ -415,7 +416,11 @@ scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32
         b = __shfl_sync(kFull, b, leader);
         __syncwarp();
         if (valid && lane == leader) run[e] = b + __popc(peers);
-        if (valid) perm_route[seg_off[e] + block_base[(size_t)blockIdx.x * E + e] + b + rank] = r;
+        if (valid) {
+            const int pos = seg_off[e] + block_base[(size_t)blockIdx.x * E + e] + b + rank;
+            perm_route[pos] = r;
+            route_pos[r] = pos;  // inverse permutation: where route r's expert row is stored
+        }
         __syncwarp();
     }
 }
@@ -453,8 +458,10 @@ permute_rows_kernel(const uint16_t *__restrict__ src, const int32_t *__restrict_
 // ------------------------------------------------------------------ combine
 //
 // out[t] = sigmoid(gate_t) * shared[t] + sum_j p[t,j] * y[8t+j]   (Qwen36Model.cs:242-244),
-// f32 arithmetic in that order, rounded once to bf16. 8 columns per thread.
-__global__ void combine_kernel(const uint16_t *__restrict__ y, const uint16_t *__restrict__ ys,
+// f32 arithmetic in that order, rounded once to bf16. 8 columns per thread. The expert rows are
+// stored in expert order: route r's row is yp[route_pos[r]], the shared rows follow in ys.
+__global__ void combine_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__ route_pos,
+                               const uint16_t *__restrict__ ys,
                                const float *__restrict__ gate_logit, const float *__restrict__ probs, int T, int D,
                                uint16_t *__restrict__ out, float *__restrict__ resid,
                                const uint32_t *__restrict__ err) {
@@ -474,7 +481,7 @@ __global__ void combine_kernel(const uint16_t *__restrict__ y, const uint16_t *_
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
         const float p = probs[(size_t)t * 8 + s];
-        uint4 v = *reinterpret_cast<const uint4 *>(y + ((size_t)t * 8 + s) * D + c);
+        uint4 v = *reinterpret_cast<const uint4 *>(yp + (size_t)route_pos[(size_t)t * 8 + s] * D + c);
         uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
