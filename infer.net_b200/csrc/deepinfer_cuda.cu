@@ -389,9 +389,12 @@ void stage_mark(Context *c, int s) { CK(cudaEventRecord(g_marks ? g_marks[s] : c
 // optional. forced: ids holds input routes. Returns nothing; errors surface via d_err.
 // Stack mode (decode path only): `x` is the bf16 scratch row that decode_route_kernel fills from
 // the f32 residual `resid` normalised by `norm_w`; otherwise `x` is the block input.
+// Grouped stacks: next_norm (the next layer's RMSNorm weights) makes the combine also write the
+// next layer's input row to next_h (and next_trace).
 void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_t *y, float *resid,
                    const int32_t *forced_ids, float *probs_out, bool gemv, BlockBuffers &b, bool profile,
-                   const float *norm_w = nullptr, float eps = 0.f, uint16_t *h_trace = nullptr) {
+                   const float *norm_w = nullptr, float eps = 0.f, uint16_t *h_trace = nullptr,
+                   const float *next_norm = nullptr, uint16_t *next_h = nullptr, uint16_t *next_trace = nullptr) {
     const int E = L->E, D = L->D, I = L->I;
     cudaStream_t st = c->stream;
     const QView R = L->m[0]->view(), G = L->m[1]->view(), U = L->m[2]->view(), Dn = L->m[3]->view();
@@ -491,8 +494,11 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
                                                  b.tiles, b.n_tiles, 8 * T, 0, I, D, E, b.yr, 9 * T, c->d_err),
                                   L->bits, grid, st);
     if (profile) stage_mark(c, S_COMBINE);
-    // 7. combine
-    {
+    // 7. combine (stacks: fused with the residual update and the next layer's RMSNorm)
+    if (resid && !y) {
+        combine_norm_kernel<<<T, 256, 0, st>>>(b.yr, b.route_pos, b.ys, b.gate, probs, D, resid, next_norm, eps, next_h,
+                                               next_trace, c->d_err);
+    } else {
         const size_t n = (size_t)T * (D / 8);
         combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(b.yr, b.route_pos, b.ys, b.gate, probs, T, D, y, resid,
                                                                      c->d_err);
@@ -1209,8 +1215,12 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
                     enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, true, b, profile, dn + (size_t)l * D, eps,
                                   trace_l);
                 } else {
-                    rmsnorm_kernel<<<T, 256, 0, c->stream>>>(dx, dn + (size_t)l * D, D, eps, dh, trace_l);
-                    enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, false, b, profile);
+                    // layer l's RMSNorm runs in layer l-1's combine; the first one on its own
+                    if (l == 0) rmsnorm_kernel<<<T, 256, 0, c->stream>>>(dx, dn, D, eps, dh, trace_l);
+                    const bool more = l + 1 < n_layers;
+                    enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, false, b, profile, nullptr, eps, nullptr,
+                                  more ? dn + (size_t)(l + 1) * D : nullptr, more ? dh : nullptr,
+                                  more && dht ? dht + (size_t)(l + 1) * T * D : nullptr);
                 }
                 g_marks = nullptr;
                 if (dit)

@@ -425,6 +425,89 @@ scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32
     }
 }
 
+// ------------------------------------------------------------------ combine + next RMSNorm
+//
+// Stacked layers: one CTA (256 threads) per token. resid[t] += out[t] with out the combine
+// above (same f32 expression and order per column), then -- when the next layer's norm weights
+// are given -- h[t] = bf16(resid[t] * rsqrt(mean(resid[t]^2) + eps) * w) (gpu_graph.mm:48-61)
+// from the updated row still in registers, so the next layer's RMSNorm costs no extra pass.
+// D % 8 == 0 and D <= 8192.
+__global__ void __launch_bounds__(256)
+combine_norm_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__ route_pos,
+                    const uint16_t *__restrict__ ys, const float *__restrict__ gate_logit,
+                    const float *__restrict__ probs, int D, float *__restrict__ resid,
+                    const float *__restrict__ norm_w, float eps, uint16_t *__restrict__ h,
+                    uint16_t *__restrict__ h_trace, const uint32_t *__restrict__ err) {
+    __shared__ float part[8];
+    if (*err) return;  // a failed call leaves the residual untouched
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float g = sigmoid_ref(gate_logit[t]);
+    float pr[8];
+    int32_t pos[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        pr[s] = probs[(size_t)t * 8 + s];
+        pos[s] = route_pos[(size_t)t * 8 + s];
+    }
+    float r[4][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int c = (tid + k * 256) * 8;
+        if (c >= D) break;
+        float o[8];
+        {
+            const uint4 v = *reinterpret_cast<const uint4 *>(ys + (size_t)t * D + c);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = ((j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1])) * g;
+        }
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(yp + (size_t)pos[s] * D + c);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float prod = pr[s] * ((j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]));
+                o[j] = o[j] + prod;
+            }
+        }
+        float4 *rp = reinterpret_cast<float4 *>(resid + (size_t)t * D + c);
+        float4 a = rp[0], b = rp[1];
+        a.x += o[0]; a.y += o[1]; a.z += o[2]; a.w += o[3];
+        b.x += o[4]; b.y += o[5]; b.z += o[6]; b.w += o[7];
+        rp[0] = a;
+        rp[1] = b;
+        r[k][0] = a.x; r[k][1] = a.y; r[k][2] = a.z; r[k][3] = a.w;
+        r[k][4] = b.x; r[k][5] = b.y; r[k][6] = b.z; r[k][7] = b.w;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(r[k][j], r[k][j], ss);
+    }
+    if (!norm_w) return;
+#pragma unroll
+    for (int n = 16; n; n >>= 1) ss += __shfl_xor_sync(kFull, ss, n);
+    if ((tid & 31) == 0) part[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += part[i];
+    const float scale = 1.0f / sqrtf(tot / (float)D + eps);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int c = (tid + k * 256) * 8;
+        if (c >= D) break;
+        const float4 w0 = *reinterpret_cast<const float4 *>(norm_w + c), w1 = *reinterpret_cast<const float4 *>(norm_w + c + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint4 o;
+        o.x = (uint32_t)f32_to_bf16_bits(r[k][0] * scale * wv[0]) | ((uint32_t)f32_to_bf16_bits(r[k][1] * scale * wv[1]) << 16);
+        o.y = (uint32_t)f32_to_bf16_bits(r[k][2] * scale * wv[2]) | ((uint32_t)f32_to_bf16_bits(r[k][3] * scale * wv[3]) << 16);
+        o.z = (uint32_t)f32_to_bf16_bits(r[k][4] * scale * wv[4]) | ((uint32_t)f32_to_bf16_bits(r[k][5] * scale * wv[5]) << 16);
+        o.w = (uint32_t)f32_to_bf16_bits(r[k][6] * scale * wv[6]) | ((uint32_t)f32_to_bf16_bits(r[k][7] * scale * wv[7]) << 16);
+        *reinterpret_cast<uint4 *>(h + (size_t)t * D + c) = o;
+        if (h_trace) *reinterpret_cast<uint4 *>(h_trace + (size_t)t * D + c) = o;
+    }
+}
+
 // ------------------------------------------------------------------ permuted token rows
 //
 // xp[pos] = src[perm_route[pos] / 8] for the routed positions pos < *count (expert order), so
