@@ -53,7 +53,15 @@ decode_route_kernel(const float *__restrict__ x, const float *__restrict__ norm_
     __shared__ int last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int E = R.rows, row = blockIdx.x * 8 + warp;
-    if (lane == 0 && row < E) prefetch_qrow(R, (size_t)row);
+    // weights do not depend on the previous kernel: load them before waiting for it
+    const bool pre = D <= 2048;
+    RouterRaw rr, sr;
+    if (pre) {
+        if (row < E) router_raw_load(R, row, D, rr);
+        if (warp == 0) router_raw_load(SR, 0, D, sr);
+    } else if (lane == 0 && row < E) {
+        prefetch_qrow(R, (size_t)row);
+    }
     grid_dep_wait();
     if (x) {
         for (int t = 0; t < T; ++t) {
@@ -87,7 +95,7 @@ decode_route_kernel(const float *__restrict__ x, const float *__restrict__ norm_
     if (row < E) {
         const float bb = bias ? bias[row] : 0.f;
         for (int t = 0; t < T; ++t) {
-            const float v = canonical_dot_warp(R, row, hs + t * D, D);
+            const float v = pre ? router_raw_dot(rr, hs + t * D, D) : canonical_dot_warp(R, row, hs + t * D, D);
             if (lane == 0) logits[(size_t)t * E + row] = v + bb;
         }
     }
@@ -98,6 +106,11 @@ decode_route_kernel(const float *__restrict__ x, const float *__restrict__ norm_
     __syncthreads();
     if (!last) return;
     __threadfence();
+    if (pre && T > 1)  // the shared gate row preloaded by warp 0 goes to every warp
+        for (int k = 0; k < 8; ++k) {
+            sr.q[k].x = __shfl_sync(kFull, sr.q[k].x, lane);
+            sr.q[k].y = __shfl_sync(kFull, sr.q[k].y, lane);
+        }
     for (int t = warp; t < T; t += 8) {
         float v[8];
         bool nonfinite = false;
@@ -122,7 +135,7 @@ decode_route_kernel(const float *__restrict__ x, const float *__restrict__ norm_
             p[n] = expf(chosen[n] - mx);
             sum += p[n];
         }
-        const float g = canonical_dot_warp(SR, 0, hs + t * D, D);
+        const float g = (pre && warp == 0) ? router_raw_dot(sr, hs + t * D, D) : canonical_dot_warp(SR, 0, hs + t * D, D);
         if (lane < 8) {
             float pv = 0.f;
             int32_t sv = 0;
@@ -162,15 +175,32 @@ decode_gate_up_kernel(const uint16_t *__restrict__ h, int T, int D, int I, QView
     const QView G = shared ? sg : g, U = shared ? su : u;
     const size_t row = (size_t)(shared ? 0 : ids[(size_t)t * 8 + j]) * I + i;
     float ga = 0.f, ua = 0.f;
-    for (int c = lane_id(); c < D / 16; c += 32) {
-        float wg[16], wu[16], xv[16];
-        load_weights16<BITS>(G, row, c, wg);
-        load_weights16<BITS>(U, row, c, wu);
-        load_x16_bf16(xs, c, xv);
+    // the raw chunks of up to 4 x 32 columns-of-16 per pass are all requested before use
+    constexpr int MAXC = 4;
+    const int nc = D / 16;
+    for (int c0 = lane_id(); c0 < nc; c0 += 32 * MAXC) {
+        RawChunk<BITS> rg[MAXC], ru[MAXC];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            ga = fmaf(wg[k], xv[k], ga);
-            ua = fmaf(wu[k], xv[k], ua);
+        for (int k = 0; k < MAXC; ++k) {
+            const int c = c0 + 32 * k;
+            if (c < nc) {
+                rg[k] = load_chunk<BITS>(G, row, c);
+                ru[k] = load_chunk<BITS>(U, row, c);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < MAXC; ++k) {
+            const int c = c0 + 32 * k;
+            if (c >= nc) break;
+            float wg[16], wu[16], xv[16];
+            chunk_weights<BITS>(rg[k], c, wg);
+            chunk_weights<BITS>(ru[k], c, wu);
+            load_x16_bf16(xs, c, xv);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                ga = fmaf(wg[e], xv[e], ga);
+                ua = fmaf(wu[e], xv[e], ua);
+            }
         }
     }
     ga = warp_sum_butterfly(ga);
@@ -191,36 +221,45 @@ decode_down_kernel(const float *__restrict__ act, int T, int D, int I, QView dn,
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = lane_id();
     const bool live = warp < T * D;
     const int t = live ? warp / D : 0, d = live ? warp % D : 0;
-    if (live && lane < 9) {
-        const int e = lane < 8 ? min(max(ids[(size_t)t * 8 + lane], 0), dn.experts - 1) : 0;
-        prefetch_qrow(lane < 8 ? dn : sd, (size_t)e * D + d);
+    float y[9], acc[9];
+    int row[9];  // expert * D + d (< 2^31)
+#pragma unroll
+    for (int j = 0; j < 9; ++j) {
+        acc[j] = 0.f;
+        row[j] = (j == 8 ? 0 : min(max(ids[(size_t)t * 8 + j], 0), dn.experts - 1)) * D + d;
     }
+    // The weights do not depend on the gate/up kernel: the first chunk of each of the 9 rows is
+    // loaded before waiting for it (the ids are final: the route kernel completed before the
+    // gate/up kernel released this launch).
+    const int nc = I / 16;
+    RawChunk<BITS> raw[9];
+    if (live && lane < nc)
+#pragma unroll
+        for (int j = 0; j < 9; ++j) raw[j] = load_chunk<BITS>(j == 8 ? sd : dn, row[j], lane);
     grid_dep_wait();
     grid_dep_launch();
     if (!live) return;
-    float y[9];
+    for (int c = lane; c < nc; c += 32) {
+        if (c != lane)
 #pragma unroll
-    for (int j = 0; j < 9; ++j) {
-        const bool shared = j == 8;
-        const QView M = shared ? sd : dn;
-        const size_t row = (size_t)(shared ? 0 : ids[(size_t)t * 8 + j]) * D + d;
-        const float *a = act + ((size_t)t * 9 + j) * I;
-        float acc = 0.f;
-        for (int c = lane; c < I / 16; c += 32) {
+            for (int j = 0; j < 9; ++j) raw[j] = load_chunk<BITS>(j == 8 ? sd : dn, row[j], c);
+#pragma unroll
+        for (int j = 0; j < 9; ++j) {
             float w[16];
-            load_weights16<BITS>(M, row, c, w);
-            const float4 *ap = reinterpret_cast<const float4 *>(a + c * 16);
+            chunk_weights<BITS>(raw[j], c, w);
+            const float4 *ap = reinterpret_cast<const float4 *>(act + ((size_t)t * 9 + j) * I + c * 16);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const float4 av = ap[k];
-                acc = fmaf(w[4 * k], av.x, acc);
-                acc = fmaf(w[4 * k + 1], av.y, acc);
-                acc = fmaf(w[4 * k + 2], av.z, acc);
-                acc = fmaf(w[4 * k + 3], av.w, acc);
+                acc[j] = fmaf(w[4 * k], av.x, acc[j]);
+                acc[j] = fmaf(w[4 * k + 1], av.y, acc[j]);
+                acc[j] = fmaf(w[4 * k + 2], av.z, acc[j]);
+                acc[j] = fmaf(w[4 * k + 3], av.w, acc[j]);
             }
         }
-        y[j] = warp_sum_butterfly(acc);
     }
+#pragma unroll
+    for (int j = 0; j < 9; ++j) y[j] = warp_sum_butterfly(acc[j]);
     if (lane == 0) {
         if (*err) return;
         float o = y[8] * sigmoid_ref(gate_logit[t]);

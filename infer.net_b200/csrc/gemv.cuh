@@ -62,21 +62,39 @@ __global__ void quant_gate_up_kernel(QView g, QView u, const float *__restrict__
 
 // ------------------------------------------------------------------ decode block path
 //
-// 16 codes of row chunk c (columns 16c .. 16c+15) as f32 weights.
+// 16 codes of row chunk c (columns 16c .. 16c+15): the raw words (loaded first, so that many
+// chunks are in flight) and their f32 weights w = fma(q, scale, bias).
 template <int BITS>
-__device__ __forceinline__ void load_weights16(const QView &m, size_t row, int c, float *w) {
+struct RawChunk {
+    uint32_t q[BITS == 8 ? 4 : 3];
+    uint16_t s, b;
+};
+template <int BITS>
+__device__ __forceinline__ RawChunk<BITS> load_chunk(const QView &m, size_t row, int c) {
+    RawChunk<BITS> r;
     const uint32_t *rw = m.packed + row * m.words_per_row();
-    const float s = bf16_bits_to_f32(__ldg(m.scales + row * m.groups_per_row() + (c >> 2)));
-    const float b = bf16_bits_to_f32(__ldg(m.biases + row * m.groups_per_row() + (c >> 2)));
+    r.s = __ldg(m.scales + row * m.groups_per_row() + (c >> 2));
+    r.b = __ldg(m.biases + row * m.groups_per_row() + (c >> 2));
     if constexpr (BITS == 8) {
-        uint4 q = ldg_nc_v4(rw + c * 4);
-        uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = fmaf(byte_to_f32(qw[i >> 2], i & 3), s, b);
+        const uint4 q = ldg_nc_v4(rw + c * 4);
+        r.q[0] = q.x; r.q[1] = q.y; r.q[2] = q.z; r.q[3] = q.w;
     } else {
         // 80 bits starting at bit 80c: words 5c/2 .. +2, offset 0 or 16
         const int w0 = (5 * c) >> 1;
-        uint32_t a = ldg_nc_u32(rw + w0), bb = ldg_nc_u32(rw + w0 + 1), cc = ldg_nc_u32(rw + w0 + 2);
+        r.q[0] = ldg_nc_u32(rw + w0);
+        r.q[1] = ldg_nc_u32(rw + w0 + 1);
+        r.q[2] = ldg_nc_u32(rw + w0 + 2);
+    }
+    return r;
+}
+template <int BITS>
+__device__ __forceinline__ void chunk_weights(const RawChunk<BITS> &r, int c, float *w) {
+    const float s = bf16_bits_to_f32(r.s), b = bf16_bits_to_f32(r.b);
+    if constexpr (BITS == 8) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = fmaf(byte_to_f32(r.q[i >> 2], i & 3), s, b);
+    } else {
+        uint32_t a = r.q[0], bb = r.q[1], cc = r.q[2];
         if (c & 1) {
             a = __funnelshift_r(a, bb, 16);
             bb = __funnelshift_r(bb, cc, 16);
@@ -90,6 +108,10 @@ __device__ __forceinline__ void load_weights16(const QView &m, size_t row, int c
             w[i] = fmaf(code_to_f32(q & 31u), s, b);
         }
     }
+}
+template <int BITS>
+__device__ __forceinline__ void load_weights16(const QView &m, size_t row, int c, float *w) {
+    chunk_weights<BITS>(load_chunk<BITS>(m, row, c), c, w);
 }
 
 __device__ __forceinline__ void load_x16_bf16(const uint16_t *x, int c, float *v) {

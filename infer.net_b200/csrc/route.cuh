@@ -24,24 +24,85 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
+// Raw codes, scales and biases of one lane's columns of an 8-bit router row, up to 8 column
+// blocks of 256 (D <= 2048), loaded ahead of the activation row they will meet.
+struct RouterRaw {
+    uint2 q[8];
+    uint16_t s[8], b[8];
+};
+__device__ __forceinline__ void router_raw_load(const QView &m, int row, int D, RouterRaw &r) {
+    const uint32_t lane = lane_id();
+    const uint32_t *w = m.packed + (size_t)row * m.words_per_row();
+    const uint16_t *sc = m.scales + (size_t)row * m.groups_per_row();
+    const uint16_t *bi = m.biases + (size_t)row * m.groups_per_row();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int base = k * 256 + lane * 8;
+        if (base < D) {
+            r.q[k] = __ldg(reinterpret_cast<const uint2 *>(w + base / 4));
+            r.s[k] = __ldg(sc + base / 64);
+            r.b[k] = __ldg(bi + base / 64);
+        }
+    }
+}
+// The canonical dot product (below) of a preloaded row with x (shared or global memory).
+__device__ __forceinline__ float router_raw_dot(const RouterRaw &r, const uint16_t *x, int D) {
+    const uint32_t lane = lane_id();
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int base = k * 256 + lane * 8;
+        if (base >= D) break;
+        const uint4 xv = *reinterpret_cast<const uint4 *>(x + base);
+        const float s = bf16_bits_to_f32(r.s[k]), bb = bf16_bits_to_f32(r.b[k]);
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float wv = fmaf(byte_to_f32(j < 4 ? r.q[k].x : r.q[k].y, j & 3), s, bb);
+            const float xf = (j & 1) ? bf16_hi(xw[j >> 1]) : bf16_lo(xw[j >> 1]);
+            acc = fmaf(wv, xf, acc);
+        }
+    }
+    return warp_sum_butterfly(acc);
+}
+
 // Canonical dot product of one 8-bit router row with one bf16 activation row (in global or
-// shared memory), evaluated by a whole warp; returns the same value in every lane.
+// shared memory), evaluated by a whole warp; returns the same value in every lane. The codes,
+// scales and biases of up to 8 column blocks are requested before any of them is used (one
+// memory round trip per 2048 columns instead of one per block); the arithmetic order is the
+// canonical one.
 __device__ __forceinline__ float canonical_dot_warp(const QView &m, int row, const uint16_t *x, int D) {
     const uint32_t lane = lane_id();
     const uint32_t *w = m.packed + (size_t)row * m.words_per_row();
     const uint16_t *sc = m.scales + (size_t)row * m.groups_per_row();
     const uint16_t *bi = m.biases + (size_t)row * m.groups_per_row();
+    const int nb = D / 256;
     float acc = 0.0f;
-    for (int base = lane * 8; base < D; base += 256) {
-        uint2 q = __ldg(reinterpret_cast<const uint2 *>(w + base / 4));
-        const uint4 xv = *reinterpret_cast<const uint4 *>(x + base);  // x may be shared or global
-        float s = bf16_bits_to_f32(__ldg(sc + base / 64)), b = bf16_bits_to_f32(__ldg(bi + base / 64));
-        uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    for (int b0 = 0; b0 < nb; b0 += 8) {
+        uint2 q[8];
+        uint16_t sv[8], bv[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float wv = fmaf(byte_to_f32(j < 4 ? q.x : q.y, j & 3), s, b);
-            float xf = (j & 1) ? bf16_hi(xw[j >> 1]) : bf16_lo(xw[j >> 1]);
-            acc = fmaf(wv, xf, acc);
+        for (int k = 0; k < 8; ++k) {
+            const int base = (b0 + k) * 256 + lane * 8;
+            if (b0 + k < nb) {
+                q[k] = __ldg(reinterpret_cast<const uint2 *>(w + base / 4));
+                sv[k] = __ldg(sc + base / 64);
+                bv[k] = __ldg(bi + base / 64);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (b0 + k >= nb) break;
+            const int base = (b0 + k) * 256 + lane * 8;
+            const uint4 xv = *reinterpret_cast<const uint4 *>(x + base);  // x may be shared or global
+            const float s = bf16_bits_to_f32(sv[k]), bb = bf16_bits_to_f32(bv[k]);
+            const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float wv = fmaf(byte_to_f32(j < 4 ? q[k].x : q[k].y, j & 3), s, bb);
+                const float xf = (j & 1) ? bf16_hi(xw[j >> 1]) : bf16_lo(xw[j >> 1]);
+                acc = fmaf(wv, xf, acc);
+            }
         }
     }
     return warp_sum_butterfly(acc);
