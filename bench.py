@@ -46,6 +46,19 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
+def profiled_traffic():
+    """DRAM bytes (read + write) per launch of the 8K-token gate/up kernel, from the committed ncu
+    summary (profiles/grouped_gemm_gate_up_8k.md); None when absent."""
+    import re
+    path = os.path.join(ROOT, "profiles", "grouped_gemm_gate_up_8k.md")
+    try:
+        with open(path) as f:
+            m = re.search(r"traffic per launch \(read \+ write\) \| ([0-9.]+) MB", f.read())
+        return float(m.group(1)) * 1e6 if m else None
+    except OSError:
+        return None
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
 
@@ -210,7 +223,9 @@ def run_ours(args):
         "roofline": {"kernel": "grouped_gemm<gate_up,8bit>", "bound": "tensor", "achieved": achieved,
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
-                     "traffic": None, "peak_source": pk["source"] + " sustained bf16"},
+                     "traffic": profiled_traffic() if TOKENS == 8192 else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 8K-token launch",
+                     "peak_source": pk["source"] + " sustained bf16"},
         "stage_ms_per_step": {k: v / args.steps for k, v in stage_tot.items()},
         "cpu_baseline": cpu,
         "e2e": None if e2e is None else {
