@@ -274,3 +274,233 @@ decode_down_kernel(const float *__restrict__ act, int T, int D, int I, QView dn,
 }
 
 }  // namespace di
+
+namespace di {
+
+// ------------------------------------------------------------------ fused decode FFN (T = 1)
+//
+// gate/up + SwiGLU + down + combine of one token in one kernel of one CTA per SM (16 warps).
+// Phase 1: the CTA bulk-copies its share of the 9 experts' weight rows -- (gate, up) row pairs p in
+// [c*9I/G, (c+1)*9I/G) and the 9 down rows of the outputs d in [c*D/G, (c+1)*D/G) -- into shared
+// memory, so the layer's whole weight stream is in flight at once (the shared expert's rows before
+// the route kernel has finished, the routed rows once its ids are known). The rows of one expert
+// in a CTA's share are consecutive in HBM, so each field (codes, scales, biases) of each expert is
+// one copy. One warp issues them, gate/up before down, so the gate/up rows land first and phase 2
+// runs while the down rows stream in. Phase 2: act = silu(gate . h) * (up . h) of its pairs
+// (quantized.mm:148-189). A grid barrier (all CTAs are resident: one CTA per SM). Phase 3: act is
+// staged once in the gate/up region; out[d] = sigmoid(gate_logit) * (shared_down[d] . act_s) +
+// sum_j p_j * (down_j[d] . act_j) (Qwen36Model.cs:242-244), one warp per output with the combine
+// weights folded into the lanes' partial sums, resid += out. Needs D % 512 == 0 and I % 512 == 0
+// (16-byte rows of scales) and the layout below to fit in shared memory.
+// Shared memory, field-major: gate/up region = gate codes [pairs][gu_row], up codes, gate scales
+// [pairs][gu_grp], gate biases, up scales, up biases; down region = codes [9][outs][dn_row], scales
+// [9][outs][dn_grp], biases.
+constexpr int kFfnThreads = 512;
+struct FfnLayout {
+    int pairs, outs;                     // per CTA (upper bounds)
+    int gu_row, gu_grp, dn_row, dn_grp;  // bytes of a code row / of a scale or bias row
+    int gu_off, dn_off, bar_off, total;
+    __host__ __device__ int gu_code(int m) const { return gu_off + m * pairs * gu_row; }             // m: 0 gate, 1 up
+    __host__ __device__ int gu_sb(int m, int k) const { return gu_off + 2 * pairs * gu_row + (2 * m + k) * pairs * gu_grp; }
+    __host__ __device__ int dn_code() const { return dn_off; }
+    __host__ __device__ int dn_sb(int k) const { return dn_off + 9 * outs * dn_row + k * 9 * outs * dn_grp; }
+};
+__host__ __device__ inline FfnLayout ffn_layout(int D, int I, int bits, int grid) {
+    FfnLayout f;
+    f.pairs = (9 * I + grid - 1) / grid;
+    f.outs = (D + grid - 1) / grid;
+    f.gu_row = D * bits / 8;
+    f.gu_grp = D / 64 * 2;
+    f.dn_row = I * bits / 8;
+    f.dn_grp = I / 64 * 2;
+    f.gu_off = (D * 2 + 127) & ~127;
+    // the gate/up region also holds act [9][I] f32 and the 9 combine weights in phase 3
+    const int gu_bytes = max(2 * f.pairs * (f.gu_row + 2 * f.gu_grp), 9 * I * 4 + 64);
+    f.dn_off = f.gu_off + ((gu_bytes + 127) & ~127);
+    f.bar_off = f.dn_off + ((9 * f.outs * (f.dn_row + 2 * f.dn_grp) + 127) & ~127);
+    f.total = f.bar_off + 64;
+    return f;
+}
+
+// mbarrier.expect_tx without an arrival (registers bytes of copies issued before the arrival)
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// 16 weights of chunk c of a code row held in shared memory (scale / bias rows beside it).
+template <int BITS>
+__device__ __forceinline__ void smem_chunk_weights(const uint8_t *codes, const uint16_t *sc, const uint16_t *bi, int c,
+                                                   float *w) {
+    RawChunk<BITS> r;
+    r.s = sc[c >> 2];
+    r.b = bi[c >> 2];
+    if constexpr (BITS == 8) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(codes + c * 16);
+        r.q[0] = q.x; r.q[1] = q.y; r.q[2] = q.z; r.q[3] = q.w;
+    } else {
+        const uint32_t *wd = reinterpret_cast<const uint32_t *>(codes) + ((5 * c) >> 1);
+        r.q[0] = wd[0]; r.q[1] = wd[1]; r.q[2] = wd[2];
+    }
+    chunk_weights<BITS>(r, c, w);
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kFfnThreads, 1)
+decode_ffn_kernel(const uint16_t *__restrict__ h, int D, int I, QView g, QView u, QView sg, QView su, QView dn, QView sd,
+                  const int32_t *__restrict__ ids, const float *__restrict__ probs, const float *__restrict__ gate_logit,
+                  float *__restrict__ act, uint16_t *__restrict__ out, float *__restrict__ resid,
+                  uint32_t *__restrict__ grid_ctr, uint32_t gen, uint32_t *__restrict__ err) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const FfnLayout f = ffn_layout(D, I, BITS, gridDim.x);
+    uint16_t *xs = reinterpret_cast<uint16_t *>(sm);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + f.bar_off);  // [0] gate/up rows, [1] down rows
+    int32_t *ids_s = reinterpret_cast<int32_t *>(sm + f.bar_off + 16);  // the 8 routed expert ids
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    const int P = 9 * I, p_lo = (int)((long long)blockIdx.x * P / gridDim.x),
+              p_hi = (int)((long long)(blockIdx.x + 1) * P / gridDim.x);
+    const int d_lo = (int)((long long)blockIdx.x * D / gridDim.x), d_hi = (int)((long long)(blockIdx.x + 1) * D / gridDim.x);
+    const int np = p_hi - p_lo, nd = d_hi - d_lo;
+    const int j_lo = p_lo / I, j_hi = (p_hi - 1) / I, nseg = np > 0 ? j_hi - j_lo + 1 : 0;
+    // Copies of the CTA's share, one per field of each expert segment: gate/up segments are the
+    // pairs of one expert slot j (rows e_j*I + i0 .. i1), down segments are one expert's rows
+    // e_j*D + d_lo .. d_hi. Copy k < nseg*6 is a gate/up field, the rest down fields; `routed`
+    // selects the copies of routed experts (their ids come from ids_s).
+    auto issue_copy = [&](int k, bool routed) {
+        if (k < nseg * 6) {
+            const int sg_ = k / 6, field = k % 6, j = j_lo + sg_;
+            if ((j < 8) != routed) return;
+            const int i0 = j == j_lo ? p_lo % I : 0, i1 = j == j_hi ? (p_hi - 1) % I + 1 : I;
+            const int q0 = j * I + i0 - p_lo, cnt = i1 - i0;
+            const int e = j < 8 ? ids_s[j] : 0;
+            const int m = field & 1, kind = field >> 1;  // m: gate / up; kind: codes, scales, biases
+            const QView &W = m ? (j < 8 ? u : su) : (j < 8 ? g : sg);
+            const size_t row = (size_t)e * I + i0;
+            if (kind == 0)
+                bulk_load(sm + f.gu_code(m) + q0 * f.gu_row, reinterpret_cast<const uint8_t *>(W.packed) + row * f.gu_row,
+                          (uint32_t)cnt * f.gu_row, &bar[0]);
+            else
+                bulk_load(sm + f.gu_sb(m, kind - 1) + q0 * f.gu_grp, (kind == 1 ? W.scales : W.biases) + row * (f.gu_grp / 2),
+                          (uint32_t)cnt * f.gu_grp, &bar[0]);
+        } else {
+            const int kk = k - nseg * 6, j = kk / 3, kind = kk % 3;
+            if ((j < 8) != routed || nd == 0) return;
+            const int e = j < 8 ? ids_s[j] : 0;
+            const QView &W = j < 8 ? dn : sd;
+            const size_t row = (size_t)e * D + d_lo;
+            if (kind == 0)
+                bulk_load(sm + f.dn_code() + j * f.outs * f.dn_row, reinterpret_cast<const uint8_t *>(W.packed) + row * f.dn_row,
+                          (uint32_t)nd * f.dn_row, &bar[1]);
+            else
+                bulk_load(sm + f.dn_sb(kind - 1) + j * f.outs * f.dn_grp, (kind == 1 ? W.scales : W.biases) + row * (f.dn_grp / 2),
+                          (uint32_t)nd * f.dn_grp, &bar[1]);
+        }
+    };
+    const int ncopies = nseg * 6 + 27;
+    // the barriers expect the whole share's bytes up front; the shared expert's rows do not depend
+    // on the route kernel and are requested before waiting for it
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbarrier_init();
+        mbar_arrive_expect_tx(&bar[0], (uint32_t)np * 2 * (f.gu_row + 2 * f.gu_grp));
+        mbar_arrive_expect_tx(&bar[1], (uint32_t)(9 * nd * (f.dn_row + 2 * f.dn_grp)));
+    }
+    __syncthreads();
+    if (warp == 0)
+        for (int k = lane; k < ncopies; k += 32) issue_copy(k, false);
+    grid_dep_wait();  // the route kernel has written h, ids, probs and the gate logit
+    if (tid < 8) ids_s[tid] = min(max(ids[tid], 0), g.experts - 1);
+    for (int k = tid; k < D / 8; k += blockDim.x) reinterpret_cast<uint4 *>(xs)[k] = reinterpret_cast<const uint4 *>(h)[k];
+    __syncthreads();
+    if (warp == 0)  // in lane order: gate/up copies (k < nseg*6) are requested before the down copies
+        for (int k = lane; k < ncopies; k += 32) issue_copy(k, true);
+    bool ok = mbar_wait(&bar[0], 0, err, kErrTimeout);
+    // ---- phase 2: the CTA's (gate, up) pairs
+    if (ok)
+        for (int q = warp; q < np; q += nw) {
+            const int p = p_lo + q, j = p / I, i = p % I;
+            const uint8_t *gc = sm + f.gu_code(0) + q * f.gu_row, *uc = sm + f.gu_code(1) + q * f.gu_row;
+            const uint16_t *gs = reinterpret_cast<const uint16_t *>(sm + f.gu_sb(0, 0) + q * f.gu_grp);
+            const uint16_t *gb = reinterpret_cast<const uint16_t *>(sm + f.gu_sb(0, 1) + q * f.gu_grp);
+            const uint16_t *us = reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 0) + q * f.gu_grp);
+            const uint16_t *ub = reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 1) + q * f.gu_grp);
+            float ga[2] = {0.f, 0.f}, ua[2] = {0.f, 0.f};
+            for (int c = lane; c < D / 16; c += 32) {
+                float wg[16], wu[16], xv[16];
+                smem_chunk_weights<BITS>(gc, gs, gb, c, wg);
+                smem_chunk_weights<BITS>(uc, us, ub, c, wu);
+                load_x16_bf16(xs, c, xv);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    ga[e & 1] = fmaf(wg[e], xv[e], ga[e & 1]);
+                    ua[e & 1] = fmaf(wu[e], xv[e], ua[e & 1]);
+                }
+            }
+            const float gsum = warp_sum_butterfly(ga[0] + ga[1]);
+            const float usum = warp_sum_butterfly(ua[0] + ua[1]);
+            if (lane == 0) act[(size_t)j * I + i] = silu_ref(gsum) * usum;
+        }
+    // ---- grid barrier: every CTA's act values are written
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(grid_ctr, 1u);
+        const uint32_t target = gen * gridDim.x;
+        const uint64_t t0 = global_ns();
+        for (uint32_t n = 0;; ++n) {
+            if (*reinterpret_cast<volatile uint32_t *>(grid_ctr) >= target) break;
+            if ((n & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+                atomicOr(err, kErrTimeout);
+                break;
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    grid_dep_launch();
+    // act of all 9 experts into the (now free) gate/up region, with the combine weights after it
+    float *acts = reinterpret_cast<float *>(sm + f.gu_off);
+    float *coef = acts + 9 * I;
+    const int cpr = I / 16;  // chunks per down row
+    // float4 q of chunk c of expert j goes to [j][q][c]: the lanes of phase 3 (consecutive c) then
+    // read consecutive float4s
+    for (int k = tid; k < 9 * I / 4; k += blockDim.x) {
+        const int j = k / (4 * cpr), rem = k - j * 4 * cpr;
+        reinterpret_cast<float4 *>(acts)[j * 4 * cpr + (rem & 3) * cpr + (rem >> 2)] =
+            __ldcg(reinterpret_cast<const float4 *>(act) + k);
+    }
+    if (tid < 9) coef[tid] = tid < 8 ? probs[tid] : sigmoid_ref(gate_logit[0]);
+    ok = mbar_wait(&bar[1], 0, err, kErrTimeout) && ok;
+    __syncthreads();
+    if (!ok || *reinterpret_cast<volatile uint32_t *>(err)) return;
+    // ---- phase 3: the CTA's outputs; lane tasks k = (expert j, chunk c) over the 9 down rows
+    for (int o = warp; o < nd; o += nw) {
+        const int d = d_lo + o;
+        float a = 0.f;
+        for (int k = lane; k < 9 * cpr; k += 32) {
+            const int j = k / cpr, c = k - j * cpr, r = j * f.outs + o;
+            float w[16];
+            smem_chunk_weights<BITS>(sm + f.dn_code() + r * f.dn_row,
+                                     reinterpret_cast<const uint16_t *>(sm + f.dn_sb(0) + r * f.dn_grp),
+                                     reinterpret_cast<const uint16_t *>(sm + f.dn_sb(1) + r * f.dn_grp), c, w);
+            const float4 *ap = reinterpret_cast<const float4 *>(acts) + j * 4 * cpr + c;
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 av = ap[q * cpr];
+                s0 = fmaf(w[4 * q], av.x, s0);
+                s1 = fmaf(w[4 * q + 1], av.y, s1);
+                s0 = fmaf(w[4 * q + 2], av.z, s0);
+                s1 = fmaf(w[4 * q + 3], av.w, s1);
+            }
+            a = fmaf(coef[j], s0 + s1, a);
+        }
+        const float r = warp_sum_butterfly(a);
+        if (lane == 0) {
+            if (out) out[d] = f32_to_bf16_bits(r);
+            if (resid) resid[d] += r;
+        }
+    }
+}
+
+}  // namespace di

@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "decode_stack.cuh"
 #include "ep.cuh"
 #include "gemv.cuh"
 #include "generate.cuh"
@@ -99,6 +100,14 @@ struct Context {
     // CUDA graph of the last decode-path stack, replayed while its key matches
     std::vector<uint64_t> graph_key;
     cudaGraphExec_t graph_exec = nullptr;
+    // persistent one-token stack kernel: exchange words + generation counter (zeroed once), and
+    // the per-layer descriptors of the last stack, re-uploaded when its key changes
+    unsigned long long *ll = nullptr;
+    size_t ll_words = 0;
+    ds::StackLayer *d_stack = nullptr;
+    size_t stack_cap = 0;
+    std::vector<ds::StackLayer> h_stack;
+    std::vector<uint64_t> stack_key;
 };
 
 std::mutex g_registry;
@@ -219,6 +228,121 @@ uint64_t eps_bits(float eps) {
     return u;
 }
 
+// The fused one-token decode FFN needs 16-byte scale rows (D, I multiples of 512) and its
+// per-CTA weight share to fit in shared memory.
+bool ffn_fits(const Context *c, const Layer *L) {
+    if (L->D % 512 || L->I % 512) return false;
+    return ffn_layout(L->D, L->I, L->bits, c->sms).total <= 227 * 1024;
+}
+
+// The persistent one-token stack kernel: layers sharing D, I, E and bits, D and I multiples of 512
+// (16-byte scale rows), D <= 2048, I <= 512 and at most 32 (gate, up) pairs per CTA (per-thread
+// register budgets), its per-CTA share in shared memory, and one CTA resident on every SM (a
+// cooperative launch).
+bool stack_fits(Context *c, void *const *layers, int n) {
+    const Layer *L0 = static_cast<const Layer *>(layers[0]);
+    for (int l = 0; l < n; ++l) {
+        const Layer *L = static_cast<const Layer *>(layers[l]);
+        if (L->D != L0->D || L->I != L0->I || L->E != L0->E || L->bits != L0->bits) return false;
+    }
+    const int D = L0->D, I = L0->I;
+    if (D % 512 || D > 2048 || I % 512 || 9 * I > ds::kMaxActWords * ds::kThreads || L0->E > 256) return false;
+    const ds::Layout f = ds::layout(D, I, L0->bits, c->sms);
+    const int smem = f.total;
+    if (smem > 227 * 1024 || f.pairs > ds::kPairsPerWarp * ds::kWarps) return false;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, L0->bits == 8 ? ds::decode_stack_kernel<8>
+                                                                             : ds::decode_stack_kernel<5>,
+                                                      ds::kThreads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return per_sm >= 1;
+}
+
+// Enqueue the persistent stack kernel for one token: x (f32 [D]) is updated in place; h_trace /
+// ids_trace (device, optional) receive every layer's normalised input row and expert ids.
+void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, float eps, float *x, uint16_t *h_trace,
+                   int32_t *ids_trace) {
+    const Layer *L0 = static_cast<const Layer *>(layers[0]);
+    const int D = L0->D, I = L0->I, E = L0->E;
+    // exchange words: [0] the generation counter and the x arrivals, [1] the act arrivals, then
+    // x [D], act [9 I], logits [E + 1]
+    const size_t words = 2 + (size_t)D + 9 * (size_t)I + E + 1;
+    if (c->ll_words < words) {
+        if (c->ll) CK(cudaFree(c->ll));
+        c->ll = nullptr;
+        c->ll_words = 0;
+        CK(cudaMalloc(&c->ll, words * 8));
+        CK(cudaMemsetAsync(c->ll, 0, words * 8, c->stream));  // generation 0 matches no exchange
+        c->ll_words = words;
+    }
+    std::vector<uint64_t> key = {(uint64_t)n, (uint64_t)(uintptr_t)norms};
+    for (int l = 0; l < n; ++l) {
+        const Layer *L = static_cast<const Layer *>(layers[l]);
+        key.push_back(L->gen);
+        key.push_back((uint64_t)(uintptr_t)L->bias);
+    }
+    if (key != c->stack_key) {
+        c->h_stack.resize(n);
+        for (int l = 0; l < n; ++l) {
+            const Layer *L = static_cast<const Layer *>(layers[l]);
+            ds::StackLayer &s = c->h_stack[l];
+            s.R = L->m[0]->view();
+            s.G = L->m[1]->view();
+            s.U = L->m[2]->view();
+            s.Dn = L->m[3]->view();
+            s.SG = L->m[4]->view();
+            s.SU = L->m[5]->view();
+            s.SD = L->m[6]->view();
+            s.SR = L->m[7]->view();
+            s.bias = L->bias;
+            s.norm = norms + (size_t)l * D;
+        }
+        if (c->stack_cap < (size_t)n) {
+            if (c->d_stack) CK(cudaFree(c->d_stack));
+            c->d_stack = nullptr;
+            c->stack_cap = 0;
+            CK(cudaMalloc(&c->d_stack, (size_t)n * sizeof(ds::StackLayer)));
+            c->stack_cap = n;
+        }
+        CK(cudaMemcpyAsync(c->d_stack, c->h_stack.data(), (size_t)n * sizeof(ds::StackLayer), cudaMemcpyHostToDevice,
+                           c->stream));
+        c->stack_key = key;
+    }
+    ds::StackParams sp;
+    sp.layers = c->d_stack;
+    sp.n_layers = n;
+    sp.D = D;
+    sp.I = I;
+    sp.E = E;
+    sp.eps = eps;
+    sp.x = x;
+    sp.h_trace = h_trace;
+    sp.ids_trace = ids_trace;
+    sp.gen_base = reinterpret_cast<uint32_t *>(c->ll);
+    sp.ctr_x = sp.gen_base + 1;
+    sp.ctr_act = sp.gen_base + 2;
+    sp.ll_x = c->ll + 2;
+    sp.ll_act = sp.ll_x + D;
+    sp.ll_logit = sp.ll_act + 9 * (size_t)I;
+    sp.err = c->d_err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c->sms);
+    cfg.blockDim = dim3(ds::kThreads);
+    cfg.dynamicSmemBytes = ds::layout(D, I, L0->bits, c->sms).total;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once: they exchange data
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (L0->bits == 8)
+        CK(cudaLaunchKernelEx(&cfg, ds::decode_stack_kernel<8>, sp));
+    else
+        CK(cudaLaunchKernelEx(&cfg, ds::decode_stack_kernel<5>, sp));
+}
+
 bool kernels_configured = false;
 void configure_kernels() {
     if (kernels_configured) return;
@@ -232,6 +356,10 @@ void configure_kernels() {
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          gg::SMEM);
     cudaFuncSetAttribute(decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecodeSmemMax);
+    cudaFuncSetAttribute(decode_ffn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(decode_ffn_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(ds::decode_stack_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(ds::decode_stack_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     kernels_configured = true;
 }
 
@@ -330,7 +458,8 @@ struct BlockBuffers {
     Tile *tiles;
     uint16_t *act, *yr, *ys, *xp;
     float *act32;
-    uint32_t *counter;  // last-CTA ticket of decode_route_kernel (kept at zero between launches)
+    uint32_t *counter;  // [0] last-CTA ticket of decode_route_kernel (kept at zero between launches),
+                        // [1] grid-barrier arrivals of decode_ffn_kernel (zeroed per call)
     int nblocks, max_tiles;
 };
 
@@ -356,7 +485,7 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     size_t o_yp = gemv ? 0 : cv.take<uint16_t>((size_t)T * 9 * D);  // expert rows by position, shared rows last
     size_t o_xp = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
     size_t o_a32 = gemv ? cv.take<float>((size_t)T * 9 * I) : 0;
-    size_t o_ctr = cv.take<uint32_t>(1);
+    size_t o_ctr = cv.take<uint32_t>(2);
     size_t need = cv.off + 256;
     ensure_workspace(c, need);
     b.x = host_io ? at<uint16_t>(c, o_x) : nullptr;
@@ -394,7 +523,8 @@ void stage_mark(Context *c, int s) { CK(cudaEventRecord(g_marks ? g_marks[s] : c
 void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_t *y, float *resid,
                    const int32_t *forced_ids, float *probs_out, bool gemv, BlockBuffers &b, bool profile,
                    const float *norm_w = nullptr, float eps = 0.f, uint16_t *h_trace = nullptr,
-                   const float *next_norm = nullptr, uint16_t *next_h = nullptr, uint16_t *next_trace = nullptr) {
+                   const float *next_norm = nullptr, uint16_t *next_h = nullptr, uint16_t *next_trace = nullptr,
+                   uint32_t gen = 1) {
     const int E = L->E, D = L->D, I = L->I;
     cudaStream_t st = c->stream;
     const QView R = L->m[0]->view(), G = L->m[1]->view(), U = L->m[2]->view(), Dn = L->m[3]->view();
@@ -414,6 +544,24 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
             stage_mark(c, S_SCAN);
             stage_mark(c, S_SCATTER);
             stage_mark(c, S_GATE_UP);
+        }
+        if (T == 1 && ffn_fits(c, L)) {
+            // one token: the fused gate/up + down kernel (one CTA per SM, weights staged in smem)
+            const FfnLayout f = ffn_layout(D, I, L->bits, c->sms);
+            if (L->bits == 8)
+                launch(decode_ffn_kernel<8>, dim3(c->sms), dim3(kFfnThreads), (size_t)f.total, st, true, (const uint16_t *)x, D, I,
+                       G, U, SG, SU, Dn, SD, (const int32_t *)ids, (const float *)probs, (const float *)b.gate, b.act32, y,
+                       stacked ? resid : nullptr, b.counter + 1, gen, c->d_err);
+            else
+                launch(decode_ffn_kernel<5>, dim3(c->sms), dim3(kFfnThreads), (size_t)f.total, st, true, (const uint16_t *)x, D, I,
+                       G, U, SG, SU, Dn, SD, (const int32_t *)ids, (const float *)probs, (const float *)b.gate, b.act32, y,
+                       stacked ? resid : nullptr, b.counter + 1, gen, c->d_err);
+            if (profile) {
+                stage_mark(c, S_DOWN);
+                stage_mark(c, S_COMBINE);
+                stage_mark(c, S_N);
+            }
+            return;
         }
         const int gw = T * 9 * I;
         if (L->bits == 8)
@@ -592,6 +740,8 @@ API void di_quant_destroy(void *p) {
         if (c->ev_stage[i]) cudaEventDestroy(c->ev_stage[i]);
     for (cudaEvent_t e : c->layer_events) cudaEventDestroy(e);
     if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
+    if (c->ll) cudaFree(c->ll);
+    if (c->d_stack) cudaFree(c->d_stack);
     if (c->ev_start) cudaEventDestroy(c->ev_start);
     if (c->ev_stop) cudaEventDestroy(c->ev_stop);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -1074,7 +1224,7 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
         int32_t *dids = dev_io ? ids : at<int32_t>(c, o_ids_io);
         float *dprobs = dev_io ? probs : at<float>(c, o_probs_io);
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
-        CK(cudaMemsetAsync(b.counter, 0, sizeof(uint32_t), c->stream));
+        CK(cudaMemsetAsync(b.counter, 0, 2 * sizeof(uint32_t), c->stream));
         CK(cudaEventRecord(c->ev_start, c->stream));
         if (!dev_io) {
             CK(cudaMemcpyAsync(b.x, x, (size_t)T * D * 2, cudaMemcpyHostToDevice, c->stream));
@@ -1213,7 +1363,7 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
                 if (gemv) {
                     // RMSNorm is fused into the decode route kernel
                     enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, true, b, profile, dn + (size_t)l * D, eps,
-                                  trace_l);
+                                  trace_l, nullptr, nullptr, nullptr, (uint32_t)l + 1);
                 } else {
                     // layer l's RMSNorm runs in layer l-1's combine; the first one on its own
                     if (l == 0) rmsnorm_kernel<<<T, 256, 0, c->stream>>>(dx, dn, D, eps, dh, trace_l);
@@ -1228,8 +1378,12 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
                                        c->stream));
             }
         };
-        CK(cudaMemsetAsync(b.counter, 0, sizeof(uint32_t), c->stream));
-        if (gemv && !profile) {
+        CK(cudaMemsetAsync(b.counter, 0, 2 * sizeof(uint32_t), c->stream));
+        const bool persistent = gemv && T == 1 && !profile && stack_fits(c, layers, n_layers);
+        if (persistent) {
+            // one token: every layer in one persistent cooperative kernel
+            enqueue_stack(c, layers, n_layers, dn, eps, dx, dht, dit);
+        } else if (gemv && !profile) {
             // decode: one CUDA graph for the whole stack, rebuilt only when its inputs change
             std::vector<uint64_t> key = {(uint64_t)n_layers, (uint64_t)T, (uint64_t)(uintptr_t)dx,
                                          (uint64_t)(uintptr_t)dn, (uint64_t)(uintptr_t)dht, (uint64_t)(uintptr_t)dit,
@@ -1269,6 +1423,11 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
         if (dev_io) CK(cudaEventRecord(c->ev_stop, c->stream));
         CK(cudaStreamSynchronize(c->stream));
         if (*c->h_err) {
+            if (persistent && (*c->h_err & kErrTimeout)) {
+                // an abandoned call leaves arrival counts and generations out of step: start over
+                CK(cudaMemsetAsync(c->ll, 0, c->ll_words * 8, c->stream));
+                CK(cudaStreamSynchronize(c->stream));
+            }
             set_error(error, capacity, "%s", device_error_text(*c->h_err));
             return -1;
         }
@@ -1759,7 +1918,7 @@ API int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int token
     const size_t o_lg = cv.take<float>((size_t)T * E), o_p = cv.take<float>((size_t)T * 8);
     const size_t o_g = cv.take<float>((size_t)T), o_ids = cv.take<int32_t>((size_t)T * 8);
     const size_t o_bc = cv.take<int32_t>((size_t)b.nblocks * E), o_a = cv.take<float>((size_t)T * 9 * I);
-    const size_t o_ctr = cv.take<uint32_t>(1);
+    const size_t o_ctr = cv.take<uint32_t>(2);
     if (cv.off > DI_MOE_STATIC_SCRATCH_BYTES) {
         set_error(error, capacity,
                   "Allocation-free MoE block needs %zu bytes of scratch for T=%d, E=%d, I=%d; the fixed array holds %u",
@@ -1794,7 +1953,7 @@ API int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int token
         // every buffer above is fully rewritten by the kernels; the error word and the route
         // kernel's completion ticket must start at zero
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
-        CK(cudaMemsetAsync(b.counter, 0, sizeof(uint32_t), c->stream));
+        CK(cudaMemsetAsync(b.counter, 0, 2 * sizeof(uint32_t), c->stream));
         CK(cudaEventRecord(c->ev_start, c->stream));
         enqueue_block(c, L, x, T, y, nullptr, nullptr, probs, true, b, false);
         if (launch_check(error, capacity)) return -1;

@@ -275,37 +275,56 @@ __global__ void router_logits_gemv_kernel(const uint16_t *__restrict__ x, int T,
 // 8 chosen logits (Qwen36Model.cs:259-261, :293-298). Non-finite logits set kErrNonFinite.
 // The warp also computes the shared-route gate logit (canonical order). Each CTA owns a
 // contiguous token range and writes the per-expert route counts of that range.
-// 8 rounds of a warp arg-max over (value desc, index asc): the 8 largest logits in descending
-// order with ties to the lower expert id. v[j] is this lane's candidate lane + 32j; all lanes
-// return the same sel/chosen. Non-finite candidates must already be replaced by -inf.
+// The 8 largest logits in descending order with ties to the lower expert id. v[j] is this
+// lane's candidate lane + 32j; all lanes return the same sel/chosen. Non-finite candidates must
+// already be replaced by -inf. Each lane first sorts its 8 candidates (a 19-comparator network
+// on (value desc, id asc)); each of the 8 rounds is then a warp max of the lanes' heads as
+// order-preserving integer keys and, among equal keys, a warp min of their ids (redux.sync),
+// after which the winning lane drops its head. -0 ranks as +0 (they compare equal as floats).
+__device__ __forceinline__ uint32_t order_key(float v) {
+    const uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 __device__ __forceinline__ void select_top8(const float *v, int E, int32_t *sel, float *chosen) {
     const int lane = lane_id();
-    uint32_t used = 0;  // bit j: candidate lane+32j taken
+    uint32_t key[8], id[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        id[j] = (uint32_t)(lane + 32 * j);
+        key[j] = (int)id[j] < E ? order_key(v[j]) : 0u;  // every real key (even -inf's) is above 0
+    }
+    auto cmpswap = [&](int a, int b) {  // afterwards (key, id)[a] precedes (key, id)[b]
+        const bool sw = key[b] > key[a] || (key[b] == key[a] && id[b] < id[a]);
+        const uint32_t ka = key[a], ia = id[a];
+        key[a] = sw ? key[b] : ka;
+        id[a] = sw ? id[b] : ia;
+        key[b] = sw ? ka : key[b];
+        id[b] = sw ? ia : id[b];
+    };
+    cmpswap(0, 2); cmpswap(1, 3); cmpswap(4, 6); cmpswap(5, 7);
+    cmpswap(0, 4); cmpswap(1, 5); cmpswap(2, 6); cmpswap(3, 7);
+    cmpswap(0, 1); cmpswap(2, 3); cmpswap(4, 5); cmpswap(6, 7);
+    cmpswap(2, 4); cmpswap(3, 5);
+    cmpswap(1, 4); cmpswap(3, 6);
+    cmpswap(1, 2); cmpswap(3, 4); cmpswap(5, 6);
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-        float best = -INFINITY;
-        int bid = 0x7fffffff;
+        const uint32_t best = __reduce_max_sync(kFull, key[0]);
+        const uint32_t win = __reduce_min_sync(kFull, key[0] == best ? id[0] : 0xffffffffu);
+        sel[n] = (int32_t)win;
+        chosen[n] = key_value(best);
+        if (id[0] == win) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = lane + 32 * j;
-            const bool ok = e < E && !((used >> j) & 1u);
-            if (ok && (v[j] > best || bid == 0x7fffffff)) {
-                best = v[j];
-                bid = e;
+            for (int j = 0; j < 7; ++j) {
+                key[j] = key[j + 1];
+                id[j] = id[j + 1];
             }
+            key[7] = 0u;
+            id[7] = 0xffffffffu;
         }
-#pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const float ob = __shfl_xor_sync(kFull, best, off);
-            const int oi = __shfl_xor_sync(kFull, bid, off);
-            if (oi != 0x7fffffff && (bid == 0x7fffffff || ob > best || (ob == best && oi < bid))) {
-                best = ob;
-                bid = oi;
-            }
-        }
-        sel[n] = bid;
-        chosen[n] = best;
-        if ((bid & 31) == lane) used |= 1u << (bid >> 5);
     }
 }
 

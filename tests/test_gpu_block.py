@@ -166,6 +166,81 @@ def test_stack_teacher_forced_layers(ctx):
         assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
 
 
+@pytest.mark.parametrize("bits", [8, 5])
+def test_full_geometry_decode_stack(ctx, bits):
+    # one token through two full-size layers: the fused decode FFN (one CTA per SM, grid barrier
+    # per layer) inside the captured decode graph, checked layer by layer like the test above
+    n, D, T = 2, 2048, 1
+    pairs = [layer_pair(ctx, 42, bits, 256, D, 512, layer=l) for l in range(n)]
+    norms = (1.0 + 0.05 * np.cos(np.arange(n * D))).astype(np.float32).reshape(n, D)
+    x0 = O.bf16_to_f32(O.gen_bf16(16, O.ACT_STREAM, T * D)).reshape(T, D)
+    for _ in range(2):  # first call captures the graph, the second replays it
+        xg, ht, it, _ = di.moe_stack(ctx, [p[1] for p in pairs], norms, x0, 1e-6, di.PATH_GEMV, trace=True)
+        x = x0.copy()
+        for l, (L, _) in enumerate(pairs):
+            rc, out, ids, _, _ = O.moe_block(L, ht[l], O.MODE_F32)
+            assert rc == 0 and np.array_equal(ids, it[l])
+            x = x + out
+        ma, rl = O.tolerance_report(xg, x)
+        assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
+
+
+@pytest.mark.parametrize("bits", [8, 5])
+def test_persistent_stack_small_geometry(ctx, bits):
+    # D = I = 512 and E = 64: the one-token stack runs as one persistent kernel whose exchanges
+    # carry 65 router words (the shared expert's gate logit after the last expert); layer 1 has a
+    # router bias. Repeated calls must give the same bits (fresh exchange generations each call).
+    n, D, E = 3, 512, 64
+    bias = (-0.5 * np.log(np.arange(E) + 1.0)).astype(np.float32)
+    oracle_layers = [O.Layer(44, layer=l, bits=bits, E=E, D=D, I=512, router_bias=bias if l == 1 else None)
+                     for l in range(n)]
+    layers = [di.MoeLayer.from_oracle(ctx, L) for L in oracle_layers]
+    norms = (1.0 + 0.1 * np.sin(np.arange(n * D))).astype(np.float32).reshape(n, D)
+    x0 = O.bf16_to_f32(O.gen_bf16(17, O.ACT_STREAM, D)).reshape(1, D)
+    first = None
+    for _ in range(3):
+        xg, ht, it, _ = di.moe_stack(ctx, layers, norms, x0, 1e-6, di.PATH_GEMV, trace=True)
+        x = x0.copy()
+        for l, L in enumerate(oracle_layers):
+            rc, out, ids, _, _ = O.moe_block(L, ht[l], O.MODE_F32)
+            assert rc == 0 and np.array_equal(ids, it[l])
+            x = x + out
+        ma, rl = O.tolerance_report(xg, x)
+        assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
+        if first is None:
+            first = xg
+        assert np.array_equal(first, xg)
+    for G in layers:
+        G.close()
+
+
+def test_top8_exact_ties_go_to_the_lower_id(ctx):
+    # router rows 3, 40, 77, 150 and 10, 11 are copies of one another with equal bias, so their
+    # logits tie exactly; the selection order must be ascending id within each tie group in the
+    # prefill top-8, the per-layer decode route kernel and the persistent stack kernel alike
+    E, D = 256, 512
+    L = O.Layer(45, bits=8, E=E, D=D, I=512)
+    r = L.m["router"]
+    bias = np.zeros(E, np.float32)
+    for group, b in (((3, 40, 77, 150), 4.0), ((10, 11), 2.0)):
+        for row in group[1:]:
+            r.packed[0, row] = r.packed[0, group[0]]
+            r.scales[0, row] = r.scales[0, group[0]]
+            r.biases[0, row] = r.biases[0, group[0]]
+        bias[list(group)] = b
+    L.router_bias = bias
+    G = di.MoeLayer.from_oracle(ctx, L)
+    for T, flags in ((33, di.PATH_GROUPED), (1, di.PATH_GEMV)):
+        _, _, ids = check_block(ctx, L, G, T, flags)
+        assert list(ids[0, :4]) == [3, 40, 77, 150]
+    x0 = O.bf16_to_f32(O.gen_bf16(18, O.ACT_STREAM, D)).reshape(1, D)
+    norms = np.ones((1, D), np.float32)
+    _, ht, it, _ = di.moe_stack(ctx, [G], norms, x0, 1e-6, di.PATH_GEMV, trace=True)
+    _, _, oids, _, _ = O.moe_block(L, ht[0], O.MODE_F32)
+    assert np.array_equal(it[0], oids) and list(it[0, 0, :4]) == [3, 40, 77, 150]
+    G.close()
+
+
 def test_decode_stack_graph_replays_match(ctx):
     # the decode stack is captured as a CUDA graph on first use and replayed afterwards;
     # replays must give the same bits as the first (captured) run, and a changed input must flow
