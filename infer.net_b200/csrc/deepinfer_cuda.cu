@@ -235,10 +235,20 @@ bool ffn_fits(const Context *c, const Layer *L) {
     return ffn_layout(L->D, L->I, L->bits, c->sms).total <= 227 * 1024;
 }
 
-// The persistent one-token stack kernel: layers sharing D, I, E and bits, D and I multiples of 512
-// (16-byte scale rows), D <= 2048, I <= 512 and at most 32 (gate, up) pairs per CTA (per-thread
-// register budgets), its per-CTA share in shared memory, and one CTA resident on every SM (a
-// cooperative launch).
+// The persistent one-token stack kernel of a geometry (null when none is built for it).
+using StackKernel = void (*)(const ds::StackParams);
+StackKernel stack_kernel(int bits, int D) {
+    if (bits == 8) return D == 512 ? ds::decode_stack_kernel<8, 512> : D == 1024 ? ds::decode_stack_kernel<8, 1024>
+                                       : D == 2048 ? ds::decode_stack_kernel<8, 2048> : nullptr;
+    if (bits == 5) return D == 512 ? ds::decode_stack_kernel<5, 512> : D == 1024 ? ds::decode_stack_kernel<5, 1024>
+                                       : D == 2048 ? ds::decode_stack_kernel<5, 2048> : nullptr;
+    return nullptr;
+}
+
+// The persistent one-token stack kernel: layers sharing D, I, E and bits; D in {512, 1024, 2048}
+// (a power-of-two number of 16-element chunks per warp), I = 512 (one chunk of a down row per
+// lane), at most 32 (gate, up) pairs and 16 outputs per CTA, its per-CTA share in shared memory,
+// and one CTA resident on every SM (a cooperative launch).
 bool stack_fits(Context *c, void *const *layers, int n) {
     const Layer *L0 = static_cast<const Layer *>(layers[0]);
     for (int l = 0; l < n; ++l) {
@@ -246,14 +256,13 @@ bool stack_fits(Context *c, void *const *layers, int n) {
         if (L->D != L0->D || L->I != L0->I || L->E != L0->E || L->bits != L0->bits) return false;
     }
     const int D = L0->D, I = L0->I;
-    if (D % 512 || D > 2048 || I % 512 || 9 * I > ds::kMaxActWords * ds::kThreads || L0->E > 256) return false;
+    if ((D != 512 && D != 1024 && D != 2048) || I != ds::kI || L0->E > 256) return false;
     const ds::Layout f = ds::layout(D, I, L0->bits, c->sms);
     const int smem = f.total;
-    if (smem > 227 * 1024 || f.pairs > ds::kPairsPerWarp * ds::kWarps) return false;
+    if (smem > 227 * 1024 || f.pairs > 2 * ds::kGroupPairs || f.outs > ds::kMaxOuts) return false;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, L0->bits == 8 ? ds::decode_stack_kernel<8>
-                                                                             : ds::decode_stack_kernel<5>,
-                                                      ds::kThreads, smem) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel(L0->bits, D), ds::kThreads, smem) !=
+        cudaSuccess) {
         cudaGetLastError();
         return false;
     }
@@ -266,8 +275,8 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
                    int32_t *ids_trace) {
     const Layer *L0 = static_cast<const Layer *>(layers[0]);
     const int D = L0->D, I = L0->I, E = L0->E;
-    // exchange words: [0] the generation counter and the x arrivals, [1] the act arrivals, then
-    // x [D], act [9 I], logits [E + 1]
+    // exchange words: [0] the generation counter and the x arrivals, [1] the act and logit
+    // arrivals, then x [D], act [9 I], logits [E + 1]
     const size_t words = 2 + (size_t)D + 9 * (size_t)I + E + 1;
     if (c->ll_words < words) {
         if (c->ll) CK(cudaFree(c->ll));
@@ -313,8 +322,6 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
     ds::StackParams sp;
     sp.layers = c->d_stack;
     sp.n_layers = n;
-    sp.D = D;
-    sp.I = I;
     sp.E = E;
     sp.eps = eps;
     sp.x = x;
@@ -323,6 +330,7 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
     sp.gen_base = reinterpret_cast<uint32_t *>(c->ll);
     sp.ctr_x = sp.gen_base + 1;
     sp.ctr_act = sp.gen_base + 2;
+    sp.ctr_logit = sp.gen_base + 3;
     sp.ll_x = c->ll + 2;
     sp.ll_act = sp.ll_x + D;
     sp.ll_logit = sp.ll_act + 9 * (size_t)I;
@@ -337,10 +345,7 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (L0->bits == 8)
-        CK(cudaLaunchKernelEx(&cfg, ds::decode_stack_kernel<8>, sp));
-    else
-        CK(cudaLaunchKernelEx(&cfg, ds::decode_stack_kernel<5>, sp));
+    CK(cudaLaunchKernelEx(&cfg, stack_kernel(L0->bits, D), sp));
 }
 
 bool kernels_configured = false;
@@ -358,8 +363,9 @@ void configure_kernels() {
     cudaFuncSetAttribute(decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecodeSmemMax);
     cudaFuncSetAttribute(decode_ffn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(decode_ffn_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(ds::decode_stack_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(ds::decode_stack_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    for (int bits : {8, 5})
+        for (int D : {512, 1024, 2048})
+            cudaFuncSetAttribute(stack_kernel(bits, D), cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     kernels_configured = true;
 }
 
