@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
     float *red = reinterpret_cast<float *>(sm + f.red());
     volatile int *abort_s = reinterpret_cast<volatile int *>(sm + f.abort_flag());
     float *xown = reinterpret_cast<float *>(sm + f.xown());
-    const int cpd = D / 16, cpw = cpd / kWarps, slots = 32 / cpw;  // S5: chunks per warp, pair slots
+    constexpr int cpd = D / 16, cpw = cpd / kWarps;  // chunks of h; S5: chunks per warp
     const int cl = lane & (cpw - 1), slot = lane / cpw, my_c = warp * cpw + cl;
 
     // this CTA's shares: (gate, up) pairs [p_lo, p_hi) of the 9*I, outputs [d_lo, d_hi), router rows [r_lo, r_hi) of E+1
@@ -539,12 +539,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         // partial (gate, up) dots of chunk my_c for the group's pairs slot + slots*k; summed over
         // the warp's chunks (butterfly within the slot's lanes) into part[warp][pair][gate/up]
         auto group_partials = [&](int qb, int qe) {
-#pragma unroll 1
-            for (int k = 0; k < 4; ++k) {
-                const int ql = slot + slots * k, q = qb + ql;
-                const bool mine = k * slots < kGroupPairs && q < qe;
-                float gp = 0.f, up = 0.f;
-                if (mine) {
+            constexpr int kSlots = 32 / cpw, kRounds = kGroupPairs / kSlots;
+            float gp[kRounds], up[kRounds];
+#pragma unroll
+            for (int k = 0; k < kRounds; ++k) {
+                const int q = qb + slot + kSlots * k;
+                gp[k] = up[k] = 0.f;
+                if (q < qe) {
                     float wg[16], wu[16];
                     chunk_denormals<BITS>(sm + f.gu_code(0) + q * f.gu_row, my_c, wg);
                     chunk_denormals<BITS>(sm + f.gu_code(1) + q * f.gu_row, my_c, wu);
@@ -553,20 +554,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                     const float gb = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(0, 1) + so));
                     const float us = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 0) + so));
                     const float ub = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 1) + so));
-                    gp = fmaf(gs, chunk_dot(wg, x4) * kDotScale, gb * xcv);
-                    up = fmaf(us, chunk_dot(wu, x4) * kDotScale, ub * xcv);
-                }
-                if (k * slots < kGroupPairs) {
-                    for (int n = 1; n < cpw; n <<= 1) {
-                        gp += __shfl_xor_sync(kFull, gp, n);
-                        up += __shfl_xor_sync(kFull, up, n);
-                    }
-                    if (mine && cl == 0) {
-                        part[(warp * kGroupPairs + ql) * 2] = gp;
-                        part[(warp * kGroupPairs + ql) * 2 + 1] = up;
-                    }
+                    gp[k] = fmaf(gs, chunk_dot(wg, x4) * kDotScale, gb * xcv);
+                    up[k] = fmaf(us, chunk_dot(wu, x4) * kDotScale, ub * xcv);
                 }
             }
+            // sum over the warp's chunks: butterflies within each slot's lanes, rounds interleaved
+#pragma unroll
+            for (int n = 1; n < cpw; n <<= 1)
+#pragma unroll
+                for (int k = 0; k < kRounds; ++k) {
+                    gp[k] += __shfl_xor_sync(kFull, gp[k], n);
+                    up[k] += __shfl_xor_sync(kFull, up[k], n);
+                }
+            if (cl == 0)
+#pragma unroll
+                for (int k = 0; k < kRounds; ++k) {
+                    const int ql = slot + kSlots * k;
+                    if (qb + ql < qe) {
+                        part[(warp * kGroupPairs + ql) * 2] = gp[k];
+                        part[(warp * kGroupPairs + ql) * 2 + 1] = up[k];
+                    }
+                }
         };
         // warp 0: pair (lane >> 1) of the group, lane & 1 gate / up: the 16 warp partials in order
         auto group_act = [&](int qb, int qe) {
@@ -627,16 +635,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                 atomicOr(p.err, kErrTimeout);
                 *abort_s = 1;
             } else {
-#pragma unroll 2
-                for (int o = 0; o < nd; ++o) {
-                    const int r = j * f.outs + o;
-                    float w[16];
-                    chunk_denormals<BITS>(sm + f.dn_code() + r * f.dn_row, lane, w);
-                    const int so = r * f.dn_grp + (lane >> 2) * 2;
-                    const float sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.dn_sb(0) + so));
-                    const float bi = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.dn_sb(1) + so));
-                    const float v = warp_sum_butterfly(fmaf(sc, chunk_dot(w, a4) * kDotScale, bi * asum));
-                    if (lane == 0) part[j * kMaxOuts + o] = v;
+                // four outputs at a time: their loads, dots and butterflies interleave
+                for (int o0 = 0; o0 < nd; o0 += 4) {
+                    float v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int o = o0 + u;
+                        v[u] = 0.f;
+                        if (o < nd) {
+                            const int r = j * f.outs + o;
+                            float w[16];
+                            chunk_denormals<BITS>(sm + f.dn_code() + r * f.dn_row, lane, w);
+                            const int so = r * f.dn_grp + (lane >> 2) * 2;
+                            const float sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.dn_sb(0) + so));
+                            const float bi = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.dn_sb(1) + so));
+                            v[u] = fmaf(sc, chunk_dot(w, a4) * kDotScale, bi * asum);
+                        }
+                    }
+#pragma unroll
+                    for (int n = 16; n; n >>= 1)
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) v[u] += __shfl_xor_sync(kFull, v[u], n);
+                    if (lane == 0)
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            if (o0 + u < nd) part[j * kMaxOuts + o0 + u] = v[u];
                 }
             }
         }

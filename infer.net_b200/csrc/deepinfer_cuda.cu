@@ -1540,7 +1540,47 @@ struct Ep {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
     int32_t *h_counts = nullptr;  // pinned [world*world]
+    // symmetric buffers (ep.cuh), mapped into every rank through CUDA IPC
+    size_t cap = 0;                        // tokens per rank they hold
+    int sym_D = 0;                         // hidden size they were laid out for
+    uint8_t *sym = nullptr;                // this rank's
+    uint8_t *peer_sym[kMaxRanks] = {};     // every rank's, in this process's address space
+    uint64_t steps = 0;                    // layer steps completed: every arrival counter reads this
+    bool broken = false;                   // a device wait failed: the counters are out of step
 };
+struct EpSymLayout {
+    size_t rx, meta, back, sync, bytes;
+};
+EpSymLayout ep_sym_layout(int G, size_t cap, int D) {
+    auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    EpSymLayout o;
+    o.rx = 0;
+    o.meta = up(o.rx + (size_t)G * cap * D * 2);
+    o.back = up(o.meta + (size_t)G * cap * sizeof(RowMeta));
+    o.sync = up(o.back + (size_t)G * cap * D * 2);
+    o.bytes = up(o.sync + 4 * kMaxRanks * sizeof(uint32_t));
+    return o;
+}
+EpPeers ep_peers(const Ep *ep) {
+    const EpSymLayout o = ep_sym_layout(ep->world, ep->cap, ep->sym_D);
+    EpPeers p{};
+    for (int q = 0; q < ep->world; ++q) {
+        p.rx[q] = reinterpret_cast<uint16_t *>(ep->peer_sym[q] + o.rx);
+        p.meta[q] = reinterpret_cast<RowMeta *>(ep->peer_sym[q] + o.meta);
+        p.back[q] = reinterpret_cast<uint16_t *>(ep->peer_sym[q] + o.back);
+        p.sync[q] = reinterpret_cast<uint32_t *>(ep->peer_sym[q] + o.sync);
+    }
+    return p;
+}
+void ep_release_sym(Ep *ep) {
+    for (int q = 0; q < ep->world; ++q)
+        if (q != ep->rank && ep->peer_sym[q]) cudaIpcCloseMemHandle(ep->peer_sym[q]);
+    if (ep->sym) cudaFree(ep->sym);
+    ep->sym = nullptr;
+    for (int q = 0; q < kMaxRanks; ++q) ep->peer_sym[q] = nullptr;
+    ep->cap = 0;
+    ep->sym_D = 0;
+}
 std::set<Ep *> g_eps;
 bool live_ep(void *p) {
     std::lock_guard<std::mutex> g(g_registry);
@@ -1554,6 +1594,45 @@ struct NcclFail {
         ncclResult_t r_ = (call);                                                                     \
         if (r_ != ncclSuccess) throw NcclFail{std::string(#call) + ": " + nc->getErrorString(r_)};    \
     } while (0)
+
+// Collective (every rank of the group calls it with the same arguments): make the symmetric
+// buffers hold `cap` tokens per rank of hidden size D, allocating, zeroing and mapping them
+// across the ranks (CUDA IPC handles gathered through NCCL) when they do not yet.
+void ep_prepare(Ep *ep, size_t cap, int D) {
+    if (ep->sym && cap <= ep->cap && D == ep->sym_D) return;
+    const NcclApi *nc = nccl_api(nullptr);
+    Context *c = ep->ctx;
+    CK(cudaStreamSynchronize(c->stream));
+    ep_release_sym(ep);
+    const EpSymLayout o = ep_sym_layout(ep->world, cap, D);
+    CK(cudaMalloc(&ep->sym, o.bytes));
+    CK(cudaMemsetAsync(ep->sym, 0, o.bytes, c->stream));
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, ep->sym));
+    Carve cv;
+    const size_t o_h = cv.take<uint8_t>(sizeof(cudaIpcMemHandle_t) * (ep->world + 1));
+    ensure_workspace(c, cv.off + 256);
+    uint8_t *dh = at<uint8_t>(c, o_h);
+    CK(cudaMemcpyAsync(dh, &mine, sizeof(mine), cudaMemcpyHostToDevice, c->stream));
+    // every rank's handle; a rank's zeroing precedes its handle in stream order, so no rank can
+    // write into a buffer before it is cleared
+    NK(nc->allGather(dh, dh + sizeof(mine), sizeof(mine), ncclUint8, ep->comm, c->stream));
+    std::vector<cudaIpcMemHandle_t> all(ep->world);
+    CK(cudaMemcpyAsync(all.data(), dh + sizeof(mine), sizeof(mine) * ep->world, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    for (int q = 0; q < ep->world; ++q) {
+        if (q == ep->rank) {
+            ep->peer_sym[q] = ep->sym;
+            continue;
+        }
+        void *p = nullptr;
+        CK(cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess));
+        ep->peer_sym[q] = static_cast<uint8_t *>(p);
+    }
+    ep->cap = cap;
+    ep->sym_D = D;
+    ep->steps = 0;  // fresh counters
+}
 }  // namespace
 
 API int di_moe_ep_unique_id(uint8_t *id, char *error, int capacity) {
@@ -1624,6 +1703,7 @@ API void di_moe_ep_destroy(void *p) {
     }
     DeviceGuard dg(ep->ctx->device);
     cudaStreamSynchronize(ep->ctx->stream);
+    ep_release_sym(ep);
     nccl_api(nullptr)->commDestroy(ep->comm);
     cudaFreeHost(ep->h_counts);
     delete ep;
@@ -1719,26 +1799,38 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         }
     }
     const bool dev_io = flags & DI_MOE_DEVICE_IO;
+    if (ep->broken) {
+        set_error(error, capacity, "Expert-parallel group failed in an earlier call; create it again");
+        return -1;
+    }
     const NcclApi *nc = nccl_api(nullptr);
     DeviceGuard dg(c->device);
     cudaStream_t st = c->stream;
     try {
         for (int l = 0; l < n_layers; ++l)
             for (int i = 0; i < 8; ++i) sync_matrix(static_cast<Layer *>(layers[l])->m[i]);
-        // total tokens over the ranks bounds the rows any rank can receive
+        // the largest token count of any rank sizes the symmetric buffers (one host round trip
+        // per call; the layers below run without any)
         Carve cv0;
         const size_t o_tok = cv0.take<int32_t>(2);
         ensure_workspace(c, cv0.off + 256);
         int32_t *d_tok = at<int32_t>(c, o_tok);
         CK(cudaMemcpyAsync(d_tok, &T, 4, cudaMemcpyHostToDevice, st));
-        NK(nc->allReduce(d_tok, d_tok + 1, 1, ncclInt32, ncclSum, ep->comm, st));
+        NK(nc->allReduce(d_tok, d_tok + 1, 1, ncclInt32, ncclMax, ep->comm, st));
         CK(cudaMemcpyAsync(ep->h_counts, d_tok + 1, 4, cudaMemcpyDeviceToHost, st));
         CK(cudaStreamSynchronize(st));
-        const int Rmax = ep->h_counts[0];
-        const int Smax = T * std::min(8, G);
+        ep_prepare(ep, (size_t)ep->h_counts[0], D);
+        const int cap = (int)ep->cap;
+        const int RC = G * cap;  // received row slots: region s = rows from rank s
+        const EpPeers peers = ep_peers(ep);
+        const EpSymLayout so_ = ep_sym_layout(G, cap, D);
+        uint16_t *my_rx = reinterpret_cast<uint16_t *>(ep->sym + so_.rx);
+        RowMeta *my_meta = reinterpret_cast<RowMeta *>(ep->sym + so_.meta);
+        uint16_t *my_back = reinterpret_cast<uint16_t *>(ep->sym + so_.back);
+        uint32_t *my_sync = reinterpret_cast<uint32_t *>(ep->sym + so_.sync);
         const int nb_l = (T + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA;
-        const int nb_r = (Rmax + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA;
-        const int max_tiles = (8 * Rmax + gg::BN - 1) / gg::BN + El + (T + gg::BN - 1) / gg::BN + 2;
+        const int nbr = (RC + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA;
+        const int max_tiles = (8 * RC + gg::BN - 1) / gg::BN + El + (T + gg::BN - 1) / gg::BN + 2;
         Carve cv;
         cv.take<int32_t>(2);  // keep the token-count words
         const size_t o_x = dev_io ? 0 : cv.take<float>((size_t)T * D), o_n = dev_io ? 0 : cv.take<float>((size_t)n_layers * D);
@@ -1746,30 +1838,24 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         const size_t o_ids = cv.take<int32_t>((size_t)T * 8), o_p = cv.take<float>((size_t)T * 8), o_g = cv.take<float>(T);
         const size_t o_bc = cv.take<int32_t>((size_t)nb_l * E), o_sidx = cv.take<int32_t>((size_t)T * G);
         const size_t o_sc = cv.take<int32_t>(kMaxRanks), o_so = cv.take<int32_t>(kMaxRanks);
-        const size_t o_all = cv.take<int32_t>(kMaxRanks * kMaxRanks);
-        const size_t o_sx = cv.take<uint16_t>((size_t)Smax * D), o_sm = cv.take<RowMeta>((size_t)Smax);
-        const size_t o_rx = cv.take<uint16_t>((size_t)(Rmax + T) * D), o_rm = cv.take<RowMeta>((size_t)Rmax + 1);
-        const size_t o_il = cv.take<int32_t>((size_t)Rmax * 8 + 8), o_rbc = cv.take<int32_t>((size_t)(nb_r + 1) * (El + 1));
-        const size_t o_rbb = cv.take<int32_t>((size_t)(nb_r + 1) * (El + 1)), o_sgc = cv.take<int32_t>(El + 2);
+        const size_t o_il = cv.take<int32_t>((size_t)RC * 8 + 8), o_rbc = cv.take<int32_t>((size_t)(nbr + 1) * (El + 1));
+        const size_t o_rbb = cv.take<int32_t>((size_t)(nbr + 1) * (El + 1)), o_sgc = cv.take<int32_t>(El + 2);
         const size_t o_sgo = cv.take<int32_t>(El + 2), o_t = cv.take<Tile>(max_tiles), o_nt = cv.take<int32_t>(1);
-        const size_t o_pm = cv.take<int32_t>((size_t)Rmax * 8 + 8), o_act = cv.take<uint16_t>(((size_t)Rmax * 8 + T) * I);
-        const size_t o_y = cv.take<uint16_t>(((size_t)Rmax * 8 + T) * D + 8), o_rp = cv.take<int32_t>((size_t)Rmax * 8 + 8);
-        const size_t o_z = cv.take<uint16_t>((size_t)Rmax * D + 8), o_bk = cv.take<uint16_t>((size_t)Smax * D);
-        const size_t o_xp = cv.take<uint16_t>((size_t)Rmax * 8 * D + 8);
+        const size_t o_pm = cv.take<int32_t>((size_t)RC * 8 + 8), o_act = cv.take<uint16_t>(((size_t)RC * 8 + T) * I);
+        const size_t o_y = cv.take<uint16_t>(((size_t)RC * 8 + T) * D + 8), o_rp = cv.take<int32_t>((size_t)RC * 8 + 8);
+        const size_t o_xp = cv.take<uint16_t>((size_t)RC * 8 * D + 8);
         ensure_workspace(c, cv.off + 256);
         float *dx = dev_io ? x : at<float>(c, o_x);
         const float *dn = dev_io ? norms : at<float>(c, o_n);
-        uint16_t *h = at<uint16_t>(c, o_h), *sx = at<uint16_t>(c, o_sx), *rx = at<uint16_t>(c, o_rx);
-        uint16_t *act = at<uint16_t>(c, o_act), *y = at<uint16_t>(c, o_y);
+        uint16_t *h = at<uint16_t>(c, o_h), *act = at<uint16_t>(c, o_act), *y = at<uint16_t>(c, o_y);
+        uint16_t *xp = at<uint16_t>(c, o_xp);
         int32_t *rpos = at<int32_t>(c, o_rp);
-        uint16_t *z = at<uint16_t>(c, o_z), *bk = at<uint16_t>(c, o_bk), *xp = at<uint16_t>(c, o_xp);
         float *logits = at<float>(c, o_lg), *probs = at<float>(c, o_p), *gate = at<float>(c, o_g);
         int32_t *ids = at<int32_t>(c, o_ids), *bc = at<int32_t>(c, o_bc), *sidx = at<int32_t>(c, o_sidx);
-        int32_t *sc = at<int32_t>(c, o_sc), *so = at<int32_t>(c, o_so), *all = at<int32_t>(c, o_all);
+        int32_t *sc = at<int32_t>(c, o_sc), *so = at<int32_t>(c, o_so);
         int32_t *il = at<int32_t>(c, o_il), *rbc = at<int32_t>(c, o_rbc), *rbb = at<int32_t>(c, o_rbb);
         int32_t *sgc = at<int32_t>(c, o_sgc), *sgo = at<int32_t>(c, o_sgo), *nt = at<int32_t>(c, o_nt);
         int32_t *perm = at<int32_t>(c, o_pm);
-        RowMeta *smeta = at<RowMeta>(c, o_sm), *rmeta = at<RowMeta>(c, o_rm);
         Tile *tiles = at<Tile>(c, o_t);
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st));
         CK(cudaEventRecord(c->ev_start, st));
@@ -1782,81 +1868,52 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             Layer *L = static_cast<Layer *>(layers[l]);
             const QView R = L->m[0]->view(), Gm = L->m[1]->view(), U = L->m[2]->view(), Dm = L->m[3]->view();
             const QView SG = L->m[4]->view(), SU = L->m[5]->view(), SD = L->m[6]->view(), SR = L->m[7]->view();
-            // 1. route the local tokens
-            rmsnorm_kernel<<<T, 256, 0, st>>>(dx, dn + (size_t)l * D, D, eps, h, nullptr);
+            const uint32_t target = (uint32_t)(ep->steps + (uint64_t)l + 1);  // arrivals per rank so far
+            // 1. route the local tokens (layer l's RMSNorm ran in layer l-1's combine)
+            if (l == 0) rmsnorm_kernel<<<T, 256, 0, st>>>(dx, dn, D, eps, h, nullptr);
             router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
                                    router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);
             topk_count_kernel<<<nb_l, topk::WARPS * 32, 0, st>>>(logits, T, E, h, D, SR, nullptr, ids, probs, gate, bc,
                                                                   c->d_err);
-            // 2. one row per (token, destination GPU), then the counts of every pair of GPUs
+            // 2. one row per (token, destination rank), written into the destinations over NVLink
             ep_layout_kernel<<<1, 1024, 0, st>>>(ids, T, El, G, sidx, sc, so);
-            ep_pack_kernel<<<T, 256, 0, st>>>(h, ids, probs, D, G, sidx, so, sx, smeta);
-            NK(nc->allGather(sc, all, G, ncclInt32, ep->comm, st));
-            CK(cudaMemcpyAsync(ep->h_counts, all, sizeof(int32_t) * G * G, cudaMemcpyDeviceToHost, st));
-            CK(cudaStreamSynchronize(st));
-            int scnt[kMaxRanks], rcnt[kMaxRanks], soff[kMaxRanks], roff[kMaxRanks], Rn = 0, Sn = 0;
-            for (int q = 0; q < G; ++q) {
-                scnt[q] = ep->h_counts[rank * G + q];
-                rcnt[q] = ep->h_counts[q * G + rank];
-                soff[q] = Sn;
-                roff[q] = Rn;
-                Sn += scnt[q];
-                Rn += rcnt[q];
-            }
-            if (Rn > Rmax || Sn > Smax) throw CudaFail{"expert-parallel row counts exceed their bound"};
-            // 3. dispatch token rows and their routing metadata
-            NK(nc->groupStart());
-            for (int q = 0; q < G; ++q) {
-                if (scnt[q]) {
-                    NK(nc->send(sx + (size_t)soff[q] * D, (size_t)scnt[q] * D * 2, ncclUint8, q, ep->comm, st));
-                    NK(nc->send(smeta + soff[q], (size_t)scnt[q] * sizeof(RowMeta), ncclUint8, q, ep->comm, st));
-                }
-                if (rcnt[q]) {
-                    NK(nc->recv(rx + (size_t)roff[q] * D, (size_t)rcnt[q] * D * 2, ncclUint8, q, ep->comm, st));
-                    NK(nc->recv(rmeta + roff[q], (size_t)rcnt[q] * sizeof(RowMeta), ncclUint8, q, ep->comm, st));
-                }
-            }
-            NK(nc->groupEnd());
-            // 4. local experts over the received rows, shared expert over the local rows
-            CK(cudaMemcpyAsync(rx + (size_t)Rn * D, h, (size_t)T * D * 2, cudaMemcpyDeviceToDevice, st));
-            const int nbr = std::max(1, (Rn + topk::TOK_PER_CTA - 1) / topk::TOK_PER_CTA);
-            if (Rn > 0) ep_recv_count_kernel<<<nbr, 256, 0, st>>>(rmeta, Rn, L->E_off, El, il, rbc);
-            else CK(cudaMemsetAsync(rbc, 0, sizeof(int32_t) * (El + 1), st));
-            scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, Rn, T, gg::BN, rbb, sgc, sgo, tiles, nt,
+            ep_dispatch_kernel<<<std::min((T + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank, cap,
+                                                                                  sidx, sc, peers, my_sync + 3 * G + 1);
+            // 3. the rows every rank sent here -> local routes, expert segments, GEMM tiles
+            ep_recv_routes_kernel<<<nbr, 256, 0, st>>>(my_meta, my_sync, target, G, cap, L->E_off, El, peers, il, rbc,
+                                                       c->d_err);
+            scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, RC, T, gg::BN, rbb, sgc, sgo, tiles, nt,
                                                   max_tiles, c->d_err);
-            if (Rn > 0) scatter_routes_kernel<<<nbr, 32, 0, st>>>(il, Rn, El + 1, rbb, sgo, perm, rpos);
-            if (Rn > 0) permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(rx, perm, sgo + El, D, xp);
-            launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, Gm, U, SG, SU, xp, 8 * Rn, rx, Rn + T,
-                                                            perm, tiles, nt, 8 * Rn, Rn, D, I, El + 1, act,
-                                                            8 * Rn + T, c->d_err),
+            scatter_routes_kernel<<<nbr, 32, 0, st>>>(il, RC, El + 1, rbb, sgo, perm, rpos);
+            permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(my_rx, perm, sgo + El, D, xp);
+            // 4. local experts over the received rows, shared expert over the local rows
+            launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, Gm, U, SG, SU, xp, 8 * RC, h, T, perm,
+                                                            tiles, nt, 8 * RC, 0, D, I, El + 1, act, 8 * RC + T,
+                                                            c->d_err),
                                              L->bits, grid, st);
-            launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dm, Dm, SD, SD, act, 8 * Rn + T, nullptr, 0,
-                                                         perm, tiles, nt, 8 * Rn, 0, I, D, El + 1, y, 8 * Rn + T,
+            launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dm, Dm, SD, SD, act, 8 * RC + T, nullptr, 0,
+                                                         perm, tiles, nt, 8 * RC, 0, I, D, El + 1, y, 8 * RC + T,
                                                          c->d_err),
                                           L->bits, grid, st);
-            // 5. partial row sums back to the token owners, then the owner's combine
-            if (Rn > 0) {
-                const size_t n = (size_t)Rn * (D / 8);
-                ep_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(y, rpos, il, rmeta, Rn, D, El, z);
+            // 5. partial row sums straight back into the token owners, then the owner's combine
+            ep_reduce_send_kernel<<<std::min((RC + 7) / 8, 8 * c->sms), 256, 0, st>>>(
+                y, rpos, il, my_meta, my_sync, G, rank, cap, D, El, peers, my_sync + 3 * G + 2, c->d_err);
+            ep_combine_kernel<<<T, 256, 0, st>>>(my_back, sidx, G, cap, my_sync, target, peers, y + (size_t)8 * RC * D,
+                                                 gate, D, dx, l + 1 < n_layers ? dn + (size_t)(l + 1) * D : nullptr,
+                                                 eps, h, c->d_err);
+            if (launch_check(error, capacity)) {
+                ep->broken = true;  // the ranks' arrival counts no longer agree
+                return -1;
             }
-            NK(nc->groupStart());
-            for (int q = 0; q < G; ++q) {
-                if (rcnt[q]) NK(nc->send(z + (size_t)roff[q] * D, (size_t)rcnt[q] * D * 2, ncclUint8, q, ep->comm, st));
-                if (scnt[q]) NK(nc->recv(bk + (size_t)soff[q] * D, (size_t)scnt[q] * D * 2, ncclUint8, q, ep->comm, st));
-            }
-            NK(nc->groupEnd());
-            {
-                const size_t n = (size_t)T * (D / 8);
-                ep_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(bk, sidx, so, G, y + (size_t)8 * Rn * D, gate, T,
-                                                                                D, dx,
-                                                                                c->d_err);
-            }
-            if (launch_check(error, capacity)) return -1;
         }
         CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
         if (dev_io) CK(cudaEventRecord(c->ev_stop, st));
         CK(cudaStreamSynchronize(st));
+        // every kernel signalled its peers whatever happened, so the counts advanced by n_layers
+        // steps unless a wait ran out
+        ep->steps += (uint64_t)n_layers;
         if (*c->h_err) {
+            if (*c->h_err & kErrTimeout) ep->broken = true;
             set_error(error, capacity, "%s", device_error_text(*c->h_err));
             return -1;
         }

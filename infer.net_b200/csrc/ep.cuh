@@ -1,4 +1,5 @@
-// Expert-parallel dispatch / combine helpers (one process per GPU, NCCL between them).
+// Expert-parallel dispatch / combine (one process per GPU; the kernels write each other's
+// buffers directly over NVLink, NCCL only bootstraps the group).
 //
 // GPU r of G owns experts [r*E_l, (r+1)*E_l) of every layer and a contiguous shard of the
 // tokens. A token is sent once to every GPU that owns at least one of its 8 experts, with its
@@ -24,30 +25,49 @@ struct RowMeta {
 };
 
 // Single CTA of 1024 threads: for every local token t and GPU d, send_idx[t*G + d] = position
-// of t among the tokens sent to d (or -1), send_count[d], send_off[d] (exclusive scan).
+// of t among the tokens sent to d (or -1), send_count[d], send_off[d] (exclusive scan). Thread i
+// owns a contiguous token range; the per-destination exclusive scan over threads is a warp
+// shuffle scan plus a scan of the 32 warp totals.
 __global__ void __launch_bounds__(1024)
 ep_layout_kernel(const int32_t *__restrict__ ids, int T, int E_l, int G, int32_t *__restrict__ send_idx,
                  int32_t *__restrict__ send_count, int32_t *__restrict__ send_off) {
-    __shared__ int32_t part[1024][kMaxRanks + 1];
-    const int tid = threadIdx.x;
-    const int per = (T + 1023) / 1024, t0 = tid * per, t1 = min(t0 + per, T);
+    __shared__ int32_t wsum[32][kMaxRanks];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (T + 1023) / 1024, t0 = min(tid * per, T), t1 = min(t0 + per, T);
     int cnt[kMaxRanks] = {};
     for (int t = t0; t < t1; ++t) {
         uint32_t mask = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) mask |= 1u << (ids[(size_t)t * 8 + j] / E_l);
-        for (int d = 0; d < G; ++d) cnt[d] += (mask >> d) & 1u;
+#pragma unroll
+        for (int d = 0; d < kMaxRanks; ++d) cnt[d] += (mask >> d) & 1u;
     }
-    for (int d = 0; d < G; ++d) part[tid][d] = cnt[d];
-    __syncthreads();
-    if (tid < G) {  // exclusive scan over threads, per destination
-        int run = 0;
-        for (int i = 0; i < 1024; ++i) {
-            const int v = part[i][tid];
-            part[i][tid] = run;
-            run += v;
+    int pos[kMaxRanks];
+#pragma unroll
+    for (int d = 0; d < kMaxRanks; ++d) {
+        int v = cnt[d];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(kFull, v, o);
+            if (lane >= o) v += u;
         }
-        send_count[tid] = run;
+        pos[d] = v - cnt[d];  // exclusive within the warp
+        if (lane == 31) wsum[warp][d] = v;
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int d = 0; d < kMaxRanks; ++d) {
+            const int w = wsum[lane][d];
+            int v = w;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(kFull, v, o);
+                if (lane >= o) v += u;
+            }
+            wsum[lane][d] = v - w;  // exclusive over warps
+            if (lane == 31 && d < G) send_count[d] = v;
+        }
     }
     __syncthreads();
     if (tid == 0) {
@@ -57,49 +77,145 @@ ep_layout_kernel(const int32_t *__restrict__ ids, int T, int E_l, int G, int32_t
             run += send_count[d];
         }
     }
-    int pos[kMaxRanks];
-    for (int d = 0; d < G; ++d) pos[d] = part[tid][d];
+#pragma unroll
+    for (int d = 0; d < kMaxRanks; ++d) pos[d] += wsum[warp][d];
     for (int t = t0; t < t1; ++t) {
         uint32_t mask = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) mask |= 1u << (ids[(size_t)t * 8 + j] / E_l);
-        for (int d = 0; d < G; ++d) send_idx[(size_t)t * G + d] = ((mask >> d) & 1u) ? pos[d]++ : -1;
+#pragma unroll
+        for (int d = 0; d < kMaxRanks; ++d)
+            if (d < G) send_idx[(size_t)t * G + d] = ((mask >> d) & 1u) ? pos[d]++ : -1;
     }
 }
 
-// One CTA per local token: copies h[t] and its routing metadata into each destination's block
-// of the send buffers (row send_off[d] + send_idx[t, d]).
-__global__ void __launch_bounds__(256)
-ep_pack_kernel(const uint16_t *__restrict__ h, const int32_t *__restrict__ ids, const float *__restrict__ probs, int D,
-               int G, const int32_t *__restrict__ send_idx, const int32_t *__restrict__ send_off,
-               uint16_t *__restrict__ send_x, RowMeta *__restrict__ send_meta) {
-    const int t = blockIdx.x;
-    for (int d = 0; d < G; ++d) {
-        const int k = send_idx[(size_t)t * G + d];
-        if (k < 0) continue;
-        const size_t row = (size_t)send_off[d] + k;
-        const uint4 *src = reinterpret_cast<const uint4 *>(h + (size_t)t * D);
-        uint4 *dst = reinterpret_cast<uint4 *>(send_x + row * D);
-        for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = src[i];
-        if (threadIdx.x < 8) {
-            send_meta[row].ids[threadIdx.x] = ids[(size_t)t * 8 + threadIdx.x];
-            send_meta[row].probs[threadIdx.x] = probs[(size_t)t * 8 + threadIdx.x];
+// Symmetric buffers of one rank, mapped into every rank of the group (CUDA IPC over NVLink).
+// Region s of a buffer holds what rank s wrote into it, row k = the writer's send position k:
+//   rx   [G][cap][D] bf16   token rows dispatched to this rank
+//   meta [G][cap]           their expert ids and probabilities
+//   back [G][cap][D] bf16   partial rows returned to this rank (for the tokens it sent out)
+//   sync [4G+2] u32         [0,G) dispatch arrivals from rank s, [G,2G) combine arrivals,
+//                           [2G,3G) dispatch row counts, [3G] abort word, [3G+1], [3G+2]
+//                           this rank's CTA tickets of its dispatch and of its partial-row send
+// A writing kernel signals every rank once per layer step: each CTA fences its stores at system
+// scope and takes a ticket; the last CTA writes the row counts (dispatch), fences, and bumps the
+// arrival counter of every rank, so after step n it reads n. The last CTA also resets its ticket.
+struct EpPeers {
+    uint16_t *rx[kMaxRanks];
+    RowMeta *meta[kMaxRanks];
+    uint16_t *back[kMaxRanks];
+    uint32_t *sync[kMaxRanks];
+};
+
+// Thread 0 of a CTA: wait until counters ctr[0..G) all reach `target`. Fails fast on an earlier
+// timeout of this rank or an abort written by another rank; on its own timeout it sets the error
+// word and writes the abort word of every rank.
+__device__ inline bool ep_wait_counters(const uint32_t *ctr, int G, uint32_t target, const uint32_t *abort_word,
+                                        const EpPeers &peers, uint32_t *err) {
+    const uint64_t t0 = global_ns();
+    for (int s = 0; s < G; ++s) {
+        const volatile uint32_t *c = ctr + s;
+        for (uint32_t n = 0;; ++n) {
+            if ((int)(*c - target) >= 0) break;
+            if ((n & 63u) == 0) {
+                if ((*reinterpret_cast<const volatile uint32_t *>(err) & kErrTimeout) ||
+                    *reinterpret_cast<const volatile uint32_t *>(abort_word)) {
+                    atomicOr(err, kErrTimeout);
+                    return false;
+                }
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(err, kErrTimeout);
+                    for (int q = 0; q < G; ++q) atomicExch_system(peers.sync[q] + 3 * G, 1u);
+                    return false;
+                }
+            }
         }
     }
+    __threadfence();
+    return true;
 }
 
-// Receiver: local expert of every (row, slot) -- or E_l for a slot owned by another GPU -- and
-// the per-block histogram over E_l + 1 buckets (blocks of topk::TOK_PER_CTA rows).
+// Last-CTA signal of a writing kernel (all threads call it after their stores): arrival counter
+// `slot` of every rank + 1; the dispatch also publishes its row counts (counts != null).
+__device__ inline void ep_signal(uint32_t *ticket, const EpPeers &peers, int G, int slot, int count_slot,
+                                 const int32_t *counts) {
+    __shared__ uint32_t last;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x == 0) {
+        *ticket = 0;  // the next launch counts from zero (launches on one stream do not overlap)
+        __threadfence_system();
+        if (counts)
+            for (int q = 0; q < G; ++q) peers.sync[q][count_slot] = (uint32_t)counts[q];
+        __threadfence_system();
+        for (int q = 0; q < G; ++q) atomicAdd_system(peers.sync[q] + slot, 1u);
+    }
+}
+
+// Dispatch: one warp per local token copies its row (and its routing metadata) into region
+// `rank` of every destination's rx / meta (row send_idx[t, d]) by direct stores over NVLink.
 __global__ void __launch_bounds__(256)
-ep_recv_count_kernel(const RowMeta *__restrict__ meta, int R, int E_off, int E_l, int32_t *__restrict__ ids_local,
-                     int32_t *__restrict__ block_counts) {
+ep_dispatch_kernel(const uint16_t *__restrict__ h, const int32_t *__restrict__ ids, const float *__restrict__ probs,
+                   int T, int D, int G, int rank, int cap, const int32_t *__restrict__ send_idx,
+                   const int32_t *__restrict__ send_count, EpPeers peers, uint32_t *ticket) {
+    const int lane = threadIdx.x & 31, warps = gridDim.x * (blockDim.x >> 5);
+    for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(h + (size_t)t * D);
+        uint4 v[8];  // D <= 2048: 8 chunks of 16 bytes per lane
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            if (lane + 32 * c < D / 8) v[c] = src[lane + 32 * c];
+        int32_t id = 0;
+        float pr = 0.f;
+        if (lane < 8) {
+            id = ids[(size_t)t * 8 + lane];
+            pr = probs[(size_t)t * 8 + lane];
+        }
+        for (int d = 0; d < G; ++d) {
+            const int k = send_idx[(size_t)t * G + d];
+            if (k < 0) continue;
+            const size_t row = (size_t)rank * cap + k;
+            uint4 *dst = reinterpret_cast<uint4 *>(peers.rx[d] + row * D);
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                if (lane + 32 * c < D / 8) dst[lane + 32 * c] = v[c];
+            if (lane < 8) {
+                peers.meta[d][row].ids[lane] = id;
+                peers.meta[d][row].probs[lane] = pr;
+            }
+        }
+    }
+    ep_signal(ticket, peers, G, rank, 2 * G + rank, send_count);
+}
+
+// Receiver: waits for every rank's dispatch, then the local expert of every (row, slot) of the
+// G*cap row slots -- E_l for a slot owned by another rank or a row slot nobody filled -- and the
+// per-block histogram over E_l + 1 buckets (blocks of topk::TOK_PER_CTA rows).
+__global__ void __launch_bounds__(256)
+ep_recv_routes_kernel(const RowMeta *__restrict__ meta, const uint32_t *__restrict__ sync, uint32_t target, int G,
+                      int cap, int E_off, int E_l, EpPeers peers, int32_t *__restrict__ ids_local,
+                      int32_t *__restrict__ block_counts, uint32_t *__restrict__ err) {
     __shared__ int32_t hist[kMaxBuckets];
+    __shared__ int32_t cnt[kMaxRanks];
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        ok = ep_wait_counters(sync, G, target, sync + 3 * G, peers, err);
+        for (int s = 0; s < G; ++s) cnt[s] = (int)*reinterpret_cast<const volatile uint32_t *>(sync + 2 * G + s);
+    }
     for (int i = threadIdx.x; i <= E_l; i += blockDim.x) hist[i] = 0;
     __syncthreads();
+    const int R = G * cap;
     const int r0 = blockIdx.x * topk::TOK_PER_CTA * 8;
     for (int r = r0 + threadIdx.x; r < min(r0 + topk::TOK_PER_CTA * 8, R * 8); r += blockDim.x) {
-        const int e = meta[r >> 3].ids[r & 7] - E_off;
-        const int b = (e >= 0 && e < E_l) ? e : E_l;
+        const int i = r >> 3, s = i / cap;
+        int b = E_l;
+        if (ok && i - s * cap < cnt[s]) {
+            const int e = __ldcg(&meta[i].ids[r & 7]) - E_off;
+            if (e >= 0 && e < E_l) b = e;
+        }
         ids_local[r] = b;
         atomicAdd(&hist[b], 1);
     }
@@ -107,69 +223,138 @@ ep_recv_count_kernel(const RowMeta *__restrict__ meta, int R, int E_off, int E_l
     for (int i = threadIdx.x; i <= E_l; i += blockDim.x) block_counts[(size_t)blockIdx.x * (E_l + 1) + i] = hist[i];
 }
 
-// Receiver: z[i] = sum over local slots j (slot order) of p[i,j] * y[8i+j], f32 then bf16; the
-// expert rows are stored in expert order, y[8i+j] = yp[route_pos[8i+j]].
-__global__ void ep_reduce_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__ route_pos,
-                                 const int32_t *__restrict__ ids_local,
-                                 const RowMeta *__restrict__ meta, int R, int D, int E_l, uint16_t *__restrict__ z) {
-    const int per_row = D / 8;
-    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (size_t)R * per_row) return;
-    const int i = idx / per_row, c = (idx % per_row) * 8;
-    float o[8] = {};
+// Receiver: one warp per filled row (s, k): partial row z = sum over its local slots j (slot
+// order) of p_j * y_j (f32, then bf16), stored straight into region `rank` of rank s's back
+// buffer (row k). y_j = yp[route_pos[8i + j]] (expert rows in expert order).
+__global__ void __launch_bounds__(256)
+ep_reduce_send_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__ route_pos,
+                      const int32_t *__restrict__ ids_local, const RowMeta *__restrict__ meta,
+                      const uint32_t *__restrict__ sync, int G, int rank, int cap, int D, int E_l, EpPeers peers,
+                      uint32_t *ticket, const uint32_t *__restrict__ err) {
+    __shared__ int32_t cnt[kMaxRanks];
+    if (threadIdx.x < G) cnt[threadIdx.x] = (int)__ldcg(sync + 2 * G + threadIdx.x);
+    __syncthreads();
+    const bool live = !(*reinterpret_cast<const volatile uint32_t *>(err) & kErrTimeout);
+    const int lane = threadIdx.x & 31, warps = gridDim.x * (blockDim.x >> 5);
+    for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); live && i < G * cap; i += warps) {
+        const int s = i / cap, k = i - s * cap;
+        if (k >= cnt[s]) continue;
+        // slot j's position and weight in lane j (weight 0: not a local slot)
+        int pos = 0;
+        float p = 0.f;
+        if (lane < 8 && ids_local[(size_t)i * 8 + lane] < E_l) {
+            pos = route_pos[(size_t)i * 8 + lane];
+            p = __ldcg(&meta[i].probs[lane]);
+        }
+        uint16_t *dst = peers.back[s] + ((size_t)rank * cap + k) * D;
+        float pj[8];
+        int rj[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        if (ids_local[(size_t)i * 8 + j] >= E_l) continue;
-        const float p = meta[i].probs[j];
-        const uint4 v = *reinterpret_cast<const uint4 *>(yp + (size_t)route_pos[(size_t)i * 8 + j] * D + c);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        for (int j = 0; j < 8; ++j) {
+            pj[j] = __shfl_sync(kFull, p, j);
+            rj[j] = __shfl_sync(kFull, pos, j);
+        }
+        for (int c = lane; c < D / 8; c += 32) {
+            uint4 v8[8];  // the local slots' chunks, all requested before any is used
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float prod = p * ((k & 1) ? bf16_hi(w[k >> 1]) : bf16_lo(w[k >> 1]));
-            o[k] = o[k] + prod;
+            for (int j = 0; j < 8; ++j)
+                v8[j] = pj[j] != 0.f ? *reinterpret_cast<const uint4 *>(yp + (size_t)rj[j] * D + c * 8) : make_uint4(0, 0, 0, 0);
+            float o[8] = {};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (pj[j] == 0.f) continue;
+                const uint4 v = v8[j];
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const float prod = pj[j] * ((m & 1) ? bf16_hi(w[m >> 1]) : bf16_lo(w[m >> 1]));
+                    o[m] = o[m] + prod;
+                }
+            }
+            uint4 r;
+            r.x = pack_bf16x2(o[0], o[1]);
+            r.y = pack_bf16x2(o[2], o[3]);
+            r.z = pack_bf16x2(o[4], o[5]);
+            r.w = pack_bf16x2(o[6], o[7]);
+            reinterpret_cast<uint4 *>(dst)[c] = r;
         }
     }
-    uint4 r;
-    r.x = pack_bf16x2(o[0], o[1]);
-    r.y = pack_bf16x2(o[2], o[3]);
-    r.z = pack_bf16x2(o[4], o[5]);
-    r.w = pack_bf16x2(o[6], o[7]);
-    *reinterpret_cast<uint4 *>(z + (size_t)i * D + c) = r;
+    ep_signal(ticket, peers, G, G + rank, 0, nullptr);
 }
 
-// Owner: out[t] = sigmoid(gate_t) * ys[t] + sum_d back[send_off[d] + send_idx[t, d]] (ascending
-// d); resid[t] += out.
-__global__ void ep_combine_kernel(const uint16_t *__restrict__ back, const int32_t *__restrict__ send_idx,
-                                  const int32_t *__restrict__ send_off, int G, const uint16_t *__restrict__ ys,
-                                  const float *__restrict__ gate_logit, int T, int D, float *__restrict__ resid,
-                                  const uint32_t *__restrict__ err) {
-    const int per_tok = D / 8;
-    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (size_t)T * per_tok) return;
-    if (*err) return;
-    const int t = idx / per_tok, c = (idx % per_tok) * 8;
+// Owner, one CTA of 256 threads per local token: waits for every rank's partial rows, then
+// out[t] = sigmoid(gate_t) * ys[t] + sum over ranks d (ascending) of back[d][send_idx[t, d]];
+// resid[t] += out; and, when norm_w is given, the next layer's input row h[t] = bf16(resid[t] *
+// rsqrt(mean(resid[t]^2) + eps) * norm_w) (gpu_graph.mm:48-61).
+__global__ void __launch_bounds__(256)
+ep_combine_kernel(const uint16_t *__restrict__ back, const int32_t *__restrict__ send_idx, int G, int cap,
+                  const uint32_t *__restrict__ sync, uint32_t target, EpPeers peers, const uint16_t *__restrict__ ys,
+                  const float *__restrict__ gate_logit, int D, float *__restrict__ resid,
+                  const float *__restrict__ norm_w, float eps, uint16_t *__restrict__ h, uint32_t *__restrict__ err) {
+    __shared__ int ok;
+    __shared__ float part[8];
+    if (threadIdx.x == 0) ok = ep_wait_counters(sync + G, G, target, sync + 3 * G, peers, err);
+    __syncthreads();
+    if (!ok) return;
+    const int t = blockIdx.x, tid = threadIdx.x;
     const float g = sigmoid_ref(gate_logit[t]);
-    float o[8];
-    {
-        const uint4 v = *reinterpret_cast<const uint4 *>(ys + (size_t)t * D + c);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    int32_t row[kMaxRanks];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) o[k] = ((k & 1) ? bf16_hi(w[k >> 1]) : bf16_lo(w[k >> 1])) * g;
-    }
-    for (int d = 0; d < G; ++d) {
-        const int k = send_idx[(size_t)t * G + d];
-        if (k < 0) continue;
-        const uint4 v = *reinterpret_cast<const uint4 *>(back + ((size_t)send_off[d] + k) * D + c);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int d = 0; d < kMaxRanks; ++d) row[d] = d < G ? send_idx[(size_t)t * G + d] : -1;
+    float r[1][8];  // D <= 2048: one chunk of 8 per thread
+    float ss = 0.f;
 #pragma unroll
-        for (int m = 0; m < 8; ++m) o[m] = o[m] + ((m & 1) ? bf16_hi(w[m >> 1]) : bf16_lo(w[m >> 1]));
+    for (int k = 0; k < 1; ++k) {
+        const int c = (tid + k * 256) * 8;
+        if (c >= D) break;
+        float o[8];
+        {
+            const uint4 v = *reinterpret_cast<const uint4 *>(ys + (size_t)t * D + c);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = ((j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1])) * g;
+        }
+#pragma unroll
+        for (int d = 0; d < kMaxRanks; ++d) {
+            if (row[d] < 0) continue;
+            const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(back + ((size_t)d * cap + row[d]) * D + c));
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int m = 0; m < 8; ++m) o[m] = o[m] + ((m & 1) ? bf16_hi(w[m >> 1]) : bf16_lo(w[m >> 1]));
+        }
+        float4 *rp = reinterpret_cast<float4 *>(resid + (size_t)t * D + c);
+        float4 a = rp[0], b = rp[1];
+        a.x += o[0]; a.y += o[1]; a.z += o[2]; a.w += o[3];
+        b.x += o[4]; b.y += o[5]; b.z += o[6]; b.w += o[7];
+        rp[0] = a;
+        rp[1] = b;
+        r[k][0] = a.x; r[k][1] = a.y; r[k][2] = a.z; r[k][3] = a.w;
+        r[k][4] = b.x; r[k][5] = b.y; r[k][6] = b.z; r[k][7] = b.w;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(r[k][j], r[k][j], ss);
     }
-    float4 *rp = reinterpret_cast<float4 *>(resid + (size_t)t * D + c);
-    float4 a = rp[0], b = rp[1];
-    a.x += o[0]; a.y += o[1]; a.z += o[2]; a.w += o[3];
-    b.x += o[4]; b.y += o[5]; b.z += o[6]; b.w += o[7];
-    rp[0] = a;
-    rp[1] = b;
+    if (!norm_w) return;
+#pragma unroll
+    for (int n = 16; n; n >>= 1) ss += __shfl_xor_sync(kFull, ss, n);
+    if ((tid & 31) == 0) part[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += part[i];
+    const float scale = 1.0f / sqrtf(tot / (float)D + eps);
+#pragma unroll
+    for (int k = 0; k < 1; ++k) {
+        const int c = (tid + k * 256) * 8;
+        if (c >= D) break;
+        const float4 w0 = *reinterpret_cast<const float4 *>(norm_w + c), w1 = *reinterpret_cast<const float4 *>(norm_w + c + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint4 o;
+        o.x = pack_bf16x2(r[k][0] * scale * wv[0], r[k][1] * scale * wv[1]);
+        o.y = pack_bf16x2(r[k][2] * scale * wv[2], r[k][3] * scale * wv[3]);
+        o.z = pack_bf16x2(r[k][4] * scale * wv[4], r[k][5] * scale * wv[5]);
+        o.w = pack_bf16x2(r[k][6] * scale * wv[6], r[k][7] * scale * wv[7]);
+        *reinterpret_cast<uint4 *>(h + (size_t)t * D + c) = o;
+    }
 }
 
 }  // namespace di

@@ -2,7 +2,9 @@
 
 Builds a small model twice -- full layers on every rank and the rank's expert shard -- runs the
 expert-parallel stack on uneven contiguous token shards and compares the rows against the
-single-GPU stack on all tokens. Exits non-zero on a mismatch.
+single-GPU stack on all tokens. The same call is made twice (the second must repeat the first bit
+for bit: the peer buffers' arrival counters carry over between calls), then once with three times
+the tokens (every rank grows and re-maps its peer buffers). Exits non-zero on a mismatch.
 """
 import datetime
 import os
@@ -33,17 +35,30 @@ ep = di.ExpertParallel(ctx, bytes(uid.cpu().numpy().tobytes()), rank, world)
 shards = [ep.layer(di.generate_layer_matrices(ctx, SEED, l, bits, E, D, I, shard=(rank, world))) for l in range(L)]
 full = [di.MoeLayer(ctx, di.generate_layer_matrices(ctx, SEED, l, bits, E, D, I)) for l in range(L)]
 rng = np.random.default_rng(5)
-x = rng.standard_normal((T, D)).astype(np.float32)
 norms = (1.0 + 0.1 * np.cos(np.arange(L * D))).astype(np.float32).reshape(L, D)
-lo = sum(sizes[:rank])
-xs = x[lo:lo + sizes[rank]].copy()
-ep.stack(shards, norms, xs, sizes[rank], 1e-6, 0)
-ref, _, _, _ = di.moe_stack(ctx, full, norms, x, 1e-6, di.PATH_GROUPED)
-ref = ref[lo:lo + sizes[rank]]
-err = np.abs(xs.astype(np.float64) - ref)
-rel = np.linalg.norm(xs - ref) / np.linalg.norm(ref)
-ok = float(err.max()) <= 2e-2 and rel <= 5e-3
-print(f"rank {rank}: rows {sizes[rank]} max_abs {err.max():.3e} rel_l2 {rel:.3e} ok {ok}", flush=True)
+
+
+def check(sizes, label, previous=None):
+    T = sum(sizes)
+    x = rng.standard_normal((T, D)).astype(np.float32) if previous is None else previous[0]
+    lo = sum(sizes[:rank])
+    xs = x[lo:lo + sizes[rank]].copy()
+    ep.stack(shards, norms, xs, sizes[rank], 1e-6, 0)
+    ref, _, _, _ = di.moe_stack(ctx, full, norms, x, 1e-6, di.PATH_GROUPED)
+    ref = ref[lo:lo + sizes[rank]]
+    err = np.abs(xs.astype(np.float64) - ref)
+    rel = np.linalg.norm(xs - ref) / np.linalg.norm(ref)
+    ok = float(err.max()) <= 2e-2 and rel <= 5e-3
+    if previous is not None:
+        ok = ok and np.array_equal(xs, previous[1])
+    print(f"rank {rank} {label}: rows {sizes[rank]} max_abs {err.max():.3e} rel_l2 {rel:.3e} ok {ok}", flush=True)
+    return ok, (x, xs)
+
+
+ok1, first = check(sizes, "first")
+ok2, _ = check(sizes, "repeat", previous=first)
+ok3, _ = check([3 * n for n in sizes], "grown")
+ok = ok1 and ok2 and ok3
 flag = torch.tensor([0 if ok else 1], device="cuda")
 dist.all_reduce(flag)
 for l in shards + full:
