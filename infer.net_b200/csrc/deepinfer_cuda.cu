@@ -1877,8 +1877,9 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                                                                   c->d_err);
             // 2. one row per (token, destination rank), written into the destinations over NVLink
             ep_layout_kernel<<<1, 1024, 0, st>>>(ids, T, El, G, sidx, sc, so);
-            ep_dispatch_kernel<<<std::min((T + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank, cap,
-                                                                                  sidx, sc, peers, my_sync + 3 * G + 1);
+            ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
+                                                                                      cap, sidx, sc, peers,
+                                                                                      my_sync + 3 * G + 1);
             // 3. the rows every rank sent here -> local routes, expert segments, GEMM tiles
             ep_recv_routes_kernel<<<nbr, 256, 0, st>>>(my_meta, my_sync, target, G, cap, L->E_off, El, peers, il, rbc,
                                                        c->d_err);

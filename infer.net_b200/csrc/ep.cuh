@@ -155,37 +155,30 @@ __device__ inline void ep_signal(uint32_t *ticket, const EpPeers &peers, int G, 
     }
 }
 
-// Dispatch: one warp per local token copies its row (and its routing metadata) into region
-// `rank` of every destination's rx / meta (row send_idx[t, d]) by direct stores over NVLink.
+// Dispatch: one warp per (local token t, destination d) pair copies t's row (and its routing
+// metadata) into region `rank` of d's rx / meta (row send_idx[t, d]) by direct stores over NVLink.
 __global__ void __launch_bounds__(256)
 ep_dispatch_kernel(const uint16_t *__restrict__ h, const int32_t *__restrict__ ids, const float *__restrict__ probs,
                    int T, int D, int G, int rank, int cap, const int32_t *__restrict__ send_idx,
                    const int32_t *__restrict__ send_count, EpPeers peers, uint32_t *ticket) {
     const int lane = threadIdx.x & 31, warps = gridDim.x * (blockDim.x >> 5);
-    for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+    for (int td = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); td < T * G; td += warps) {
+        const int t = td / G, d = td - t * G;
+        const int k = send_idx[td];
+        if (k < 0) continue;
         const uint4 *src = reinterpret_cast<const uint4 *>(h + (size_t)t * D);
         uint4 v[8];  // D <= 2048: 8 chunks of 16 bytes per lane
 #pragma unroll
         for (int c = 0; c < 8; ++c)
             if (lane + 32 * c < D / 8) v[c] = src[lane + 32 * c];
-        int32_t id = 0;
-        float pr = 0.f;
-        if (lane < 8) {
-            id = ids[(size_t)t * 8 + lane];
-            pr = probs[(size_t)t * 8 + lane];
-        }
-        for (int d = 0; d < G; ++d) {
-            const int k = send_idx[(size_t)t * G + d];
-            if (k < 0) continue;
-            const size_t row = (size_t)rank * cap + k;
-            uint4 *dst = reinterpret_cast<uint4 *>(peers.rx[d] + row * D);
+        const size_t row = (size_t)rank * cap + k;
+        uint4 *dst = reinterpret_cast<uint4 *>(peers.rx[d] + row * D);
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
-                if (lane + 32 * c < D / 8) dst[lane + 32 * c] = v[c];
-            if (lane < 8) {
-                peers.meta[d][row].ids[lane] = id;
-                peers.meta[d][row].probs[lane] = pr;
-            }
+        for (int c = 0; c < 8; ++c)
+            if (lane + 32 * c < D / 8) dst[lane + 32 * c] = v[c];
+        if (lane < 8) {
+            peers.meta[d][row].ids[lane] = ids[(size_t)t * 8 + lane];
+            peers.meta[d][row].probs[lane] = probs[(size_t)t * 8 + lane];
         }
     }
     ep_signal(ticket, peers, G, rank, 2 * G + rank, send_count);

@@ -329,7 +329,7 @@ __device__ __forceinline__ void select_top8(const float *v, int E, int32_t *sel,
 }
 
 namespace topk {
-constexpr int WARPS = 8, TOK_PER_WARP = 8, TOK_PER_CTA = WARPS * TOK_PER_WARP;  // 64 tokens = 512 routes
+constexpr int WARPS = 16, TOK_PER_WARP = 4, TOK_PER_CTA = WARPS * TOK_PER_WARP;  // 64 tokens = 512 routes
 }
 
 __global__ void __launch_bounds__(topk::WARPS * 32)
