@@ -175,6 +175,17 @@ def run_ours(args):
         return ms.value
 
     norms_host = np.ones((LAYERS, D), np.float32)
+    if args.only_decode:  # profiling case: the batch-1 decode stack alone
+        x1 = x0[:1].clone()
+        for _ in range(args.warmup):
+            x1.copy_(x0[:1])
+            stack(x1.data_ptr(), 1, di.DEVICE_IO | di.PATH_GEMV)
+        dms = []
+        for _ in range(args.steps):
+            x1.copy_(x0[:1])
+            dms.append(stack(x1.data_ptr(), 1, di.DEVICE_IO | di.PATH_GEMV))
+        print(json.dumps({"decode_us_per_token": 1e3 * sum(dms) / len(dms), "layers": LAYERS, "steps": args.steps}))
+        return
     flags = di.DEVICE_IO | di.PATH_GROUPED | di.PROFILE
     # ---- device-resident timed region (value)
     for _ in range(args.warmup):
@@ -368,6 +379,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling case: fewer stacked layers")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="profiling case: fewer prefill tokens")
     ap.add_argument("--only-prefill", action="store_true", help="profiling case: skip the e2e and decode legs")
+    ap.add_argument("--only-decode", action="store_true", help="profiling case: only the batch-1 decode stack")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
