@@ -464,6 +464,9 @@ struct BlockBuffers {
     Tile *tiles;
     uint16_t *act, *yr, *ys, *xp;
     float *act32;
+    float *wn;             // router row norms (tensor-core router): ||r_e||, then ||W_e||
+    Tile *rtiles;          // work tiles of the approximate-logit GEMM
+    int32_t *rnt;
     uint32_t *counter;  // [0] last-CTA ticket of decode_route_kernel (kept at zero between launches),
                         // [1] grid-barrier arrivals of decode_ffn_kernel (zeroed per call)
     int nblocks, max_tiles;
@@ -492,6 +495,8 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     size_t o_xp = gemv ? 0 : cv.take<uint16_t>((size_t)T * 8 * D);
     size_t o_a32 = gemv ? cv.take<float>((size_t)T * 9 * I) : 0;
     size_t o_ctr = cv.take<uint32_t>(2);
+    size_t o_wn = cv.take<float>(2 * (size_t)E), o_rt = cv.take<Tile>((size_t)(T + 255) / 256 + 1);
+    size_t o_rnt = cv.take<int32_t>(1);
     size_t need = cv.off + 256;
     ensure_workspace(c, need);
     b.x = host_io ? at<uint16_t>(c, o_x) : nullptr;
@@ -514,8 +519,35 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     b.xp = gemv ? nullptr : at<uint16_t>(c, o_xp);
     b.act32 = gemv ? at<float>(c, o_a32) : nullptr;
     b.counter = at<uint32_t>(c, o_ctr);
+    b.wn = at<float>(c, o_wn);
+    b.rtiles = at<Tile>(c, o_rt);
+    b.rnt = at<int32_t>(c, o_rnt);
     return need;
 }
+
+// Routing of a prefill-sized batch (E a multiple of 128) in two steps (route.cuh): approximate
+// logits on the tensor cores (approx: scratch of T*E bf16) with the router rows' norms, then the
+// exact canonical logits of the candidates only -> ids, probs, gate logits, per-block route counts.
+void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, float *wn, Tile *rtiles, int32_t *rnt,
+                           uint16_t *approx, int grid, uint32_t *err, cudaStream_t st) {
+    const int E = L->E, D = L->D;
+    const QView R = L->m[0]->view();
+    router_row_norms_kernel<<<(E + 7) / 8, 256, 0, st>>>(R, E, D, wn);
+    router_tiles_kernel<<<1, 256, 0, st>>>(T, rtiles, rnt);
+    launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, R, R, R, R, x, T, nullptr, 0, nullptr, rtiles, rnt, T,
+                                                 0, D, E, 1, approx, T, err),
+                                  8, grid, st);
+}
+void enqueue_router_select(const Layer *L, const uint16_t *x, int T, const int32_t *forced, int32_t *ids,
+                           float *probs, float *gate, int32_t *block_counts, int nblocks, const float *wn,
+                           const uint16_t *approx, uint32_t *err, cudaStream_t st) {
+    const int E = L->E, D = L->D;
+    const QView R = L->m[0]->view(), SR = L->m[7]->view();
+    CK(cudaMemsetAsync(block_counts, 0, sizeof(int32_t) * (size_t)nblocks * E, st));
+    router_select_kernel<<<(T + 7) / 8, 256, 0, st>>>(approx, wn, x, T, E, D, R, SR, L->bias, forced, ids, probs, gate,
+                                                      block_counts, err);
+}
+bool router_tc_fits(const Layer *L) { return L->E % 128 == 0 && L->D <= 2048; }
 
 cudaEvent_t *g_marks = nullptr;  // event array the current enqueue records into
 void stage_mark(Context *c, int s) { CK(cudaEventRecord(g_marks ? g_marks[s] : c->ev_stage[s], c->stream)); }
@@ -592,17 +624,26 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
         }
         return;
     }
-    // 1. router logits (canonical f32 order)
-    if (gemv) {
-        router_logits_gemv_kernel<<<(E * 32 + 255) / 256, 256, 0, st>>>(x, T, D, R, L->bias, b.logits);
+    // 1-2. router logits, top-8, probabilities, shared gate logit, per-block expert counts
+    if (!gemv && router_tc_fits(L)) {
+        // tensor-core approximate logits + exact canonical logits of the candidates
+        uint16_t *approx = reinterpret_cast<uint16_t *>(b.logits);
+        enqueue_router_approx(L, x, T, b.wn, b.rtiles, b.rnt, approx, c->sms, c->d_err, st);
+        if (profile) stage_mark(c, S_TOPK);
+        enqueue_router_select(L, x, T, forced_ids, ids, probs, b.gate, b.block_counts, b.nblocks, b.wn, approx,
+                              c->d_err, st);
     } else {
-        dim3 grid((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE);
-        router_logits_kernel<<<grid, router::THREADS, sizeof(router::Smem), st>>>(x, T, D, R, L->bias, b.logits);
+        // every logit in the canonical f32 order
+        if (gemv) {
+            router_logits_gemv_kernel<<<(E * 32 + 255) / 256, 256, 0, st>>>(x, T, D, R, L->bias, b.logits);
+        } else {
+            dim3 grid((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE);
+            router_logits_kernel<<<grid, router::THREADS, sizeof(router::Smem), st>>>(x, T, D, R, L->bias, b.logits);
+        }
+        if (profile) stage_mark(c, S_TOPK);
+        topk_count_kernel<<<b.nblocks, topk::WARPS * 32, 0, st>>>(b.logits, T, E, x, D, SR, forced_ids, ids, probs,
+                                                                   b.gate, b.block_counts, c->d_err);
     }
-    if (profile) stage_mark(c, S_TOPK);
-    // 2. top-8 + probabilities + shared gate logit + per-block expert counts
-    topk_count_kernel<<<b.nblocks, topk::WARPS * 32, 0, st>>>(b.logits, T, E, x, D, SR, forced_ids, ids, probs,
-                                                               b.gate, b.block_counts, c->d_err);
     if (gemv) {
         if (profile) {
             stage_mark(c, S_SCAN);
@@ -1844,6 +1885,8 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         const size_t o_pm = cv.take<int32_t>((size_t)RC * 8 + 8), o_act = cv.take<uint16_t>(((size_t)RC * 8 + T) * I);
         const size_t o_y = cv.take<uint16_t>(((size_t)RC * 8 + T) * D + 8), o_rp = cv.take<int32_t>((size_t)RC * 8 + 8);
         const size_t o_xp = cv.take<uint16_t>((size_t)RC * 8 * D + 8);
+        const size_t o_wn = cv.take<float>(2 * (size_t)E), o_rt = cv.take<Tile>((size_t)(T + 255) / 256 + 1);
+        const size_t o_rnt = cv.take<int32_t>(1);
         ensure_workspace(c, cv.off + 256);
         float *dx = dev_io ? x : at<float>(c, o_x);
         const float *dn = dev_io ? norms : at<float>(c, o_n);
@@ -1857,6 +1900,9 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         int32_t *sgc = at<int32_t>(c, o_sgc), *sgo = at<int32_t>(c, o_sgo), *nt = at<int32_t>(c, o_nt);
         int32_t *perm = at<int32_t>(c, o_pm);
         Tile *tiles = at<Tile>(c, o_t);
+        float *wn = at<float>(c, o_wn);
+        Tile *rtiles = at<Tile>(c, o_rt);
+        int32_t *rnt = at<int32_t>(c, o_rnt);
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st));
         CK(cudaEventRecord(c->ev_start, st));
         if (!dev_io) {
@@ -1871,10 +1917,16 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             const uint32_t target = (uint32_t)(ep->steps + (uint64_t)l + 1);  // arrivals per rank so far
             // 1. route the local tokens (layer l's RMSNorm ran in layer l-1's combine)
             if (l == 0) rmsnorm_kernel<<<T, 256, 0, st>>>(dx, dn, D, eps, h, nullptr);
-            router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
-                                   router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);
-            topk_count_kernel<<<nb_l, topk::WARPS * 32, 0, st>>>(logits, T, E, h, D, SR, nullptr, ids, probs, gate, bc,
-                                                                  c->d_err);
+            if (router_tc_fits(L)) {
+                uint16_t *approx = reinterpret_cast<uint16_t *>(logits);
+                enqueue_router_approx(L, h, T, wn, rtiles, rnt, approx, grid, c->d_err, st);
+                enqueue_router_select(L, h, T, nullptr, ids, probs, gate, bc, nb_l, wn, approx, c->d_err, st);
+            } else {
+                router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
+                                       router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);
+                topk_count_kernel<<<nb_l, topk::WARPS * 32, 0, st>>>(logits, T, E, h, D, SR, nullptr, ids, probs, gate,
+                                                                      bc, c->d_err);
+            }
             // 2. one row per (token, destination rank), written into the destinations over NVLink
             ep_layout_kernel<<<1, 1024, 0, st>>>(ids, T, El, G, sidx, sc, so);
             ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,

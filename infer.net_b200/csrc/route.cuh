@@ -670,4 +670,261 @@ __global__ void combine_kernel(const uint16_t *__restrict__ yp, const int32_t *_
     }
 }
 
+// ------------------------------------------------------------------ router: tensor cores + exact check
+//
+// The routing ids must be those of the canonical f32 logits, which the tensor cores cannot
+// produce. But they can bound them. Approximate logits a[t, e] come from the grouped GEMM (DOWN
+// mode, one "expert" = the router matrix, bf16 output): its weights are W' = bf16(W), W = fma(q,
+// s, b) as the canonical order computes them, its products are exact and its f32 accumulation
+// over K <= 2048 errs by far less than 2^-13 sum|W x|. With r_e = W'_e - W_e (known from the
+// weights),
+//   |a[t,e] - logit[t,e]| <= ||r_e|| ||x_t|| + 2^-13 ||W_e|| ||x_t|| + 2^-8 |a[t,e]|  =: eps[t,e]
+// (Cauchy-Schwarz; the last term covers the bf16 output rounding, 2^-9 |A|, twice over; the
+// canonical order's own f32 error is below 2^-17 ||W|| ||x||). An expert can be among the true
+// top-8 only if a + eps >= L8, the 8th largest a - eps. Those candidates (about 10 of 256) are
+// recomputed in the canonical order and the top-8 is selected from the exact values, so ids,
+// ties and probabilities equal the all-exact router's.
+constexpr float kRouterAccumRel = 0x1p-13f;
+constexpr float kRouterOutRel = 0x1p-8f;
+constexpr float kNormMargin = 1.0f + 0x1p-10f;  // f32 rounding of the norms themselves
+constexpr int kRouterMaxCand = 64;             // above this a token falls back to all experts
+
+// ||r_e||, ||W_e|| of every router row (rows < E) into wn[e], wn[E + e]; one warp per row.
+__global__ void __launch_bounds__(256) router_row_norms_kernel(QView R, int E, int D, float *__restrict__ wn) {
+    const int e = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (e >= E) return;
+    const uint32_t *w = R.packed + (size_t)e * R.words_per_row();
+    float rr = 0.f, ww = 0.f;
+    for (int c = lane * 4; c < D; c += 128) {  // 4 codes (one word) per lane per step
+        const uint32_t q4 = w[c / 4];
+        const float s = bf16_bits_to_f32(R.scales[(size_t)e * R.groups_per_row() + c / 64]);
+        const float b = bf16_bits_to_f32(R.biases[(size_t)e * R.groups_per_row() + c / 64]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float W = fmaf(byte_to_f32(q4, j), s, b);
+            const float r = bf16_bits_to_f32(f32_to_bf16_bits(W)) - W;  // exact (Sterbenz)
+            rr = fmaf(r, r, rr);
+            ww = fmaf(W, W, ww);
+        }
+    }
+    rr = warp_sum_butterfly(rr);
+    ww = warp_sum_butterfly(ww);
+    if (lane == 0) {
+        wn[e] = sqrtf(rr) * kNormMargin;
+        wn[E + e] = sqrtf(ww) * kNormMargin;
+    }
+}
+
+// Work tiles of the approximate-logit GEMM: segment 0, 256 tokens each.
+__global__ void router_tiles_kernel(int T, Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles) {
+    const int n = (T + 255) / 256;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) tiles[i] = Tile{0, i * 256, min(256, T - i * 256)};
+    if (threadIdx.x == 0) *n_tiles = n;
+}
+
+// The canonical dot product (canonical_dot_warp) with the activation row held in registers: xr[k]
+// = x[256k + 8 lane .. +8] (bf16).
+__device__ __forceinline__ float canonical_dot_xreg(const QView &m, int row, const uint4 (&xr)[8], int D) {
+    const uint32_t lane = lane_id();
+    const uint32_t *w = m.packed + (size_t)row * m.words_per_row();
+    const uint16_t *sc = m.scales + (size_t)row * m.groups_per_row();
+    const uint16_t *bi = m.biases + (size_t)row * m.groups_per_row();
+    uint2 q[8];
+    uint16_t sv[8], bv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        if (k * 256 < D) {
+            const int base = k * 256 + lane * 8;
+            q[k] = __ldg(reinterpret_cast<const uint2 *>(w + base / 4));
+            sv[k] = __ldg(sc + base / 64);
+            bv[k] = __ldg(bi + base / 64);
+        }
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        if (k * 256 >= D) break;
+        const float s = bf16_bits_to_f32(sv[k]), bb = bf16_bits_to_f32(bv[k]);
+        const uint32_t xw[4] = {xr[k].x, xr[k].y, xr[k].z, xr[k].w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float wv = fmaf(byte_to_f32(j < 4 ? q[k].x : q[k].y, j & 3), s, bb);
+            const float xf = (j & 1) ? bf16_hi(xw[j >> 1]) : bf16_lo(xw[j >> 1]);
+            acc = fmaf(wv, xf, acc);
+        }
+    }
+    return warp_sum_butterfly(acc);
+}
+
+// The 8 largest of up to 64 (value, id) entries, two per lane (slots 0 and 1; absent entries have
+// key 0), descending with ties to the lower id; all lanes return the same sel/chosen.
+__device__ __forceinline__ void select_top8_pairs(float v0, uint32_t id0, bool has0, float v1, uint32_t id1, bool has1,
+                                                  int32_t *sel, float *chosen) {
+    uint32_t k0 = has0 ? order_key(v0) : 0u, k1 = has1 ? order_key(v1) : 0u;
+    if (k1 > k0 || (k1 == k0 && id1 < id0)) {  // slot 0 holds the lane's better entry
+        uint32_t t = k0; k0 = k1; k1 = t;
+        t = id0; id0 = id1; id1 = t;
+    }
+    if (!has0 && !has1) id0 = id1 = 0xffffffffu;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+        const uint32_t best = __reduce_max_sync(kFull, k0);
+        const uint32_t win = __reduce_min_sync(kFull, k0 == best ? id0 : 0xffffffffu);
+        sel[n] = (int32_t)win;
+        chosen[n] = key_value(best);
+        if (id0 == win && k0 == best) {
+            k0 = k1;
+            id0 = id1;
+            k1 = 0u;
+            id1 = 0xffffffffu;
+        }
+    }
+}
+
+// One warp per token: approximate logits -> candidates -> exact logits -> top-8, softmax, the
+// shared-route gate logit, and the route counts of the token's 64-token block (block_counts zeroed
+// beforehand). forced: the token's 8 ids are given (their exact logits give the probabilities).
+__global__ void __launch_bounds__(256)
+router_select_kernel(const uint16_t *__restrict__ approx, const float *__restrict__ wn, const uint16_t *__restrict__ x,
+                     int T, int E, int D, QView R, QView SR, const float *__restrict__ bias,
+                     const int32_t *__restrict__ forced_ids, int32_t *__restrict__ ids, float *__restrict__ probs,
+                     float *__restrict__ gate_logit, int32_t *__restrict__ block_counts, uint32_t *__restrict__ err) {
+    __shared__ float all_lg[8][256];  // per warp: every exact logit, when a token has too many candidates
+    __shared__ uint32_t cand_mask[8][8];  // per warp: candidate bits of experts 32 j + lane
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;
+    float *lg_all = all_lg[threadIdx.x >> 5];
+    // the token's row in registers, canonical lane partition; its norm
+    uint4 xr[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        xr[k] = make_uint4(0, 0, 0, 0);
+        if (k * 256 < D) {
+            xr[k] = *reinterpret_cast<const uint4 *>(x + (size_t)t * D + k * 256 + lane * 8);
+            const uint32_t w4[4] = {xr[k].x, xr[k].y, xr[k].z, xr[k].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float lo = bf16_lo(w4[j]), hi = bf16_hi(w4[j]);
+                ss = fmaf(lo, lo, ss);
+                ss = fmaf(hi, hi, ss);
+            }
+        }
+    }
+    const float nx = sqrtf(warp_sum_butterfly(ss)) * kNormMargin;
+    int32_t sel[8];
+    float chosen[8];
+    bool bad = false;
+    if (forced_ids) {
+        int32_t id = 0;
+        if (lane < 8) {
+            id = forced_ids[(size_t)t * 8 + lane];
+            bad = id < 0 || id >= E;
+            id = min(max(id, 0), E - 1);
+        }
+        if (__any_sync(kFull, bad) && lane == 0) atomicOr(err, kErrBadExpert);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+            const int e = __shfl_sync(kFull, id, n);
+            const float lg = canonical_dot_xreg(R, e, xr, D) + (bias ? bias[e] : 0.f);
+            sel[n] = e;
+            chosen[n] = lg;
+        }
+    } else {
+        // approximate logits and their bounds; lane l holds experts l + 32 j
+        float lo_[8], hi_[8];
+        bool nonfinite = false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane + 32 * j;
+            lo_[j] = -INFINITY;
+            hi_[j] = -INFINITY;
+            if (e < E) {
+                const float a = bf16_bits_to_f32(approx[(size_t)t * E + e]) + (bias ? bias[e] : 0.f);
+                if (!isfinite(a)) {
+                    nonfinite = true;
+                } else {
+                    const float eps = (wn[e] + kRouterAccumRel * wn[E + e]) * nx + kRouterOutRel * fabsf(a);
+                    lo_[j] = a - eps;
+                    hi_[j] = a + eps;
+                }
+            }
+        }
+        if (__any_sync(kFull, nonfinite) && lane == 0) atomicOr(err, kErrNonFinite);
+        int32_t lsel[8];
+        float lch[8];
+        select_top8(lo_, E, lsel, lch);
+        const float L8 = lch[7];
+        uint32_t *mask = cand_mask[threadIdx.x >> 5];
+        int ncand = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t mj = __ballot_sync(kFull, lane + 32 * j < E && hi_[j] >= L8);
+            if (lane == 0) mask[j] = mj;
+            ncand += __popc(mj);
+        }
+        __syncwarp();
+        // exact logits of the candidates (all experts if there are too many), ascending id; the
+        // i-th goes to lane i % 32, slot i / 32
+        const bool all = ncand > kRouterMaxCand;
+        float v0 = 0.f, v1 = 0.f;
+        uint32_t i0 = 0, i1 = 0;
+        bool h0 = false, h1 = false;
+        int i = 0;
+#pragma unroll 1
+        for (int j = 0; j < 8; ++j) {
+            uint32_t m = all ? __ballot_sync(kFull, lane + 32 * j < E) : mask[j];
+            while (m) {
+                const int b = __ffs(m) - 1;
+                m &= m - 1;
+                const int e = b + 32 * j;
+                float lg = canonical_dot_xreg(R, e, xr, D) + (bias ? bias[e] : 0.f);
+                if (!isfinite(lg)) lg = -INFINITY;
+                if (all) {
+                    if (lane == 0) lg_all[e] = lg;
+                } else {
+                    if (lane == (i & 31)) {
+                        if (i < 32) { v0 = lg; i0 = (uint32_t)e; h0 = true; }
+                        else { v1 = lg; i1 = (uint32_t)e; h1 = true; }
+                    }
+                }
+                ++i;
+            }
+        }
+        if (all) {
+            __syncwarp();
+            float vall[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) vall[j] = lane + 32 * j < E ? lg_all[lane + 32 * j] : -INFINITY;
+            select_top8(vall, E, sel, chosen);
+        } else
+            select_top8_pairs(v0, i0, h0, v1, i1, h1, sel, chosen);
+    }
+    // softmax over the chosen logits, the gate logit, outputs and the block's route counts
+    float mx = chosen[0];
+#pragma unroll
+    for (int n = 1; n < 8; ++n) mx = fmaxf(mx, chosen[n]);
+    float p[8], sum = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+        p[n] = expf(chosen[n] - mx);
+        sum += p[n];
+    }
+    const float g = canonical_dot_xreg(SR, 0, xr, D);
+    if (lane < 8) {
+        float pv = 0.f;
+        int32_t sv = 0;
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+            if (m == lane) {
+                pv = p[m];
+                sv = sel[m];
+            }
+        ids[(size_t)t * 8 + lane] = sv;
+        probs[(size_t)t * 8 + lane] = pv / sum;
+        atomicAdd(&block_counts[(size_t)(t / topk::TOK_PER_CTA) * E + sv], 1);
+    }
+    if (lane == 0) gate_logit[t] = g;
+}
+
 }  // namespace di
