@@ -755,6 +755,88 @@ __device__ __forceinline__ float canonical_dot_xreg(const QView &m, int row, con
     return warp_sum_butterfly(acc);
 }
 
+// canonical_dot_xreg of two rows at once: both rows' loads are in flight together, the two rows'
+// dequantisation and FMA chains run as packed pairs (fma.rn.f32x2 rounds each half exactly as fmaf)
+// and the butterflies interleave; each result is bit-identical to the single-row one.
+__device__ __forceinline__ void canonical_dot_xreg2(const QView &m, int row0, int row1, const uint4 (&xr)[8], int D,
+                                                    float &out0, float &out1) {
+    const uint32_t lane = lane_id();
+    const uint32_t *w0 = m.packed + (size_t)row0 * m.words_per_row(), *w1 = m.packed + (size_t)row1 * m.words_per_row();
+    const uint16_t *s0 = m.scales + (size_t)row0 * m.groups_per_row(), *s1 = m.scales + (size_t)row1 * m.groups_per_row();
+    const uint16_t *b0 = m.biases + (size_t)row0 * m.groups_per_row(), *b1 = m.biases + (size_t)row1 * m.groups_per_row();
+    uint2 qa[8], qb[8];
+    uint32_t sa[8], sb[8];  // scale | bias << 16
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        if (k * 256 < D) {
+            const int base = k * 256 + lane * 8;
+            qa[k] = __ldg(reinterpret_cast<const uint2 *>(w0 + base / 4));
+            qb[k] = __ldg(reinterpret_cast<const uint2 *>(w1 + base / 4));
+            sa[k] = (uint32_t)__ldg(s0 + base / 64) | ((uint32_t)__ldg(b0 + base / 64) << 16);
+            sb[k] = (uint32_t)__ldg(s1 + base / 64) | ((uint32_t)__ldg(b1 + base / 64) << 16);
+        }
+    float2 acc = make_float2(0.0f, 0.0f);  // (row0, row1)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        if (k * 256 >= D) break;
+        const float2 sc = make_float2(bf16_lo(sa[k]), bf16_lo(sb[k])), bi = make_float2(bf16_hi(sa[k]), bf16_hi(sb[k]));
+        const uint32_t xw[4] = {xr[k].x, xr[k].y, xr[k].z, xr[k].w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float xf = (j & 1) ? bf16_hi(xw[j >> 1]) : bf16_lo(xw[j >> 1]);
+            const float2 q = make_float2(byte_to_f32(j < 4 ? qa[k].x : qa[k].y, j & 3),
+                                         byte_to_f32(j < 4 ? qb[k].x : qb[k].y, j & 3));
+            acc = ffma2(ffma2(q, sc, bi), make_float2(xf, xf), acc);
+        }
+    }
+    float acc0 = acc.x, acc1 = acc.y;
+#pragma unroll
+    for (int n = 16; n; n >>= 1) {
+        acc0 += __shfl_xor_sync(kFull, acc0, n);
+        acc1 += __shfl_xor_sync(kFull, acc1, n);
+    }
+    out0 = acc0;
+    out1 = acc1;
+}
+
+// The 8th largest of 256 values (8 per lane, v[j] of expert lane + 32 j < E; the others ignored),
+// counting equal values separately; every lane returns it.
+__device__ __forceinline__ float eighth_largest(const float *v, int E) {
+    const int lane = lane_id();
+    uint32_t key[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) key[j] = lane + 32 * j < E ? order_key(v[j]) : 0u;
+    auto cs = [&](int a, int b) {  // descending
+        const uint32_t hi = max(key[a], key[b]), lo = min(key[a], key[b]);
+        key[a] = hi;
+        key[b] = lo;
+    };
+    cs(0, 2); cs(1, 3); cs(4, 6); cs(5, 7);
+    cs(0, 4); cs(1, 5); cs(2, 6); cs(3, 7);
+    cs(0, 1); cs(2, 3); cs(4, 5); cs(6, 7);
+    cs(2, 4); cs(3, 5);
+    cs(1, 4); cs(3, 6);
+    cs(1, 2); cs(3, 4); cs(5, 6);
+    int need = 8;
+    uint32_t res = 0u;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+        const uint32_t best = __reduce_max_sync(kFull, key[0]);
+        const int c = __popc(__ballot_sync(kFull, key[0] == best));
+        if (c >= need) {
+            res = best;
+            break;
+        }
+        need -= c;
+        if (key[0] == best) {
+#pragma unroll
+            for (int j = 0; j < 7; ++j) key[j] = key[j + 1];
+            key[7] = 0u;
+        }
+    }
+    return key_value(res);
+}
+
 // The 8 largest of up to 64 (value, id) entries, two per lane (slots 0 and 1; absent entries have
 // key 0), descending with ties to the lower id; all lanes return the same sel/chosen.
 __device__ __forceinline__ void select_top8_pairs(float v0, uint32_t id0, bool has0, float v1, uint32_t id1, bool has1,
@@ -790,6 +872,7 @@ router_select_kernel(const uint16_t *__restrict__ approx, const float *__restric
                      float *__restrict__ gate_logit, int32_t *__restrict__ block_counts, uint32_t *__restrict__ err) {
     __shared__ float all_lg[8][256];  // per warp: every exact logit, when a token has too many candidates
     __shared__ uint32_t cand_mask[8][8];  // per warp: candidate bits of experts 32 j + lane
+    __shared__ int16_t cand_id[8][kRouterMaxCand];  // per warp: the candidates, ascending
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -851,10 +934,7 @@ router_select_kernel(const uint16_t *__restrict__ approx, const float *__restric
             }
         }
         if (__any_sync(kFull, nonfinite) && lane == 0) atomicOr(err, kErrNonFinite);
-        int32_t lsel[8];
-        float lch[8];
-        select_top8(lo_, E, lsel, lch);
-        const float L8 = lch[7];
+        const float L8 = eighth_largest(lo_, E);
         uint32_t *mask = cand_mask[threadIdx.x >> 5];
         int ncand = 0;
 #pragma unroll
@@ -870,25 +950,42 @@ router_select_kernel(const uint16_t *__restrict__ approx, const float *__restric
         float v0 = 0.f, v1 = 0.f;
         uint32_t i0 = 0, i1 = 0;
         bool h0 = false, h1 = false;
-        int i = 0;
-#pragma unroll 1
-        for (int j = 0; j < 8; ++j) {
-            uint32_t m = all ? __ballot_sync(kFull, lane + 32 * j < E) : mask[j];
-            while (m) {
-                const int b = __ffs(m) - 1;
-                m &= m - 1;
-                const int e = b + 32 * j;
-                float lg = canonical_dot_xreg(R, e, xr, D) + (bias ? bias[e] : 0.f);
-                if (!isfinite(lg)) lg = -INFINITY;
-                if (all) {
-                    if (lane == 0) lg_all[e] = lg;
-                } else {
-                    if (lane == (i & 31)) {
-                        if (i < 32) { v0 = lg; i0 = (uint32_t)e; h0 = true; }
-                        else { v1 = lg; i1 = (uint32_t)e; h1 = true; }
-                    }
+        if (all) {
+            for (int e = 0; e < E; e += 2) {
+                float a0, a1;
+                canonical_dot_xreg2(R, e, min(e + 1, E - 1), xr, D, a0, a1);
+                a0 += bias ? bias[e] : 0.f;
+                a1 += bias ? bias[min(e + 1, E - 1)] : 0.f;
+                if (lane == 0) {
+                    lg_all[e] = isfinite(a0) ? a0 : -INFINITY;
+                    if (e + 1 < E) lg_all[e + 1] = isfinite(a1) ? a1 : -INFINITY;
                 }
-                ++i;
+            }
+        } else {
+            int16_t *ci = cand_id[threadIdx.x >> 5];
+            if (lane == 0) {
+                int n = 0;
+                for (int j = 0; j < 8; ++j)
+                    for (uint32_t m = mask[j]; m; m &= m - 1) ci[n++] = (int16_t)(__ffs(m) - 1 + 32 * j);
+            }
+            __syncwarp();
+            for (int i = 0; i < ncand; i += 2) {
+                const int e0 = ci[i], e1 = ci[min(i + 1, ncand - 1)];
+                float a0, a1;
+                canonical_dot_xreg2(R, e0, e1, xr, D, a0, a1);
+                a0 += bias ? bias[e0] : 0.f;
+                a1 += bias ? bias[e1] : 0.f;
+                if (!isfinite(a0)) a0 = -INFINITY;
+                if (!isfinite(a1)) a1 = -INFINITY;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int ii = i + u;
+                    if (ii >= ncand || lane != (ii & 31)) continue;
+                    const float lg = u ? a1 : a0;
+                    const uint32_t e = (uint32_t)(u ? e1 : e0);
+                    if (ii < 32) { v0 = lg; i0 = e; h0 = true; }
+                    else { v1 = lg; i1 = e; h1 = true; }
+                }
             }
         }
         if (all) {
