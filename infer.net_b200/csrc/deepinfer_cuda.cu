@@ -465,6 +465,7 @@ struct BlockBuffers {
     uint16_t *act, *yr, *ys, *xp;
     float *act32;
     float *wn;             // router row norms (tensor-core router): ||r_e||, then ||W_e||
+    float *wf;             // the router rows' f32 weights [E][D] (exact candidate logits)
     Tile *rtiles;          // work tiles of the approximate-logit GEMM
     int32_t *rnt;
     uint32_t *counter;  // [0] last-CTA ticket of decode_route_kernel (kept at zero between launches),
@@ -496,7 +497,7 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     size_t o_a32 = gemv ? cv.take<float>((size_t)T * 9 * I) : 0;
     size_t o_ctr = cv.take<uint32_t>(2);
     size_t o_wn = cv.take<float>(2 * (size_t)E), o_rt = cv.take<Tile>((size_t)(T + 255) / 256 + 1);
-    size_t o_rnt = cv.take<int32_t>(1);
+    size_t o_rnt = cv.take<int32_t>(1), o_wf = gemv ? 0 : cv.take<float>((size_t)E * D);
     size_t need = cv.off + 256;
     ensure_workspace(c, need);
     b.x = host_io ? at<uint16_t>(c, o_x) : nullptr;
@@ -520,6 +521,7 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
     b.act32 = gemv ? at<float>(c, o_a32) : nullptr;
     b.counter = at<uint32_t>(c, o_ctr);
     b.wn = at<float>(c, o_wn);
+    b.wf = gemv ? nullptr : at<float>(c, o_wf);
     b.rtiles = at<Tile>(c, o_rt);
     b.rnt = at<int32_t>(c, o_rnt);
     return need;
@@ -528,11 +530,11 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
 // Routing of a prefill-sized batch (E a multiple of 128) in two steps (route.cuh): approximate
 // logits on the tensor cores (approx: scratch of T*E bf16) with the router rows' norms, then the
 // exact canonical logits of the candidates only -> ids, probs, gate logits, per-block route counts.
-void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, float *wn, Tile *rtiles, int32_t *rnt,
+void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, float *wn, float *wf, Tile *rtiles, int32_t *rnt,
                            uint16_t *approx, int grid, uint32_t *err, cudaStream_t st) {
     const int E = L->E, D = L->D;
     const QView R = L->m[0]->view();
-    router_row_norms_kernel<<<(E + 7) / 8, 256, 0, st>>>(R, E, D, wn);
+    router_row_norms_kernel<<<(E + 7) / 8, 256, 0, st>>>(R, E, D, wn, wf);
     router_tiles_kernel<<<1, 256, 0, st>>>(T, rtiles, rnt);
     launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, R, R, R, R, x, T, nullptr, 0, nullptr, rtiles, rnt, T,
                                                  0, D, E, 1, approx, T, err),
@@ -540,12 +542,12 @@ void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, float *wn, 
 }
 void enqueue_router_select(const Layer *L, const uint16_t *x, int T, const int32_t *forced, int32_t *ids,
                            float *probs, float *gate, int32_t *block_counts, int nblocks, const float *wn,
-                           const uint16_t *approx, uint32_t *err, cudaStream_t st) {
+                           const float *wf, const uint16_t *approx, uint32_t *err, cudaStream_t st) {
     const int E = L->E, D = L->D;
     const QView R = L->m[0]->view(), SR = L->m[7]->view();
     CK(cudaMemsetAsync(block_counts, 0, sizeof(int32_t) * (size_t)nblocks * E, st));
-    router_select_kernel<<<(T + 7) / 8, 256, 0, st>>>(approx, wn, x, T, E, D, R, SR, L->bias, forced, ids, probs, gate,
-                                                      block_counts, err);
+    router_select_kernel<<<(T + 7) / 8, 256, 0, st>>>(approx, wn, wf, x, T, E, D, R, SR, L->bias, forced, ids, probs,
+                                                      gate, block_counts, err);
 }
 bool router_tc_fits(const Layer *L) { return L->E % 128 == 0 && L->D <= 2048; }
 
@@ -628,9 +630,9 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (!gemv && router_tc_fits(L)) {
         // tensor-core approximate logits + exact canonical logits of the candidates
         uint16_t *approx = reinterpret_cast<uint16_t *>(b.logits);
-        enqueue_router_approx(L, x, T, b.wn, b.rtiles, b.rnt, approx, c->sms, c->d_err, st);
+        enqueue_router_approx(L, x, T, b.wn, b.wf, b.rtiles, b.rnt, approx, c->sms, c->d_err, st);
         if (profile) stage_mark(c, S_TOPK);
-        enqueue_router_select(L, x, T, forced_ids, ids, probs, b.gate, b.block_counts, b.nblocks, b.wn, approx,
+        enqueue_router_select(L, x, T, forced_ids, ids, probs, b.gate, b.block_counts, b.nblocks, b.wn, b.wf, approx,
                               c->d_err, st);
     } else {
         // every logit in the canonical f32 order
@@ -1886,7 +1888,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         const size_t o_y = cv.take<uint16_t>(((size_t)RC * 8 + T) * D + 8), o_rp = cv.take<int32_t>((size_t)RC * 8 + 8);
         const size_t o_xp = cv.take<uint16_t>((size_t)RC * 8 * D + 8);
         const size_t o_wn = cv.take<float>(2 * (size_t)E), o_rt = cv.take<Tile>((size_t)(T + 255) / 256 + 1);
-        const size_t o_rnt = cv.take<int32_t>(1);
+        const size_t o_rnt = cv.take<int32_t>(1), o_wf = cv.take<float>((size_t)E * D);
         ensure_workspace(c, cv.off + 256);
         float *dx = dev_io ? x : at<float>(c, o_x);
         const float *dn = dev_io ? norms : at<float>(c, o_n);
@@ -1903,6 +1905,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         float *wn = at<float>(c, o_wn);
         Tile *rtiles = at<Tile>(c, o_rt);
         int32_t *rnt = at<int32_t>(c, o_rnt);
+        float *wf = at<float>(c, o_wf);
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st));
         CK(cudaEventRecord(c->ev_start, st));
         if (!dev_io) {
@@ -1919,8 +1922,8 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             if (l == 0) rmsnorm_kernel<<<T, 256, 0, st>>>(dx, dn, D, eps, h, nullptr);
             if (router_tc_fits(L)) {
                 uint16_t *approx = reinterpret_cast<uint16_t *>(logits);
-                enqueue_router_approx(L, h, T, wn, rtiles, rnt, approx, grid, c->d_err, st);
-                enqueue_router_select(L, h, T, nullptr, ids, probs, gate, bc, nb_l, wn, approx, c->d_err, st);
+                enqueue_router_approx(L, h, T, wn, wf, rtiles, rnt, approx, grid, c->d_err, st);
+                enqueue_router_select(L, h, T, nullptr, ids, probs, gate, bc, nb_l, wn, wf, approx, c->d_err, st);
             } else {
                 router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
                                        router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);

@@ -689,8 +689,10 @@ constexpr float kRouterOutRel = 0x1p-8f;
 constexpr float kNormMargin = 1.0f + 0x1p-10f;  // f32 rounding of the norms themselves
 constexpr int kRouterMaxCand = 64;             // above this a token falls back to all experts
 
-// ||r_e||, ||W_e|| of every router row (rows < E) into wn[e], wn[E + e]; one warp per row.
-__global__ void __launch_bounds__(256) router_row_norms_kernel(QView R, int E, int D, float *__restrict__ wn) {
+// ||r_e||, ||W_e|| of every router row (rows < E) into wn[e], wn[E + e], and the rows' f32 weights
+// W = fma(q, s, b) -- the values the canonical order multiplies -- into wf [E][D]; one warp per row.
+__global__ void __launch_bounds__(256) router_row_norms_kernel(QView R, int E, int D, float *__restrict__ wn,
+                                                               float *__restrict__ wf) {
     const int e = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (e >= E) return;
     const uint32_t *w = R.packed + (size_t)e * R.words_per_row();
@@ -699,13 +701,16 @@ __global__ void __launch_bounds__(256) router_row_norms_kernel(QView R, int E, i
         const uint32_t q4 = w[c / 4];
         const float s = bf16_bits_to_f32(R.scales[(size_t)e * R.groups_per_row() + c / 64]);
         const float b = bf16_bits_to_f32(R.biases[(size_t)e * R.groups_per_row() + c / 64]);
+        float Wv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const float W = fmaf(byte_to_f32(q4, j), s, b);
             const float r = bf16_bits_to_f32(f32_to_bf16_bits(W)) - W;  // exact (Sterbenz)
             rr = fmaf(r, r, rr);
             ww = fmaf(W, W, ww);
+            Wv[j] = W;
         }
+        *reinterpret_cast<float4 *>(wf + (size_t)e * D + c) = make_float4(Wv[0], Wv[1], Wv[2], Wv[3]);
     }
     rr = warp_sum_butterfly(rr);
     ww = warp_sum_butterfly(ww);
@@ -799,6 +804,38 @@ __device__ __forceinline__ void canonical_dot_xreg2(const QView &m, int row0, in
     out1 = acc1;
 }
 
+// canonical_dot_xreg2 with the rows' f32 weights precomputed (wf [rows][D], the same W values):
+// two 16-byte loads per 8 columns instead of code loads and conversions.
+__device__ __forceinline__ void canonical_dot_wf2(const float *wf, int row0, int row1, const uint4 (&xr)[8], int D,
+                                                  float &out0, float &out1) {
+    const uint32_t lane = lane_id();
+    const float *w0 = wf + (size_t)row0 * D, *w1 = wf + (size_t)row1 * D;
+    float2 acc = make_float2(0.0f, 0.0f);  // (row0, row1)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        if (k * 256 >= D) break;
+        const int base = k * 256 + lane * 8;
+        const float4 a0 = __ldg(reinterpret_cast<const float4 *>(w0 + base)), a1 = __ldg(reinterpret_cast<const float4 *>(w0 + base + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4 *>(w1 + base)), b1 = __ldg(reinterpret_cast<const float4 *>(w1 + base + 4));
+        const float wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const uint32_t xw[4] = {xr[k].x, xr[k].y, xr[k].z, xr[k].w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float xf = (j & 1) ? bf16_hi(xw[j >> 1]) : bf16_lo(xw[j >> 1]);
+            acc = ffma2(make_float2(wa[j], wb[j]), make_float2(xf, xf), acc);
+        }
+    }
+    float acc0 = acc.x, acc1 = acc.y;
+#pragma unroll
+    for (int n = 16; n; n >>= 1) {
+        acc0 += __shfl_xor_sync(kFull, acc0, n);
+        acc1 += __shfl_xor_sync(kFull, acc1, n);
+    }
+    out0 = acc0;
+    out1 = acc1;
+}
+
 // The 8th largest of 256 values (8 per lane, v[j] of expert lane + 32 j < E; the others ignored),
 // counting equal values separately; every lane returns it.
 __device__ __forceinline__ float eighth_largest(const float *v, int E) {
@@ -866,7 +903,8 @@ __device__ __forceinline__ void select_top8_pairs(float v0, uint32_t id0, bool h
 // shared-route gate logit, and the route counts of the token's 64-token block (block_counts zeroed
 // beforehand). forced: the token's 8 ids are given (their exact logits give the probabilities).
 __global__ void __launch_bounds__(256)
-router_select_kernel(const uint16_t *__restrict__ approx, const float *__restrict__ wn, const uint16_t *__restrict__ x,
+router_select_kernel(const uint16_t *__restrict__ approx, const float *__restrict__ wn, const float *__restrict__ wf,
+                     const uint16_t *__restrict__ x,
                      int T, int E, int D, QView R, QView SR, const float *__restrict__ bias,
                      const int32_t *__restrict__ forced_ids, int32_t *__restrict__ ids, float *__restrict__ probs,
                      float *__restrict__ gate_logit, int32_t *__restrict__ block_counts, uint32_t *__restrict__ err) {
@@ -953,7 +991,7 @@ router_select_kernel(const uint16_t *__restrict__ approx, const float *__restric
         if (all) {
             for (int e = 0; e < E; e += 2) {
                 float a0, a1;
-                canonical_dot_xreg2(R, e, min(e + 1, E - 1), xr, D, a0, a1);
+                canonical_dot_wf2(wf, e, min(e + 1, E - 1), xr, D, a0, a1);
                 a0 += bias ? bias[e] : 0.f;
                 a1 += bias ? bias[min(e + 1, E - 1)] : 0.f;
                 if (lane == 0) {
@@ -972,7 +1010,7 @@ router_select_kernel(const uint16_t *__restrict__ approx, const float *__restric
             for (int i = 0; i < ncand; i += 2) {
                 const int e0 = ci[i], e1 = ci[min(i + 1, ncand - 1)];
                 float a0, a1;
-                canonical_dot_xreg2(R, e0, e1, xr, D, a0, a1);
+                canonical_dot_wf2(wf, e0, e1, xr, D, a0, a1);
                 a0 += bias ? bias[e0] : 0.f;
                 a1 += bias ? bias[e1] : 0.f;
                 if (!isfinite(a0)) a0 = -INFINITY;
