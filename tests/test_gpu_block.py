@@ -241,6 +241,28 @@ def test_top8_exact_ties_go_to_the_lower_id(ctx):
     G.close()
 
 
+def test_router_many_tied_candidates_fall_back_to_all_exact(ctx):
+    # 80 identical router rows with equal bias tie exactly and lead by a wide margin, so every token
+    # has more candidates than the tensor-core router's exact check takes (64): the top-8 comes
+    # from all 256 exact logits and must be the 8 lowest ids of the tied group
+    E, D = 256, 512
+    L = O.Layer(46, bits=8, E=E, D=D, I=512)
+    r = L.m["router"]
+    group = list(range(7, 247, 3))[:80]
+    for row in group[1:]:
+        r.packed[0, row] = r.packed[0, group[0]]
+        r.scales[0, row] = r.scales[0, group[0]]
+        r.biases[0, row] = r.biases[0, group[0]]
+    bias = np.zeros(E, np.float32)
+    bias[group] = 6.0
+    L.router_bias = bias
+    G = di.MoeLayer.from_oracle(ctx, L)
+    for T, flags in ((40, di.PATH_GROUPED), (1, di.PATH_GEMV)):
+        _, _, ids = check_block(ctx, L, G, T, flags)
+        assert np.all(ids == np.array(group[:8], np.int32)[None, :])
+    G.close()
+
+
 def test_decode_stack_graph_replays_match(ctx):
     # the decode stack is captured as a CUDA graph on first use and replayed afterwards;
     # replays must give the same bits as the first (captured) run, and a changed input must flow
