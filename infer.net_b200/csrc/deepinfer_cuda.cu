@@ -676,7 +676,7 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
                                           b.seg_off, b.tiles, b.n_tiles, b.max_tiles, c->d_err);
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
-    scatter_routes_kernel<<<b.nblocks, 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos);
+    scatter_routes_kernel<<<b.nblocks, kScatterWarps * 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos);
     // token rows in expert order for the gate/up B operand (timed with the scatter)
     permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(x, b.perm, b.seg_off + E, D, b.xp);
     if (profile) stage_mark(c, S_GATE_UP);
@@ -1940,7 +1940,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                                                        c->d_err);
             scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, RC, T, gg::BN, rbb, sgc, sgo, tiles, nt,
                                                   max_tiles, c->d_err);
-            scatter_routes_kernel<<<nbr, 32, 0, st>>>(il, RC, El + 1, rbb, sgo, perm, rpos);
+            scatter_routes_kernel<<<nbr, kScatterWarps * 32, 0, st>>>(il, RC, El + 1, rbb, sgo, perm, rpos);
             permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(my_rx, perm, sgo + El, D, xp);
             // 4. local experts over the received rows, shared expert over the local rows
             launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, Gm, U, SG, SU, xp, 8 * RC, h, T, perm,

@@ -474,34 +474,37 @@ scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int n_h
 // Each CTA re-reads the routes of its token range in ascending route order and places
 // route r = t*8 + slot at seg_off[e] + block_base[blk][e] + (rank of r among earlier
 // routes of e in this block): the stable counting sort (prefill_moe.mm:12-14 order).
-__global__ void __launch_bounds__(32)
+constexpr int kScatterWarps = topk::TOK_PER_CTA * 8 / 32;  // one warp per 32 routes of a block
+__global__ void __launch_bounds__(kScatterWarps * 32)
 scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32_t *__restrict__ block_base,
                       const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route,
                       int32_t *__restrict__ route_pos) {
-    __shared__ int32_t run[kMaxBuckets];
-    const int lane = threadIdx.x;
-    for (int i = lane; i < E; i += 32) run[i] = 0;
-    __syncwarp();
-    const int r0 = blockIdx.x * topk::TOK_PER_CTA * 8;
-    const int r1 = min(r0 + topk::TOK_PER_CTA * 8, T * 8);
-    for (int base = r0; base < r1; base += 32) {
-        const int r = base + lane;
-        const bool valid = r < r1;
-        const int e = valid ? ids[r] : -1 - lane;  // invalid lanes never match real experts
-        const unsigned peers = __match_any_sync(kFull, e);
-        const int leader = __ffs(peers) - 1;
-        const int rank = __popc(peers & ((1u << lane) - 1u));
-        int b = 0;
-        if (valid && lane == leader) b = run[e];
-        b = __shfl_sync(kFull, b, leader);
-        __syncwarp();
-        if (valid && lane == leader) run[e] = b + __popc(peers);
-        if (valid) {
-            const int pos = seg_off[e] + block_base[(size_t)blockIdx.x * E + e] + b + rank;
-            perm_route[pos] = r;
-            route_pos[r] = pos;  // inverse permutation: where route r's expert row is stored
+    // cnt[w][e]: routes of e in warp w's 32 routes, then the count in warps before w
+    __shared__ int32_t cnt[kScatterWarps][kMaxBuckets];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < kScatterWarps * kMaxBuckets; i += blockDim.x) (&cnt[0][0])[i] = 0;
+    __syncthreads();
+    const int r = blockIdx.x * topk::TOK_PER_CTA * 8 + warp * 32 + lane;
+    const bool valid = r < T * 8;
+    const int e = valid ? ids[r] : -1 - lane;  // invalid lanes never match real experts
+    const unsigned peers = __match_any_sync(kFull, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (valid && lane == __ffs(peers) - 1) cnt[warp][e] = __popc(peers);
+    __syncthreads();
+    for (int x = threadIdx.x; x < E; x += blockDim.x) {  // exclusive prefix over the warps, per bucket
+        int run = 0;
+#pragma unroll
+        for (int w = 0; w < kScatterWarps; ++w) {
+            const int v = cnt[w][x];
+            cnt[w][x] = run;
+            run += v;
         }
-        __syncwarp();
+    }
+    __syncthreads();
+    if (valid) {
+        const int pos = seg_off[e] + block_base[(size_t)blockIdx.x * E + e] + cnt[warp][e] + rank;
+        perm_route[pos] = r;
+        route_pos[r] = pos;  // inverse permutation: where route r's expert row is stored
     }
 }
 
