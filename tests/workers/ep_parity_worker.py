@@ -4,7 +4,11 @@ Builds a small model twice -- full layers on every rank and the rank's expert sh
 expert-parallel stack on uneven contiguous token shards and compares the rows against the
 single-GPU stack on all tokens. The same call is made twice (the second must repeat the first bit
 for bit: the peer buffers' arrival counters carry over between calls), then once with three times
-the tokens (every rank grows and re-maps its peer buffers). Exits non-zero on a mismatch.
+the tokens (every rank grows and re-maps its peer buffers); finally one layer of a 256-expert
+model, whose router runs on the tensor cores with the exact candidate check. (One layer: deeper
+layers see inputs that differ in the last bits -- the ranks' partial rows are summed in another
+order than the single-GPU combine -- and with 256 experts a near-tie can then route a token
+differently, which is not a fault.) Exits non-zero on a mismatch.
 """
 import datetime
 import os
@@ -58,7 +62,15 @@ def check(sizes, label, previous=None):
 ok1, first = check(sizes, "first")
 ok2, _ = check(sizes, "repeat", previous=first)
 ok3, _ = check([3 * n for n in sizes], "grown")
-ok = ok1 and ok2 and ok3
+for l in shards + full:
+    l.close()
+# the full expert count: 256 experts, hidden 512, intermediate 512 (the tensor-core router)
+E, D, I, L = 256, 512, 512, 1
+shards = [ep.layer(di.generate_layer_matrices(ctx, SEED + 1, l, bits, E, D, I, shard=(rank, world))) for l in range(L)]
+full = [di.MoeLayer(ctx, di.generate_layer_matrices(ctx, SEED + 1, l, bits, E, D, I)) for l in range(L)]
+norms = (1.0 + 0.1 * np.cos(np.arange(L * D))).astype(np.float32).reshape(L, D)
+ok4, _ = check([4 * n for n in sizes], "256 experts")
+ok = ok1 and ok2 and ok3 and ok4
 flag = torch.tensor([0 if ok else 1], device="cuda")
 dist.all_reduce(flag)
 for l in shards + full:
