@@ -97,9 +97,10 @@ ep_layout_kernel(const int32_t *__restrict__ ids, int T, int E_l, int G, int32_t
 //   sync [4G+2] u32         [0,G) dispatch arrivals from rank s, [G,2G) combine arrivals,
 //                           [2G,3G) dispatch row counts, [3G] abort word, [3G+1], [3G+2]
 //                           this rank's CTA tickets of its dispatch and of its partial-row send
-// A writing kernel signals every rank once per layer step: each CTA fences its stores at system
-// scope and takes a ticket; the last CTA writes the row counts (dispatch), fences, and bumps the
-// arrival counter of every rank, so after step n it reads n. The last CTA also resets its ticket.
+// A writing kernel signals every rank once per layer step: after a CTA barrier one thread fences
+// at system scope (cumulative over the CTA's stores, which the barrier orders before it) and takes
+// a ticket; the last CTA writes the row counts (dispatch), fences, and bumps the arrival counter of
+// every rank, so after step n it reads n. The last CTA also resets its ticket.
 struct EpPeers {
     uint16_t *rx[kMaxRanks];
     RowMeta *meta[kMaxRanks];
@@ -140,9 +141,11 @@ __device__ inline bool ep_wait_counters(const uint32_t *ctr, int G, uint32_t tar
 __device__ inline void ep_signal(uint32_t *ticket, const EpPeers &peers, int G, int slot, int count_slot,
                                  const int32_t *counts) {
     __shared__ uint32_t last;
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    }
     __syncthreads();
     if (!last) return;
     if (threadIdx.x == 0) {
