@@ -60,7 +60,7 @@ def profiled_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed regions."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -101,11 +101,17 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------------- reference arm
 
+_CPU_LAYER = []
+
+
 def cpu_sample(tokens: int, threads: int):
-    """Time the oracle port of the reference block on `tokens` tokens of one full-size layer."""
+    """Time the oracle port of the reference block on `tokens` tokens of one full-size layer
+    (the layer's weights are generated once and kept for later samples)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    L = O.Layer(SEED, layer=0, bits=8)
+    if not _CPU_LAYER:
+        _CPU_LAYER.append(O.Layer(SEED, layer=0, bits=8))
+    L = _CPU_LAYER[0]
     x = O.gen_bf16(SEED, O.ACT_STREAM, tokens * D).reshape(tokens, D)
     O.moe_block(L, x[:4], O.MODE_F32, threads=threads)  # warm
     t0 = time.perf_counter()
@@ -202,13 +208,13 @@ def run_ours(args):
             step_ms.append(stack(x.data_ptr(), TOKENS, flags))
             for k, v in ctx.last_profile().items():
                 stage_tot[k] = stage_tot.get(k, 0.0) + v
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        # ---- end to end through the public API with pinned host buffers, then batch-1 decode
+        e2e, dec_us = None, None
+        if not args.only_prefill:
+            e2e, dec_us = e2e_and_decode(args, di, torch, ctx, stack, x0)
     ms = sum(step_ms) / len(step_ms)
     value = TOKENS / (ms / 1e3)
-    # ---- end to end through the public API with pinned host buffers
-    e2e, dec_us, dstage = None, None, {}
-    if not args.only_prefill:
-        e2e, dec_us, dstage = e2e_and_decode(args, di, torch, ctx, stack, x0)
     pk = peaks()
 
     # ---- roofline of the dominant kernel: grouped gate/up + SwiGLU
@@ -245,8 +251,7 @@ def run_ours(args):
         "decode": None if dec_us is None else {
             "workload": "batch-1 decode, 40 layers (configs[1])", "us_per_token": dec_us,
             "gbs": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9,
-            "hbm_frac": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9 / pk["hbm_gbs"],
-            "stage_us_per_layer_kernels": {k: v * 1e3 for k, v in dstage.items()}},
+            "hbm_frac": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9 / pk["hbm_gbs"]},
         "clocks": clk.summary(),
         "gpu_launches": args.steps * LAYERS * 8,
     }
@@ -362,17 +367,13 @@ def e2e_and_decode(args, di, torch, ctx, stack, x0):
     for _ in range(n):
         x1.copy_(x0[:1])
         dms.append(stack(x1.data_ptr(), 1, dflags))
-    # one extra profiled pass for the stage breakdown only: PROFILE runs the per-layer kernels
-    # (route, gate/up, down) with events between them, not the persistent kernel
-    stack(x1.data_ptr(), 1, dflags | di.PROFILE)
-    dstage = dict(ctx.last_profile())
-    return e2e, 1e3 * sum(dms) / len(dms), dstage
+    return e2e, 1e3 * sum(dms) / len(dms)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")

@@ -20,6 +20,7 @@ enum : uint32_t {
     kErrBadExpert = 2u,     // forced route id out of range
     kErrCapacity = 4u,      // internal work list overflow (host sizing bug)
     kErrTimeout = 8u,       // a bounded device-side wait ran out
+    kErrRange = 16u,        // a one-token stack output outside its fixed-point accumulator's range
 };
 
 // Geometry of one quantised matrix as the kernels see it.

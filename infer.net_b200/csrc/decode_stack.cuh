@@ -1,35 +1,38 @@
 // Persistent one-token decode of a whole MoE stack: every layer of Qwen36Model.cs:218-262 for one
 // token in ONE cooperative kernel of one CTA per SM, so no layer pays a kernel boundary.
 //
+// Work split. The 9 expert slots (8 routed + the shared expert) x I = 512 intermediate columns are
+// 144 units of 32 columns; CTA u < 144 owns unit (slot u / 16, columns [32 (u % 16), +32)): the 32
+// (gate, up) row pairs of those columns and the same 32 columns of every down row. Its act values
+// therefore stay in the CTA, and its share of the layer output is a partial sum over 32 columns
+// for every one of the D outputs. The partial sums of all units are added in a fixed-point
+// accumulator by 64-bit integer atomics (exact, so the result does not depend on their order).
+//
 // Per layer l (gpu_graph.mm:48-61 RMSNorm, :134-146 router/top-8, quantized.mm:148-189 expert
 // GEMVs, Qwen36Model.cs:242-244 combine):
-//   S0  the CTA requests its share of the shared expert's rows (bulk copies into shared memory)
-//       and loads its router rows into registers -- neither depends on the token;
-//   S1  the residual row x_l (exchanged, below) -> h = bf16(x * rsqrt(mean(x^2) + eps) * w),
-//       computed redundantly, identically, in every CTA;
+//   S0  token-independent copies: the CTA's router rows, and -- for a shared-expert unit -- all of
+//       its weights, requested before the token arrives;
+//   S1  x_l = x_{l-1} + y_{l-1} once every CTA has added into y_{l-1}; h = bf16(RMSNorm(x_l) * w),
+//       computed redundantly, identically, in every CTA (every CTA holds all of x);
 //   S2  its router rows' logits in the canonical f32 order (bit-exact with the oracle) ->
 //       exchanged; the row after the last expert is the shared expert's gate logit;
 //   S3  every CTA reads all logits and selects the same top-8 (ties to the lower id), softmax;
-//   S4  it requests the routed experts' rows of its first group of (gate, up) pairs;
-//   S5  act = silu(gate . h) * (up . h) of its pairs -> exchanged: the second group is requested
-//       when the first has landed and computed while it streams in, the down rows when the
-//       second has landed. Split-K: warp w owns chunks [w*D/256, (w+1)*D/256) of h (in
-//       registers), its lanes (pair, chunk); the 16 warp partials of a pair are summed in a
-//       fixed order;
-//   S6  warp j < 9 reads act of expert slot j, one 16-element chunk per lane, from the exchange
-//       words (laid out so that these reads coalesce);
-//   S7  ...and dots it with the down rows of slot j for all of the CTA's outputs d; then
-//       x_{l+1}[d] = x_l[d] + sum_j c_j * part_j[d] (c = p_0..p_7, sigmoid(gate logit)) ->
-//       exchanged (the last layer writes x instead).
+//       a routed unit requests its expert's rows (four gate/up groups, then the down columns);
+//   S4  act = silu(gate . h) * (up . h) of its 32 pairs, group by group as they land. Split-K:
+//       warp w owns chunks [w*D/256, (w+1)*D/256) of h (in registers), its lanes (pair, chunk);
+//       the 16 warp partials of a pair are summed in a fixed order;
+//   S5  for every output d: c_slot * sum over its 32 columns of down[d][i] * act[i] (a lane pair
+//       per row, 16 columns each), rounded to a multiple of 2^-32 and added into y_l[d]; then
+//       the CTA's arrival on the layer's counter (after a device-scope fence).
+// The last layer's sum is added to x by CTA 0, which writes the output row.
 //
-// Exchanges use flag-in-data words: {f32 value, generation} in one 64-bit store, so a reader
-// polls the data itself and no fence orders data before a flag. Generations grow monotonically
-// across calls (a device counter), so stale words never match. Each CTA also bumps an arrival
-// counter of the exchange (relaxed, no fence) once its words are stored; readers wait for the
-// count first and then read the words about once, instead of every CTA re-polling the same
-// lines. The count is only a hint: the words' generations decide. A slow reader can never see a
-// value overwritten by the next layer: every write of layer l+1 happens after every CTA finished
-// reading the same exchange of layer l (each step depends on the previous exchange of all CTAs).
+// The logits travel in flag-in-data words: {f32 value, generation} in one 64-bit store, so a
+// reader polls the data itself and no fence orders data before a flag. Generations grow
+// monotonically across calls (a device counter), so stale words never match. Each CTA also bumps
+// an arrival counter once its words are stored; readers wait for the count first and then read
+// the words about once. The accumulator y alternates between two buffers by layer parity; a CTA
+// clears its slice of the buffer of layer l + 1 after the logits exchange of layer l, when every
+// CTA has read it (as y_{l-1}) and before any CTA can add into it (after the exchange of l + 1).
 // All waits are bounded; a timeout sets kErrTimeout and every CTA leaves.
 //
 // Dot products: a code q becomes the exact f32 denormal q * 2^-149 (its bits), the activation is
@@ -37,6 +40,8 @@
 // (q s + b) . x = s * (q . x) + b * sum(x) per 16-element chunk: one byte permute and half a
 // packed FMA (fma.rn.f32x2) per weight. The scaled operands stay normal for |x| in [2^-40, 2^64].
 #pragma once
+#include <cuda.h>
+
 #include "decode.cuh"
 
 namespace di {
@@ -44,10 +49,21 @@ namespace ds {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kI = 512;            // intermediate size of the stack kernel: one chunk per lane in S7
-constexpr int kGroupPairs = 16;    // (gate, up) pairs of a copy group; a CTA has at most two groups
-constexpr int kMaxOuts = 16;       // outputs per CTA (rows of the S7 partial sums)
-constexpr int kDescBytes = 384;    // one StackLayer in shared memory
+constexpr int kI = 512;                       // intermediate size of the stack kernel
+constexpr int kSlice = 32;                    // intermediate columns of one unit
+constexpr int kSlicesPerSlot = kI / kSlice;   // 16
+constexpr int kUnits = 9 * kSlicesPerSlot;    // 144: the kernel needs at least this many CTAs
+constexpr int kGroupPairs = 8;                // (gate, up) pairs of a copy group
+constexpr int kGroups = kSlice / kGroupPairs; // 4
+constexpr int kDnBox = 256;                   // rows of one down-column tensor copy
+constexpr int kDnRowBytes = 32;               // bytes of a row in the down-column copies
+constexpr int kDescBytes = 384;               // one StackLayer in shared memory
+// The fixed-point accumulator: a contribution c adds round(c * 2^32); |c| < 2^23, so the 144
+// contributions of an output stay below 2^62.2 (no overflow). A larger or non-finite one sets
+// kErrRange and the host recomputes the token with the per-layer kernels.
+constexpr float kAccScale = 0x1p32f;
+constexpr float kAccInv = 0x1p-32f;
+constexpr float kAccLimit = 0x1p23f;
 
 struct StackLayer {
     QView R, SR, G, U, Dn, SG, SU, SD;
@@ -58,58 +74,52 @@ static_assert(sizeof(StackLayer) % 4 == 0 && sizeof(StackLayer) <= kDescBytes, "
 
 struct StackParams {
     const StackLayer *layers;
+    const CUtensorMap *dn_maps;     // [n_layers][2]: routed, shared down codes (box 32 B x 256 rows)
     int n_layers, E;
     float eps;
     float *x;                       // residual row [D], in/out
     uint16_t *h_trace;              // [n_layers][D] or null
     int32_t *ids_trace;             // [n_layers][8] or null
     unsigned long long *ll_logit;   // [E + 1] exchange words
-    unsigned long long *ll_act;     // [9][16][I/16]: act[j][c*16 + e] at j*I + e*(I/16) + c
-    unsigned long long *ll_x;       // [D]
+    unsigned long long *acc;        // [2][D] fixed-point layer outputs: layer l adds into acc[l & 1]
     uint32_t *gen_base;             // generations used by earlier calls
-    uint32_t *ctr_x, *ctr_act, *ctr_logit;  // exchange arrivals (G per layer step)
+    uint32_t *ctr_y, *ctr_logit;    // arrivals (G per layer step)
     uint32_t *err;
 };
 
-// Shared memory of one CTA: h (bf16) [D]; h * 2^64 (f32) [4][D/16] float4 (float4 q of chunk c
-// at [q][c]) and its chunk sums [D/16]; two layer descriptors; partial sums [16][16][2]; its
-// router rows (codes [D], scales [D/64], biases [D/64] each); the
-// gate/up region: gate codes [pairs][gu_row], up codes, gate scales, gate biases, up scales, up
-// biases; the down region: codes [9][outs][dn_row], scales, biases; misc.
+// Shared memory of one CTA: h (f32) [4][D/16] float4 (float4 q of chunk c at [q][c]) and its chunk
+// sums [D/16]; two layer descriptors; gate/up partial sums [2][16 warps][8 pairs][2]; its router
+// rows (codes [D], scales [D/64], biases [D/64] each); the gate/up region of the unit: gate codes
+// [32][gu_row], up codes, gate scales, gate biases, up scales, up biases; the down columns [D][32 B]
+// and their scales [D] and biases [D]; misc.
 struct Layout {
-    int pairs, outs, gu_row, gu_grp, dn_row, dn_grp;
-    int xq_off, xc_off, desc_off, part_off, rr_off, gu_off, dn_off, misc_off, total;
+    int gu_row, gu_grp;
+    int xc_off, desc_off, part_off, rr_off, gu_off, dn_off, dsb_off, misc_off, total;
     __host__ __device__ int rr_row_bytes(int D) const { return D + D / 16; }  // codes, scales, biases
-    __host__ __device__ int gu_code(int m) const { return gu_off + m * pairs * gu_row; }
-    __host__ __device__ int gu_sb(int m, int k) const { return gu_off + 2 * pairs * gu_row + (2 * m + k) * pairs * gu_grp; }
-    __host__ __device__ int dn_code() const { return dn_off; }
-    __host__ __device__ int dn_sb(int k) const { return dn_off + 9 * outs * dn_row + k * 9 * outs * dn_grp; }
-    // misc: 3 mbarriers (gate/up group 0, group 1, down), ids[8], coef[9], red[16], abort flag,
-    // own residual values [outs]
+    __host__ __device__ int gu_code(int m) const { return gu_off + m * kSlice * gu_row; }
+    __host__ __device__ int gu_sb(int m, int k) const { return gu_off + 2 * kSlice * gu_row + (2 * m + k) * kSlice * gu_grp; }
+    __host__ __device__ int dn_sb(int k, int D) const { return dsb_off + k * D * 2; }
+    // misc: 5 mbarriers (gate/up groups 0-3, down), ids[8], coef[9], red[16], abort flag, act[32]
     __host__ __device__ int bar() const { return misc_off; }
-    __host__ __device__ int ids() const { return misc_off + 32; }
-    __host__ __device__ int coef() const { return misc_off + 64; }
-    __host__ __device__ int red() const { return misc_off + 112; }
-    __host__ __device__ int abort_flag() const { return misc_off + 176; }
-    __host__ __device__ int xown() const { return misc_off + 192; }
+    __host__ __device__ int ids() const { return misc_off + 64; }
+    __host__ __device__ int coef() const { return misc_off + 96; }
+    __host__ __device__ int red() const { return misc_off + 144; }
+    __host__ __device__ int abort_flag() const { return misc_off + 208; }
+    __host__ __device__ int act() const { return misc_off + 224; }
 };
-__host__ __device__ inline Layout layout(int D, int I, int bits, int grid) {
+__host__ __device__ inline Layout layout(int D, int bits) {
     Layout f;
-    f.pairs = (9 * I + grid - 1) / grid;
-    f.outs = (D + grid - 1) / grid;
     f.gu_row = D * bits / 8;
     f.gu_grp = D / 64 * 2;
-    f.dn_row = I * bits / 8;
-    f.dn_grp = I / 64 * 2;
-    f.xq_off = (D * 2 + 127) & ~127;
-    f.xc_off = f.xq_off + D * 4;
+    f.xc_off = D * 4;
     f.desc_off = f.xc_off + ((D / 16 * 4 + 127) & ~127);
     f.part_off = f.desc_off + 2 * kDescBytes;
-    f.rr_off = f.part_off + kWarps * kGroupPairs * 2 * 4;
-    f.gu_off = f.rr_off + 2 * (D + D / 16);  // the CTA's (at most two) router rows
-    f.dn_off = f.gu_off + ((2 * f.pairs * (f.gu_row + 2 * f.gu_grp) + 127) & ~127);
-    f.misc_off = f.dn_off + ((9 * f.outs * (f.dn_row + 2 * f.dn_grp) + 127) & ~127);
-    f.total = f.misc_off + 192 + ((f.outs * 4 + 15) & ~15);
+    f.rr_off = f.part_off + 2 * kWarps * kGroupPairs * 2 * 4;
+    f.gu_off = (f.rr_off + 2 * (D + D / 16) + 127) & ~127;  // the CTA's (at most two) router rows
+    f.dn_off = (f.gu_off + 2 * kSlice * (f.gu_row + 2 * f.gu_grp) + 127) & ~127;
+    f.dsb_off = f.dn_off + D * kDnRowBytes;
+    f.misc_off = (f.dsb_off + 2 * D * 2 + 127) & ~127;
+    f.total = f.misc_off + 224 + kSlice * 4;
     return f;
 }
 
@@ -165,32 +175,6 @@ __device__ __forceinline__ bool ll_gather(const unsigned long long *p, const int
     for (int a = 0; a < N; ++a) v[a] = __uint_as_float((uint32_t)w[a]);
     return true;
 }
-// Words p[a * stride] for a < N (all present), as ll_gather.
-template <int N>
-__device__ __forceinline__ bool ll_gather_strided(const unsigned long long *p, int stride, uint32_t gen, float (&v)[N],
-                                                  const uint32_t *err) {
-    unsigned long long w[N];
-#pragma unroll
-    for (int a = 0; a < N; ++a) w[a] = ll_load(p + a * stride);
-    uint64_t t0 = 0;
-    for (uint32_t n = 0;; ++n) {
-        bool all = true;
-#pragma unroll
-        for (int a = 0; a < N; ++a)
-            if ((uint32_t)(w[a] >> 32) != gen) {
-                all = false;
-                w[a] = ll_load(p + a * stride);
-            }
-        if (all) break;
-        if (n == 0)
-            t0 = global_ns();
-        else if ((n & 255u) == 0 && timed_out(t0, err))
-            return false;
-    }
-#pragma unroll
-    for (int a = 0; a < N; ++a) v[a] = __uint_as_float((uint32_t)w[a]);
-    return true;
-}
 // idx[a] = first + a * stride where below count, else -1
 template <int N>
 __device__ __forceinline__ void strided_idx(int (&idx)[N], int first, int stride, int count) {
@@ -198,7 +182,8 @@ __device__ __forceinline__ void strided_idx(int (&idx)[N], int first, int stride
     for (int a = 0; a < N; ++a) idx[a] = first + a * stride < count ? first + a * stride : -1;
 }
 
-// The 16 codes of chunk c of a code row in shared memory, as f32 denormals q * 2^-149.
+// The 16 codes of chunk c of a code row in shared memory, as f32 denormals q * 2^-149 (row
+// 16-byte aligned for 8-bit codes, 4-byte aligned for 5-bit ones).
 template <int BITS>
 __device__ __forceinline__ void chunk_denormals(const uint8_t *row, int c, float *w) {
     if constexpr (BITS == 8) {
@@ -269,6 +254,29 @@ __device__ __forceinline__ void router_row_from_smem(const uint8_t *row, int D, 
         }
     }
 }
+// The canonical router dot product (router_raw_dot's order: lane l owns columns 256k + 8l + j,
+// one fma chain per lane, then the xor butterfly) with h read from the CTA's f32 chunk layout.
+template <int D>
+__device__ __forceinline__ float router_dot_h(const RouterRaw &r, const float4 *hq) {
+    constexpr int cpd = D / 16;
+    const uint32_t lane = lane_id();
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < D / 256; ++k) {
+        const int base = k * 256 + (int)lane * 8, c = base >> 4, q0 = (base & 15) >> 2;
+        const float4 lo = hq[q0 * cpd + c], hi = hq[(q0 + 1) * cpd + c];
+        const float xf[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        const float s = bf16_bits_to_f32(r.s[k]), bb = bf16_bits_to_f32(r.b[k]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float wv = fmaf(byte_to_f32(j < 4 ? r.q[k].x : r.q[k].y, j & 3), s, bb);
+            acc = fmaf(wv, xf[j], acc);
+        }
+    }
+    return warp_sum_butterfly(acc);
+}
+
+__device__ __forceinline__ float acc_value(unsigned long long v) { return __ll2float_rn((long long)v) * kAccInv; }
 
 // The hidden size is a template parameter (512, 1024 or 2048) and I = kI: with the geometry known
 // to the compiler, the loop-invariant state fits in registers (a spill would go to L2 here: the
@@ -278,105 +286,109 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
     extern __shared__ __align__(128) uint8_t sm[];
     constexpr int I = kI;
     const int E = p.E, G = gridDim.x, cta = blockIdx.x;
-    const Layout f = layout(D, I, BITS, G);
+    const Layout f = layout(D, BITS);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint16_t *xs = reinterpret_cast<uint16_t *>(sm);
-    float4 *xq = reinterpret_cast<float4 *>(sm + f.xq_off);      // h * 2^64, [4][D/16]
+    float4 *hq = reinterpret_cast<float4 *>(sm);                  // h (f32), [4][D/16]
     float *xcs = reinterpret_cast<float *>(sm + f.xc_off);       // chunk sums of h
-    float *part = reinterpret_cast<float *>(sm + f.part_off);    // S5 [warp][pair][gate/up], S7 [slot][out]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + f.bar());  // gate/up group 0, group 1, down
+    float *part = reinterpret_cast<float *>(sm + f.part_off);    // [2][warp][pair][gate/up]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + f.bar());  // gate/up groups 0-3, down
     int32_t *ids_s = reinterpret_cast<int32_t *>(sm + f.ids());
     float *coef = reinterpret_cast<float *>(sm + f.coef());
     float *red = reinterpret_cast<float *>(sm + f.red());
     volatile int *abort_s = reinterpret_cast<volatile int *>(sm + f.abort_flag());
-    float *xown = reinterpret_cast<float *>(sm + f.xown());
-    constexpr int cpd = D / 16, cpw = cpd / kWarps;  // chunks of h; S5: chunks per warp
+    float *act_s = reinterpret_cast<float *>(sm + f.act());
+    uint16_t *dn_s = reinterpret_cast<uint16_t *>(sm + f.dn_sb(0, D)), *dn_b = reinterpret_cast<uint16_t *>(sm + f.dn_sb(1, D));
+    constexpr int cpd = D / 16, cpw = cpd / kWarps;  // chunks of h; S4: chunks per warp
     const int cl = lane & (cpw - 1), slot = lane / cpw, my_c = warp * cpw + cl;
 
-    // this CTA's shares: (gate, up) pairs [p_lo, p_hi) of the 9*I, outputs [d_lo, d_hi), router rows [r_lo, r_hi) of E+1
-    const int P = 9 * I;
-    const int p_lo = (int)((long long)cta * P / G), p_hi = (int)((long long)(cta + 1) * P / G), np = p_hi - p_lo;
+    // this CTA's unit (slot uj, columns [uk * 32, +32)), its slice of the outputs (cleared in the
+    // accumulator) and its router rows [r_lo, r_hi) of E + 1
+    const bool has_unit = cta < kUnits;
+    const int uj = has_unit ? cta / kSlicesPerSlot : 0, uk = cta % kSlicesPerSlot;
+    const bool shared_unit = has_unit && uj == 8, routed_unit = has_unit && uj < 8;
     const int d_lo = (int)((long long)cta * D / G), d_hi = (int)((long long)(cta + 1) * D / G), nd = d_hi - d_lo;
     const int r_lo = (int)((long long)cta * (E + 1) / G), r_hi = (int)((long long)(cta + 1) * (E + 1) / G);
-    const int j_lo = p_lo / I;
-    // local pairs [0, np): segment 0 is expert slot j_lo up to seg_end, segment 1 slot j_lo + 1;
-    // copy group 0 is pairs [0, g_end), group 1 the rest
-    const int seg_end = np > 0 ? min(np, (j_lo + 1) * I - p_lo) : 0;
-    const int g_end = min(np, kGroupPairs);
-    const uint32_t pair_bytes = 2u * (f.gu_row + 2 * f.gu_grp), slot_dn_bytes = (uint32_t)nd * (f.dn_row + 2 * f.dn_grp);
-    const int q_shared = max(0, min(np, 8 * I - p_lo));  // local pairs from here on are the shared expert's
-    const uint32_t shared0 = (uint32_t)max(0, g_end - q_shared) * pair_bytes;
-    const uint32_t shared1 = (uint32_t)max(0, np - max(g_end, q_shared)) * pair_bytes;
-    const uint32_t routed0 = (uint32_t)g_end * pair_bytes - shared0;
-    const uint32_t routed1 = (uint32_t)(np - g_end) * pair_bytes - shared1;
-    constexpr int kGroupCopies = 12;  // per group: 2 segments x 6 fields
-    constexpr int kGuCopies = 2 * kGroupCopies;
-    constexpr int kCopies = kGuCopies + 27;
+    // the unit's bytes of a down row: [x_lo, x_lo + 32 * BITS / 8); its copies start at the 16-byte
+    // boundary x_box below (32 bytes from there always cover them)
+    const int x_lo = uk * kSlice * BITS / 8, x_box = x_lo & ~15, dn_delta = x_lo - x_box;
+    const uint32_t group_bytes = (uint32_t)kGroupPairs * 2u * (uint32_t)(f.gu_row + 2 * f.gu_grp);
+    constexpr uint32_t kDnBytes = (uint32_t)D * kDnRowBytes;
+    constexpr int kGuCopies = kGroups * 6;  // per group: gate and up codes, scales, biases
+    constexpr int kCopies = kGuCopies + D / kDnBox;
     constexpr int kDescWords = (int)sizeof(StackLayer) / 4;
 
     if (tid == 0) {
-        for (int b = 0; b < 3; ++b) mbar_init(&bar[b], 1);
+        for (int b = 0; b <= kGroups; ++b) mbar_init(&bar[b], 1);
         fence_mbarrier_init();
         *abort_s = 0;
     }
     if (tid < kDescWords)
         reinterpret_cast<uint32_t *>(sm + f.desc_off)[tid] = reinterpret_cast<const uint32_t *>(p.layers)[tid];
+    // layer 0 adds into acc[0]: clear this CTA's slice before its first arrival (the fence below
+    // orders the stores before it); acc[1] is cleared during layer 0
+    if (tid < nd) p.acc[d_lo + tid] = 0ull;
     // every CTA reads the generation base before its first exchange write; CTA 0 advances it at
     // its end, which is after the first exchange (so after every CTA has read it)
     const uint32_t base = *reinterpret_cast<const volatile uint32_t *>(p.gen_base);
     __syncthreads();
+    if (tid == 0) __threadfence();
 
-    bool armed = false;  // thread 0: this layer's arrivals (with the routed bytes) are done
+    bool armed = false;  // thread 0: this layer's copies are requested (they must land before leaving)
     uint32_t ph = 0;
+    float xv[D / kThreads];  // x[tid + 512 a]: every CTA holds the whole residual row
     for (int l = 0; l < p.n_layers; ++l) {
         const StackLayer &Ly = *reinterpret_cast<const StackLayer *>(sm + f.desc_off + (l & 1) * kDescBytes);
         const uint32_t gen = base + (uint32_t)l + 1;
         ph = (uint32_t)l & 1u;
-        // copy k: k < 24 field k%6 of gate/up piece (group k/12, segment (k%12)/6), else down
-        // field (k-24)%3 of expert slot (k-24)/3; `routed` selects slots 0..7 or slot 8
-        auto issue_copy = [&](int k, bool routed) {
+        // copy k of the unit: k < 24 field k%6 of gate/up group k/6, else down-column box k-24
+        auto issue_copy = [&](int k, int e) {
             if (k < kGuCopies) {
-                const int gr = k / kGroupCopies, sg = (k % kGroupCopies) / 6, field = k % 6;
-                const int q0 = max(sg ? seg_end : 0, gr ? g_end : 0), q1 = min(sg ? np : seg_end, gr ? np : g_end);
-                const int j = j_lo + sg;
-                if (q0 >= q1 || (j < 8) != routed) return;
-                const int e = j < 8 ? ids_s[j] : 0;
-                const int m = field & 1, kind = field >> 1;  // m: gate / up; kind: codes, scales, biases
-                const QView &W = m ? (j < 8 ? Ly.U : Ly.SU) : (j < 8 ? Ly.G : Ly.SG);
-                const size_t row = (size_t)e * I + (p_lo + q0 - j * I);
-                uint64_t *b = &bar[gr];
+                const int g = k / 6, field = k % 6, m = field & 1, kind = field >> 1;  // m: gate / up
+                const QView &W = m ? (shared_unit ? Ly.SU : Ly.U) : (shared_unit ? Ly.SG : Ly.G);
+                const int q0 = g * kGroupPairs;
+                const size_t row = (size_t)e * I + uk * kSlice + q0;
                 if (kind == 0)
                     bulk_load(sm + f.gu_code(m) + q0 * f.gu_row,
-                              reinterpret_cast<const uint8_t *>(W.packed) + row * f.gu_row, (uint32_t)(q1 - q0) * f.gu_row, b);
+                              reinterpret_cast<const uint8_t *>(W.packed) + row * f.gu_row,
+                              (uint32_t)kGroupPairs * f.gu_row, &bar[g]);
                 else
                     bulk_load(sm + f.gu_sb(m, kind - 1) + q0 * f.gu_grp,
-                              (kind == 1 ? W.scales : W.biases) + row * (f.gu_grp / 2), (uint32_t)(q1 - q0) * f.gu_grp, b);
+                              (kind == 1 ? W.scales : W.biases) + row * (f.gu_grp / 2), (uint32_t)kGroupPairs * f.gu_grp,
+                              &bar[g]);
             } else {
-                const int kk = k - kGuCopies, j = kk / 3, kind = kk % 3;
-                if ((j < 8) != routed || nd == 0) return;
-                const int e = j < 8 ? ids_s[j] : 0;
-                const QView &W = j < 8 ? Ly.Dn : Ly.SD;
-                const size_t row = (size_t)e * D + d_lo;
-                if (kind == 0)
-                    bulk_load(sm + f.dn_code() + j * f.outs * f.dn_row,
-                              reinterpret_cast<const uint8_t *>(W.packed) + row * f.dn_row, (uint32_t)nd * f.dn_row, &bar[2]);
-                else
-                    bulk_load(sm + f.dn_sb(kind - 1) + j * f.outs * f.dn_grp,
-                              (kind == 1 ? W.scales : W.biases) + row * (f.dn_grp / 2), (uint32_t)nd * f.dn_grp, &bar[2]);
+                const int b = k - kGuCopies;
+                tma_load_2d(sm + f.dn_off + b * kDnBox * kDnRowBytes, p.dn_maps + 2 * l + (shared_unit ? 1 : 0), x_box,
+                            e * D + b * kDnBox, &bar[kGroups]);
+            }
+        };
+        // the down rows' scale and bias of the unit's group: thread t takes rows t + 512 a (the
+        // stores wait for the loads, which are issued back to back, as the unit's copies stream)
+        auto load_down_sb = [&](int e) {
+            const QView &W = shared_unit ? Ly.SD : Ly.Dn;
+            const int gsel = uk * kSlice / 64;
+            uint16_t s[D / kThreads], b[D / kThreads];
+#pragma unroll
+            for (int a = 0; a < D / kThreads; ++a) {
+                const size_t o = ((size_t)e * D + tid + a * kThreads) * (I / 64) + gsel;
+                s[a] = __ldg(W.scales + o);
+                b[a] = __ldg(W.biases + o);
+            }
+#pragma unroll
+            for (int a = 0; a < D / kThreads; ++a) {
+                dn_s[tid + a * kThreads] = s[a];
+                dn_b[tid + a * kThreads] = b[a];
             }
         };
         const int my_k = lane * kWarps + warp;  // the copy this thread issues, if below kCopies
-        // ---- S0: the shared expert's rows and the router rows (token independent). The bytes of
-        // the shared copies are expected now, the routed ones with the arrivals in S3.
+        // ---- S0: token-independent copies (the shared expert's unit, the router rows)
         fence_proxy_async_smem();  // this layer's copies overwrite what the last one read
-        if (tid == 0) {
-            armed = false;
-            mbar_expect_tx(&bar[0], shared0);
-            mbar_expect_tx(&bar[1], shared1);
-            mbar_expect_tx(&bar[2], slot_dn_bytes);
+        if (shared_unit && tid == 0) {
+            for (int g = 0; g < kGroups; ++g) mbar_arrive_expect_tx(&bar[g], group_bytes);
+            mbar_arrive_expect_tx(&bar[kGroups], kDnBytes);
+            armed = true;
         }
         __syncthreads();
-        if (my_k < kCopies) issue_copy(my_k, false);
+        if (shared_unit && my_k < kCopies) issue_copy(my_k, 0);
         // the CTA's router rows into shared memory: piece k of D/16 code pieces, D/512 scale
         // pieces and D/512 bias pieces of 16 bytes per row
         {
@@ -398,61 +410,55 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         }
         const int my_row = r_lo + warp;
         const float row_bias = my_row < E && Ly.bias ? Ly.bias[my_row] : 0.f;
-        float nw[4];
+        float nw[D / kThreads];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) nw[a] = tid + a * kThreads < D ? Ly.norm[tid + a * kThreads] : 0.f;
+        for (int a = 0; a < D / kThreads; ++a) nw[a] = Ly.norm[tid + a * kThreads];
         // the next layer's descriptor into the other slot (read from S0 of the next layer on)
         if (l + 1 < p.n_layers && tid >= kThreads - kDescWords)
             reinterpret_cast<uint32_t *>(sm + f.desc_off + ((l + 1) & 1) * kDescBytes)[tid - (kThreads - kDescWords)] =
                 reinterpret_cast<const uint32_t *>(p.layers + l + 1)[tid - (kThreads - kDescWords)];
 
-        // ---- S1: residual row -> h; thread t holds x[t + 512 a]
-        float xv[4];
-        bool ok = true;
+        // ---- S1: x_l = x_{l-1} + y_{l-1} -> h
         if (l == 0) {
 #pragma unroll
-            for (int a = 0; a < 4; ++a) xv[a] = tid + a * kThreads < D ? p.x[tid + a * kThreads] : 0.f;
+            for (int a = 0; a < D / kThreads; ++a) xv[a] = p.x[tid + a * kThreads];
         } else {
-            if (tid == 0 && !wait_count(p.ctr_x, (gen - 1) * (uint32_t)G, p.err)) *abort_s = 1;
+            if (tid == 0) {
+                if (!wait_count(p.ctr_y, (gen - 1) * (uint32_t)G, p.err)) {
+                    atomicOr(p.err, kErrTimeout);
+                    *abort_s = 1;
+                } else {
+                    __threadfence();  // every CTA's additions into y_{l-1} precede its arrival
+                    if (*reinterpret_cast<const volatile uint32_t *>(p.err) & kErrRange) *abort_s = 1;
+                }
+            }
             __syncthreads();
-            int idx[4];
-            strided_idx(idx, tid, kThreads, D);
-            ok = !*abort_s && ll_gather<4>(p.ll_x, idx, gen - 1, xv, p.err);
+            if (*abort_s) break;
+            const unsigned long long *y = p.acc + (size_t)((l - 1) & 1) * D;
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
-                if (tid + a * kThreads >= D) xv[a] = 0.f;
-        }
-        if (!ok) {
-            atomicOr(p.err, kErrTimeout);
-            *abort_s = 1;
+            for (int a = 0; a < D / kThreads; ++a) xv[a] += acc_value(__ldcg(y + tid + a * kThreads));
         }
         float ss = 0.f;
 #pragma unroll
-        for (int a = 0; a < 4; ++a) ss = fmaf(xv[a], xv[a], ss);
+        for (int a = 0; a < D / kThreads; ++a) ss = fmaf(xv[a], xv[a], ss);
         ss = warp_sum_butterfly(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
-        if (*abort_s) break;
         float tot = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) tot += red[w];
         const float scale = 1.0f / sqrtf(tot / (float)D + p.eps);
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
+        for (int a = 0; a < D / kThreads; ++a) {
             const int d = tid + a * kThreads;  // a warp holds 32 consecutive d: two chunks of 16
-            float hf = 0.f;
-            if (d < D) {
-                const uint16_t h = f32_to_bf16_bits(xv[a] * scale * nw[a]);
-                hf = bf16_bits_to_f32(h);
-                xs[d] = h;
-                reinterpret_cast<float *>(xq)[((d & 15) >> 2) * cpd * 4 + (d >> 4) * 4 + (d & 3)] = hf * kXScale;
-                if (cta == 0 && p.h_trace) p.h_trace[(size_t)l * D + d] = h;
-                if (d >= d_lo && d < d_hi) xown[d - d_lo] = xv[a];
-            }
-            // chunk sums: the 16 lanes of a chunk (D is a multiple of 512, so d < D for all or none)
+            const uint16_t h = f32_to_bf16_bits(xv[a] * scale * nw[a]);
+            float hf = bf16_bits_to_f32(h);
+            reinterpret_cast<float *>(hq)[((d & 15) >> 2) * cpd * 4 + (d >> 4) * 4 + (d & 3)] = hf;
+            if (cta == 0 && p.h_trace) p.h_trace[(size_t)l * D + d] = h;
+            // chunk sums: the 16 lanes of a chunk
 #pragma unroll
             for (int n = 8; n; n >>= 1) hf += __shfl_xor_sync(kFull, hf, n);
-            if (d < D && (d & 15) == 0) xcs[d >> 4] = hf;
+            if ((d & 15) == 0) xcs[d >> 4] = hf;
         }
         cp_async_wait<0>();  // the router rows
         __syncthreads();
@@ -461,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         if (my_row < r_hi) {
             RouterRaw rr;
             router_row_from_smem(sm + f.rr_off + warp * f.rr_row_bytes(D), D, rr);
-            float v = router_raw_dot(rr, xs, D);
+            float v = router_dot_h<D>(rr, hq);
             if (my_row < E) v = v + row_bias;
             if (lane == 0) ll_store(p.ll_logit + my_row, v, gen);
         }
@@ -470,6 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
 
         // ---- S3: all logits -> the same top-8 in every CTA; word 8 of every lane is the gate logit
         if (warp == 0) {
+            bool ok = true;
             if (lane == 0 && !wait_count(p.ctr_logit, gen * (uint32_t)G, p.err)) *abort_s = 1;
             __syncwarp();
             float v[9];
@@ -518,176 +525,164 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                 }
                 if (lane == 0) {
                     coef[8] = sigmoid_ref(g);
-                    mbar_arrive_expect_tx(&bar[0], routed0);
-                    mbar_arrive_expect_tx(&bar[1], routed1);
-                    mbar_arrive_expect_tx(&bar[2], 8u * slot_dn_bytes);
-                    armed = true;
-                }
-            }
-        }
-        __syncthreads();
-        if (*abort_s) break;
-
-        // ---- S4: the routed rows of gate/up group 0
-        if (my_k < kGroupCopies) issue_copy(my_k, true);
-
-        // ---- S5: act of the CTA's pairs, group by group
-        float4 x4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) x4[i] = xq[i * cpd + my_c];
-        const float xcv = xcs[my_c];
-        // partial (gate, up) dots of chunk my_c for the group's pairs slot + slots*k; summed over
-        // the warp's chunks (butterfly within the slot's lanes) into part[warp][pair][gate/up]
-        auto group_partials = [&](int qb, int qe) {
-            constexpr int kSlots = 32 / cpw, kRounds = kGroupPairs / kSlots;
-            float gp[kRounds], up[kRounds];
-#pragma unroll
-            for (int k = 0; k < kRounds; ++k) {
-                const int q = qb + slot + kSlots * k;
-                gp[k] = up[k] = 0.f;
-                if (q < qe) {
-                    float wg[16], wu[16];
-                    chunk_denormals<BITS>(sm + f.gu_code(0) + q * f.gu_row, my_c, wg);
-                    chunk_denormals<BITS>(sm + f.gu_code(1) + q * f.gu_row, my_c, wu);
-                    const int so = q * f.gu_grp + (my_c >> 2) * 2;  // byte offset of this chunk's group
-                    const float gs = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(0, 0) + so));
-                    const float gb = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(0, 1) + so));
-                    const float us = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 0) + so));
-                    const float ub = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 1) + so));
-                    gp[k] = fmaf(gs, chunk_dot(wg, x4) * kDotScale, gb * xcv);
-                    up[k] = fmaf(us, chunk_dot(wu, x4) * kDotScale, ub * xcv);
-                }
-            }
-            // sum over the warp's chunks: butterflies within each slot's lanes, rounds interleaved
-#pragma unroll
-            for (int n = 1; n < cpw; n <<= 1)
-#pragma unroll
-                for (int k = 0; k < kRounds; ++k) {
-                    gp[k] += __shfl_xor_sync(kFull, gp[k], n);
-                    up[k] += __shfl_xor_sync(kFull, up[k], n);
-                }
-            if (cl == 0)
-#pragma unroll
-                for (int k = 0; k < kRounds; ++k) {
-                    const int ql = slot + kSlots * k;
-                    if (qb + ql < qe) {
-                        part[(warp * kGroupPairs + ql) * 2] = gp[k];
-                        part[(warp * kGroupPairs + ql) * 2 + 1] = up[k];
+                    if (routed_unit) {
+                        for (int b = 0; b < kGroups; ++b) mbar_arrive_expect_tx(&bar[b], group_bytes);
+                        mbar_arrive_expect_tx(&bar[kGroups], kDnBytes);
+                        armed = true;
                     }
                 }
-        };
-        // warp 0: pair (lane >> 1) of the group, lane & 1 gate / up: the 16 warp partials in order
-        auto group_act = [&](int qb, int qe) {
-            if (warp != 0) return;
-            const int ql = lane >> 1, q = qb + ql;
-            float s = 0.f;
-            if (q < qe)
-#pragma unroll
-                for (int w = 0; w < kWarps; ++w) s += part[(w * kGroupPairs + ql) * 2 + (lane & 1)];
-            const float u = __shfl_down_sync(kFull, s, 1);
-            if (q < qe && !(lane & 1)) {
-                const int pp = p_lo + q, j = pp / I, i = pp - j * I;
-                ll_store(p.ll_act + (size_t)j * I + (i & 15) * (I / 16) + (i >> 4), silu_ref(s) * u, gen);
-            }
-        };
-        ok = mbar_wait(&bar[0], ph, p.err, kErrTimeout);
-        // group 1 streams while group 0 is computed (issued whatever the wait gave, so that every
-        // requested byte lands before this CTA can leave)
-        if (my_k >= kGroupCopies && my_k < kGuCopies) issue_copy(my_k, true);
-        if (ok) group_partials(0, g_end);
-        __syncthreads();
-        if (ok) group_act(0, g_end);
-        ok = mbar_wait(&bar[1], ph, p.err, kErrTimeout) && ok;
-        if (my_k >= kGuCopies && my_k < kCopies) issue_copy(my_k, true);  // down rows, behind group 1
-        __syncthreads();  // group 0's partials are consumed
-        if (ok) group_partials(g_end, np);
-        if (!ok) *abort_s = 1;
-        __syncthreads();
-        if (*abort_s) break;
-        group_act(g_end, np);
-        __syncthreads();
-        if (tid == 0) {
-            atomicAdd(p.ctr_act, 1u);
-            if (!wait_count(p.ctr_act, gen * (uint32_t)G, p.err)) {
-                atomicOr(p.err, kErrTimeout);
-                *abort_s = 1;
             }
         }
         __syncthreads();
         if (*abort_s) break;
+        // every CTA has read y_{l-1} (before its logits): clear this CTA's slice of the buffer that
+        // layer l + 1 adds into
+        if (tid < nd) p.acc[(size_t)((l + 1) & 1) * D + d_lo + tid] = 0ull;
+        if (has_unit) {
+            const int e = routed_unit ? ids_s[uj] : 0;
+            if (routed_unit && my_k < kCopies) issue_copy(my_k, e);
+            load_down_sb(e);
+        }
 
-        // ---- S6 + S7: warp 7 + j: act of slot j, chunk `lane`, against the down rows of slot j
-        // (warp 0, which ran the top-8 and the act sums, stays out)
-        if (warp >= kWarps - 9) {
-            const int j = warp - (kWarps - 9);
-            float av[16];
-            ok = ll_gather_strided<16>(p.ll_act + j * I + lane, I / 16, gen, av, p.err);
-            float asum = 0.f;
+        if (has_unit) {
+            // ---- S4: act of the unit's 32 pairs, group by group
+            float4 x4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 hv = hq[i * cpd + my_c];
+                x4[i] = make_float4(hv.x * kXScale, hv.y * kXScale, hv.z * kXScale, hv.w * kXScale);
+            }
+            const float xcv = xcs[my_c];
+            // partial (gate, up) dots of chunk my_c for the group's pairs slot + slots*k; summed over
+            // the warp's chunks (butterfly within the slot's lanes) into part[g & 1][warp][pair][gate/up]
+            auto group_partials = [&](int g) {
+                constexpr int kSlots = 32 / cpw, kRounds = (kGroupPairs + kSlots - 1) / kSlots;
+                float gp[kRounds], up[kRounds];
+#pragma unroll
+                for (int k = 0; k < kRounds; ++k) {
+                    const int ql = slot + kSlots * k, q = g * kGroupPairs + ql;
+                    gp[k] = up[k] = 0.f;
+                    if (ql < kGroupPairs) {
+                        float wg[16], wu[16];
+                        chunk_denormals<BITS>(sm + f.gu_code(0) + q * f.gu_row, my_c, wg);
+                        chunk_denormals<BITS>(sm + f.gu_code(1) + q * f.gu_row, my_c, wu);
+                        const int so = q * f.gu_grp + (my_c >> 2) * 2;  // byte offset of this chunk's group
+                        const float gs = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(0, 0) + so));
+                        const float gb = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(0, 1) + so));
+                        const float us = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 0) + so));
+                        const float ub = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.gu_sb(1, 1) + so));
+                        gp[k] = fmaf(gs, chunk_dot(wg, x4) * kDotScale, gb * xcv);
+                        up[k] = fmaf(us, chunk_dot(wu, x4) * kDotScale, ub * xcv);
+                    }
+                }
+#pragma unroll
+                for (int n = 1; n < cpw; n <<= 1)
+#pragma unroll
+                    for (int k = 0; k < kRounds; ++k) {
+                        gp[k] += __shfl_xor_sync(kFull, gp[k], n);
+                        up[k] += __shfl_xor_sync(kFull, up[k], n);
+                    }
+                if (cl == 0)
+#pragma unroll
+                    for (int k = 0; k < kRounds; ++k) {
+                        const int ql = slot + kSlots * k;
+                        if (ql < kGroupPairs) {
+                            float *pp = part + (((g & 1) * kWarps + warp) * kGroupPairs + ql) * 2;
+                            pp[0] = gp[k];
+                            pp[1] = up[k];
+                        }
+                    }
+            };
+            // warp 0: pair (lane >> 1) of the group, lane & 1 gate / up: the 16 warp partials in order
+            auto group_act = [&](int g) {
+                if (warp != 0) return;
+                const int ql = lane >> 1;
+                float s = 0.f;
+                if (ql < kGroupPairs)
+#pragma unroll
+                    for (int w = 0; w < kWarps; ++w) s += part[(((g & 1) * kWarps + w) * kGroupPairs + ql) * 2 + (lane & 1)];
+                const float u = __shfl_down_sync(kFull, s, 1);
+                if (ql < kGroupPairs && !(lane & 1)) act_s[g * kGroupPairs + ql] = silu_ref(s) * u;
+            };
+            bool ok = true;
+#pragma unroll 1
+            for (int g = 0; g < kGroups; ++g) {
+                ok = mbar_wait(&bar[g], ph, p.err, kErrTimeout) && ok;
+                if (ok) group_partials(g);
+                __syncthreads();
+                if (ok) group_act(g);
+            }
+            ok = mbar_wait(&bar[kGroups], ph, p.err, kErrTimeout) && ok;
+            if (!ok) *abort_s = 1;
+            __syncthreads();  // the unit's act values are complete
+            if (*abort_s) break;
+
+            // ---- S5: lane pair (row r, half hf): 16 columns of down row r against act, pairs summed;
+            // c_slot * sum rounded to the accumulator's grid and added into y_l[r]
+            const int hf = lane & 1;
             float4 a4[4];
+            float asum = 0.f;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                asum += (av[4 * q] + av[4 * q + 1]) + (av[4 * q + 2] + av[4 * q + 3]);
-                a4[q] = make_float4(av[4 * q] * kXScale, av[4 * q + 1] * kXScale, av[4 * q + 2] * kXScale,
-                                    av[4 * q + 3] * kXScale);
+                const float4 av = reinterpret_cast<const float4 *>(act_s)[4 * hf + q];
+                asum += (av.x + av.y) + (av.z + av.w);
+                a4[q] = make_float4(av.x * kXScale, av.y * kXScale, av.z * kXScale, av.w * kXScale);
             }
-            ok = ok && mbar_wait(&bar[2], ph, p.err, kErrTimeout);
-            if (!ok) {
+            const float cj = coef[uj];
+            unsigned long long *y = p.acc + (size_t)(l & 1) * D;
+            bool range = false;
+#pragma unroll 2
+            for (int a = 0; a < D / 256; ++a) {
+                const int r = (tid >> 1) + 256 * a;
+                float w[16];
+                chunk_denormals<BITS>(sm + f.dn_off + r * kDnRowBytes + dn_delta, hf, w);
+                const float sc = bf16_bits_to_f32(dn_s[r]), bi = bf16_bits_to_f32(dn_b[r]);
+                float v = fmaf(sc, chunk_dot(w, a4) * kDotScale, bi * asum);
+                v += __shfl_xor_sync(kFull, v, 1);
+                const float c = cj * v;
+                if (!hf) {
+                    long long qv = 0;
+                    if (fabsf(c) < kAccLimit)
+                        qv = __float2ll_rn(c * kAccScale);
+                    else
+                        range = true;  // also NaN
+                    atomicAdd(y + r, (unsigned long long)qv);
+                }
+            }
+            if (range) atomicOr(p.err, kErrRange);
+            armed = false;  // every copy of the layer has landed
+        }
+        __syncthreads();  // the regions are reused by the next layer's copies; the additions are issued
+        if (tid == 0) {
+            __threadfence();  // this CTA's additions (and its accumulator clears) before its arrival
+            atomicAdd(p.ctr_y, 1u);
+        }
+    }
+    cp_async_wait<0>();  // an abandoned layer may still be copying its router rows
+    __syncthreads();
+    if (cta == 0 && !*abort_s) {
+        // the output row: x = x_{L-1} + y_{L-1}
+        if (tid == 0) {
+            if (!wait_count(p.ctr_y, (base + (uint32_t)p.n_layers) * (uint32_t)G, p.err)) {
                 atomicOr(p.err, kErrTimeout);
                 *abort_s = 1;
             } else {
-                // four outputs at a time: their loads, dots and butterflies interleave
-                for (int o0 = 0; o0 < nd; o0 += 4) {
-                    float v[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int o = o0 + u;
-                        v[u] = 0.f;
-                        if (o < nd) {
-                            const int r = j * f.outs + o;
-                            float w[16];
-                            chunk_denormals<BITS>(sm + f.dn_code() + r * f.dn_row, lane, w);
-                            const int so = r * f.dn_grp + (lane >> 2) * 2;
-                            const float sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.dn_sb(0) + so));
-                            const float bi = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(sm + f.dn_sb(1) + so));
-                            v[u] = fmaf(sc, chunk_dot(w, a4) * kDotScale, bi * asum);
-                        }
-                    }
-#pragma unroll
-                    for (int n = 16; n; n >>= 1)
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) v[u] += __shfl_xor_sync(kFull, v[u], n);
-                    if (lane == 0)
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            if (o0 + u < nd) part[j * kMaxOuts + o0 + u] = v[u];
-                }
+                __threadfence();
+                if (*reinterpret_cast<const volatile uint32_t *>(p.err) & kErrRange) *abort_s = 1;
             }
         }
         __syncthreads();
-        if (*abort_s) break;
-        const bool last = l + 1 == p.n_layers;
-        if (tid < nd) {
-            float out = 0.f;
+        if (!*abort_s) {
+            const unsigned long long *y = p.acc + (size_t)((p.n_layers - 1) & 1) * D;
 #pragma unroll
-            for (int j = 0; j < 9; ++j) out = fmaf(coef[j], part[j * kMaxOuts + tid], out);
-            const int d = d_lo + tid;
-            const float xn = xown[tid] + out;
-            if (last)
-                p.x[d] = xn;
-            else
-                ll_store(p.ll_x + d, xn, gen);
+            for (int a = 0; a < D / kThreads; ++a)
+                p.x[tid + a * kThreads] = xv[a] + acc_value(__ldcg(y + tid + a * kThreads));
         }
-        __syncthreads();  // the regions are reused by the next layer's copies
-        if (tid == 0) atomicAdd(p.ctr_x, 1u);
     }
     if (tid == 0) {
-        if (*abort_s) {
-            // leave no copy in flight into this CTA's shared memory: complete the barriers' phases
-            // (arriving without the routed bytes if they were never requested) and wait for them
-            if (!armed)
-                for (int b = 0; b < 3; ++b) mbar_arrive_expect_tx(&bar[b], 0);
-            for (int b = 0; b < 3; ++b) mbar_wait(&bar[b], ph, p.err, kErrTimeout);
-        }
+        // leave no copy in flight into this CTA's shared memory
+        if (*abort_s && armed)
+            for (int b = 0; b <= kGroups; ++b) mbar_wait(&bar[b], ph, p.err, kErrTimeout);
         if (cta == 0) *reinterpret_cast<volatile uint32_t *>(p.gen_base) = base + (uint32_t)p.n_layers;
     }
 }

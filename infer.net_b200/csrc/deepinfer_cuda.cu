@@ -104,7 +104,9 @@ struct Context {
     // the per-layer descriptors of the last stack, re-uploaded when its key changes
     unsigned long long *ll = nullptr;
     size_t ll_words = 0;
+    size_t ll_used = 0;  // words of the layout the last stack call used
     ds::StackLayer *d_stack = nullptr;
+    CUtensorMap *d_stack_maps = nullptr;  // [stack_cap][2] down-column maps of the stack kernel
     size_t stack_cap = 0;
     std::vector<ds::StackLayer> h_stack;
     std::vector<uint64_t> stack_key;
@@ -246,9 +248,9 @@ StackKernel stack_kernel(int bits, int D) {
 }
 
 // The persistent one-token stack kernel: layers sharing D, I, E and bits; D in {512, 1024, 2048}
-// (a power-of-two number of 16-element chunks per warp), I = 512 (one chunk of a down row per
-// lane), at most 32 (gate, up) pairs and 16 outputs per CTA, its per-CTA share in shared memory,
-// and one CTA resident on every SM (a cooperative launch).
+// (a power-of-two number of 16-element chunks per warp), I = 512 (16 units of 32 columns per
+// expert slot), E <= 256, at least one CTA per unit (144), its shared-memory share within the
+// limit, and one CTA resident on every SM (a cooperative launch).
 bool stack_fits(Context *c, void *const *layers, int n) {
     const Layer *L0 = static_cast<const Layer *>(layers[0]);
     for (int l = 0; l < n; ++l) {
@@ -256,10 +258,9 @@ bool stack_fits(Context *c, void *const *layers, int n) {
         if (L->D != L0->D || L->I != L0->I || L->E != L0->E || L->bits != L0->bits) return false;
     }
     const int D = L0->D, I = L0->I;
-    if ((D != 512 && D != 1024 && D != 2048) || I != ds::kI || L0->E > 256) return false;
-    const ds::Layout f = ds::layout(D, I, L0->bits, c->sms);
-    const int smem = f.total;
-    if (smem > 227 * 1024 || f.pairs > 2 * ds::kGroupPairs || f.outs > ds::kMaxOuts) return false;
+    if ((D != 512 && D != 1024 && D != 2048) || I != ds::kI || L0->E > 256 || c->sms < ds::kUnits) return false;
+    const int smem = ds::layout(D, L0->bits).total;
+    if (smem > 227 * 1024) return false;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel(L0->bits, D), ds::kThreads, smem) !=
         cudaSuccess) {
@@ -269,15 +270,18 @@ bool stack_fits(Context *c, void *const *layers, int n) {
     return per_sm >= 1;
 }
 
+void encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t dim0, uint64_t dim1,
+               uint64_t stride, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw);
+
 // Enqueue the persistent stack kernel for one token: x (f32 [D]) is updated in place; h_trace /
 // ids_trace (device, optional) receive every layer's normalised input row and expert ids.
 void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, float eps, float *x, uint16_t *h_trace,
                    int32_t *ids_trace) {
     const Layer *L0 = static_cast<const Layer *>(layers[0]);
     const int D = L0->D, I = L0->I, E = L0->E;
-    // exchange words: [0] the generation counter and the x arrivals, [1] the act and logit
-    // arrivals, then x [D], act [9 I], logits [E + 1]
-    const size_t words = 2 + (size_t)D + 9 * (size_t)I + E + 1;
+    // exchange words: [0] the generation counter and the y arrivals, [1] the logit arrivals, then
+    // the accumulators y [2][D], logits [E + 1]
+    const size_t words = 2 + 2 * (size_t)D + E + 1;
     if (c->ll_words < words) {
         if (c->ll) CK(cudaFree(c->ll));
         c->ll = nullptr;
@@ -285,7 +289,11 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
         CK(cudaMalloc(&c->ll, words * 8));
         CK(cudaMemsetAsync(c->ll, 0, words * 8, c->stream));  // generation 0 matches no exchange
         c->ll_words = words;
+    } else if (c->ll_used != words) {
+        // another geometry's words may sit where this one's logit words are: start over
+        CK(cudaMemsetAsync(c->ll, 0, c->ll_words * 8, c->stream));
     }
+    c->ll_used = words;
     std::vector<uint64_t> key = {(uint64_t)n, (uint64_t)(uintptr_t)norms};
     for (int l = 0; l < n; ++l) {
         const Layer *L = static_cast<const Layer *>(layers[l]);
@@ -312,15 +320,33 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
             if (c->d_stack) CK(cudaFree(c->d_stack));
             c->d_stack = nullptr;
             c->stack_cap = 0;
+            if (c->d_stack_maps) CK(cudaFree(c->d_stack_maps));
+            c->d_stack_maps = nullptr;
             CK(cudaMalloc(&c->d_stack, (size_t)n * sizeof(ds::StackLayer)));
+            CK(cudaMalloc(&c->d_stack_maps, (size_t)n * 2 * sizeof(CUtensorMap)));
             c->stack_cap = n;
+        }
+        // the down codes as 2-D byte tensors [rows][I * bits / 8]: a unit copies 32-byte columns of
+        // 256 rows at a time
+        std::vector<CUtensorMap> maps((size_t)n * 2);
+        for (int l = 0; l < n; ++l) {
+            const ds::StackLayer &s = c->h_stack[l];
+            const uint64_t rb = (uint64_t)I * L0->bits / 8;
+            encode_2d(&maps[2 * l], CU_TENSOR_MAP_DATA_TYPE_UINT8, s.Dn.packed, rb, (uint64_t)E * D, rb, ds::kDnRowBytes,
+                      ds::kDnBox, CU_TENSOR_MAP_SWIZZLE_NONE);
+            encode_2d(&maps[2 * l + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, s.SD.packed, rb, (uint64_t)D, rb, ds::kDnRowBytes,
+                      ds::kDnBox, CU_TENSOR_MAP_SWIZZLE_NONE);
         }
         CK(cudaMemcpyAsync(c->d_stack, c->h_stack.data(), (size_t)n * sizeof(ds::StackLayer), cudaMemcpyHostToDevice,
                            c->stream));
+        CK(cudaMemcpyAsync(c->d_stack_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice,
+                           c->stream));
+        CK(cudaStreamSynchronize(c->stream));  // `maps` is pageable host memory
         c->stack_key = key;
     }
     ds::StackParams sp;
     sp.layers = c->d_stack;
+    sp.dn_maps = c->d_stack_maps;
     sp.n_layers = n;
     sp.E = E;
     sp.eps = eps;
@@ -328,17 +354,15 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
     sp.h_trace = h_trace;
     sp.ids_trace = ids_trace;
     sp.gen_base = reinterpret_cast<uint32_t *>(c->ll);
-    sp.ctr_x = sp.gen_base + 1;
-    sp.ctr_act = sp.gen_base + 2;
-    sp.ctr_logit = sp.gen_base + 3;
-    sp.ll_x = c->ll + 2;
-    sp.ll_act = sp.ll_x + D;
-    sp.ll_logit = sp.ll_act + 9 * (size_t)I;
+    sp.ctr_y = sp.gen_base + 1;
+    sp.ctr_logit = sp.gen_base + 2;
+    sp.acc = c->ll + 2;
+    sp.ll_logit = sp.acc + 2 * (size_t)D;
     sp.err = c->d_err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c->sms);
     cfg.blockDim = dim3(ds::kThreads);
-    cfg.dynamicSmemBytes = ds::layout(D, I, L0->bits, c->sms).total;
+    cfg.dynamicSmemBytes = ds::layout(D, L0->bits).total;
     cfg.stream = c->stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once: they exchange data
@@ -707,6 +731,7 @@ const char *device_error_text(uint32_t e) {
     if (e & kErrNonFinite) return "Non-finite router logits.";
     if (e & kErrBadExpert) return "Expert ID out of bounds";
     if (e & kErrTimeout) return "Device wait timed out";
+    if (e & kErrRange) return "Decode output outside the fixed-point accumulator's range";
     return "Internal work list overflow";
 }
 
@@ -791,6 +816,7 @@ API void di_quant_destroy(void *p) {
     if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
     if (c->ll) cudaFree(c->ll);
     if (c->d_stack) cudaFree(c->d_stack);
+    if (c->d_stack_maps) cudaFree(c->d_stack_maps);
     if (c->ev_start) cudaEventDestroy(c->ev_start);
     if (c->ev_stop) cudaEventDestroy(c->ev_stop);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -1428,7 +1454,7 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
             }
         };
         CK(cudaMemsetAsync(b.counter, 0, 2 * sizeof(uint32_t), c->stream));
-        const bool persistent = gemv && T == 1 && !profile && stack_fits(c, layers, n_layers);
+        bool persistent = gemv && T == 1 && !profile && stack_fits(c, layers, n_layers);
         if (persistent) {
             // one token: every layer in one persistent cooperative kernel
             enqueue_stack(c, layers, n_layers, dn, eps, dx, dht, dit);
@@ -1471,6 +1497,18 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
         CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
         if (dev_io) CK(cudaEventRecord(c->ev_stop, c->stream));
         CK(cudaStreamSynchronize(c->stream));
+        if (persistent && *c->h_err == kErrRange) {
+            // an output outside the one-token kernel's fixed-point range (it left x unwritten):
+            // start its exchange state over and compute the token with the per-layer kernels
+            CK(cudaMemsetAsync(c->ll, 0, c->ll_words * 8, c->stream));
+            CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
+            persistent = false;
+            enqueue_layers();
+            if (launch_check(error, capacity)) return -1;
+            CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+            if (dev_io) CK(cudaEventRecord(c->ev_stop, c->stream));
+            CK(cudaStreamSynchronize(c->stream));
+        }
         if (*c->h_err) {
             if (persistent && (*c->h_err & kErrTimeout)) {
                 // an abandoned call leaves arrival counts and generations out of step: start over

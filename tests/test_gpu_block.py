@@ -214,6 +214,34 @@ def test_persistent_stack_small_geometry(ctx, bits):
         G.close()
 
 
+def test_stack_output_beyond_fixed_point_range_is_recomputed(ctx):
+    # the one-token kernel adds the experts' outputs in a fixed-point accumulator that takes
+    # contributions below 2^23; a shared expert whose down scales and biases are multiplied by 2^32
+    # (exact in bf16) exceeds it, so the kernel leaves x unwritten and the host computes the token
+    # with the per-layer kernels; an ordinary call afterwards runs in the persistent kernel again
+    D = 512
+    L = O.Layer(46, bits=8, E=64, D=D, I=512)
+    m = L.m["shared_down"]
+    for arr in (m.scales, m.biases):
+        nz = (arr & 0x7F80) != 0
+        arr[nz] += np.uint16(32 << 7)
+    G = di.MoeLayer.from_oracle(ctx, L)
+    x0 = O.bf16_to_f32(O.gen_bf16(18, O.ACT_STREAM, D)).reshape(1, D)
+    xg, ht, it, _ = di.moe_stack(ctx, [G], np.ones((1, D), np.float32), x0, 1e-6, di.PATH_GEMV, trace=True)
+    rc, out, ids, _, _ = O.moe_block(L, ht[0], O.MODE_F32)
+    assert rc == 0 and np.array_equal(ids, it[0])
+    ref = x0 + out
+    assert np.abs(ref).max() > 2.0**26
+    assert np.linalg.norm(xg - ref) / np.linalg.norm(ref) <= REL_L2
+    G.close()
+    L2, G2 = layer_pair(ctx, 47, 8, 64, D, 512)
+    xg, ht, it, _ = di.moe_stack(ctx, [G2], np.ones((1, D), np.float32), x0, 1e-6, di.PATH_GEMV, trace=True)
+    rc, out, ids, _, _ = O.moe_block(L2, ht[0], O.MODE_F32)
+    assert rc == 0 and np.array_equal(ids, it[0])
+    ma, rl = O.tolerance_report(xg, x0 + out)
+    assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
+
+
 def test_top8_exact_ties_go_to_the_lower_id(ctx):
     # router rows 3, 40, 77, 150 and 10, 11 are copies of one another with equal bias, so their
     # logits tie exactly; the selection order must be ascending id within each tie group in the
