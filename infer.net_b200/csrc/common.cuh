@@ -124,6 +124,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders this thread's global accesses of the async proxy (bulk copies, reductions) with its
+// later generic ones.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Bulk reduction: dst[i] += src[i] for `bytes` / 8 unsigned 64-bit words, performed at L2 by the
+// copy engine (both addresses 16-byte aligned, bytes a multiple of 16); tracked by this thread's
+// bulk async-groups.
+__device__ __forceinline__ void bulk_reduce_add_u64(void *dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.u64 [%0], [%1], %2;" ::"l"(
+                     __cvta_generic_to_global(dst)),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
+// A 16-bit load (zero-extended into a 32-bit register, so no instruction touches the value until
+// it is used) through the read-only path that the compiler may not move or merge: its latency
+// overlaps whatever runs until then.
+__device__ __forceinline__ uint32_t ld_nc_u16(const uint16_t *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
 
 __device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gmem_src, bool valid) {
     uint32_t n = valid ? 16u : 0u;  // src-size 0 zero-fills the 16 bytes

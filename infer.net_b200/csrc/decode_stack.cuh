@@ -22,8 +22,9 @@
 //       warp w owns chunks [w*D/256, (w+1)*D/256) of h (in registers), its lanes (pair, chunk);
 //       the 16 warp partials of a pair are summed in a fixed order;
 //   S5  for every output d: c_slot * sum over its 32 columns of down[d][i] * act[i] (a lane pair
-//       per row, 16 columns each), rounded to a multiple of 2^-32 and added into y_l[d]; then
-//       the CTA's arrival on the layer's counter (after a device-scope fence).
+//       per row, 16 columns each), rounded to a multiple of 2^-32; one bulk reduction of the copy
+//       engine adds the CTA's D values into y_l at L2; then the CTA's arrival on the layer's
+//       counter (after a device-scope fence).
 // The last layer's sum is added to x by CTA 0, which writes the output row.
 //
 // The logits travel in flag-in-data words: {f32 value, generation} in one 64-bit store, so a
@@ -62,6 +63,7 @@ constexpr int kDescBytes = 384;               // one StackLayer in shared memory
 // contributions of an output stay below 2^62.2 (no overflow). A larger or non-finite one sets
 // kErrRange and the host recomputes the token with the per-layer kernels.
 constexpr float kAccScale = 0x1p32f;
+constexpr int kAccCopies = 4;  // CTA c adds into copy c % 4: 36 contributions per address, not 144
 constexpr float kAccInv = 0x1p-32f;
 constexpr float kAccLimit = 0x1p23f;
 
@@ -81,24 +83,23 @@ struct StackParams {
     uint16_t *h_trace;              // [n_layers][D] or null
     int32_t *ids_trace;             // [n_layers][8] or null
     unsigned long long *ll_logit;   // [E + 1] exchange words
-    unsigned long long *acc;        // [2][D] fixed-point layer outputs: layer l adds into acc[l & 1]
+    unsigned long long *acc;        // [2][kAccCopies][D] fixed-point layer outputs: layer l adds into acc[l & 1]
     uint32_t *gen_base;             // generations used by earlier calls
     uint32_t *ctr_y, *ctr_logit;    // arrivals (G per layer step)
     uint32_t *err;
 };
 
 // Shared memory of one CTA: h (f32) [4][D/16] float4 (float4 q of chunk c at [q][c]) and its chunk
-// sums [D/16]; two layer descriptors; gate/up partial sums [2][16 warps][8 pairs][2]; its router
+// sums [D/16]; two layer descriptors; gate/up partial sums [16 warps][32 pairs][2]; its router
 // rows (codes [D], scales [D/64], biases [D/64] each); the gate/up region of the unit: gate codes
-// [32][gu_row], up codes, gate scales, gate biases, up scales, up biases; the down columns [D][32 B]
-// and their scales [D] and biases [D]; misc.
+// [32][gu_row], up codes, gate scales, gate biases, up scales, up biases (once consumed, it holds the
+// unit's fixed-point output vector [D]); the down columns [D][32 B]; misc.
 struct Layout {
     int gu_row, gu_grp;
-    int xc_off, desc_off, part_off, rr_off, gu_off, dn_off, dsb_off, misc_off, total;
+    int xc_off, desc_off, part_off, rr_off, gu_off, dn_off, misc_off, total;
     __host__ __device__ int rr_row_bytes(int D) const { return D + D / 16; }  // codes, scales, biases
     __host__ __device__ int gu_code(int m) const { return gu_off + m * kSlice * gu_row; }
     __host__ __device__ int gu_sb(int m, int k) const { return gu_off + 2 * kSlice * gu_row + (2 * m + k) * kSlice * gu_grp; }
-    __host__ __device__ int dn_sb(int k, int D) const { return dsb_off + k * D * 2; }
     // misc: 5 mbarriers (gate/up groups 0-3, down), ids[8], coef[9], red[16], abort flag, act[32]
     __host__ __device__ int bar() const { return misc_off; }
     __host__ __device__ int ids() const { return misc_off + 64; }
@@ -114,11 +115,10 @@ __host__ __device__ inline Layout layout(int D, int bits) {
     f.xc_off = D * 4;
     f.desc_off = f.xc_off + ((D / 16 * 4 + 127) & ~127);
     f.part_off = f.desc_off + 2 * kDescBytes;
-    f.rr_off = f.part_off + 2 * kWarps * kGroupPairs * 2 * 4;
+    f.rr_off = f.part_off + kWarps * kSlice * 2 * 4;
     f.gu_off = (f.rr_off + 2 * (D + D / 16) + 127) & ~127;  // the CTA's (at most two) router rows
     f.dn_off = (f.gu_off + 2 * kSlice * (f.gu_row + 2 * f.gu_grp) + 127) & ~127;
-    f.dsb_off = f.dn_off + D * kDnRowBytes;
-    f.misc_off = (f.dsb_off + 2 * D * 2 + 127) & ~127;
+    f.misc_off = (f.dn_off + D * kDnRowBytes + 127) & ~127;
     f.total = f.misc_off + 224 + kSlice * 4;
     return f;
 }
@@ -290,14 +290,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float4 *hq = reinterpret_cast<float4 *>(sm);                  // h (f32), [4][D/16]
     float *xcs = reinterpret_cast<float *>(sm + f.xc_off);       // chunk sums of h
-    float *part = reinterpret_cast<float *>(sm + f.part_off);    // [2][warp][pair][gate/up]
+    float *part = reinterpret_cast<float *>(sm + f.part_off);    // [warp][pair][gate/up]
     uint64_t *bar = reinterpret_cast<uint64_t *>(sm + f.bar());  // gate/up groups 0-3, down
     int32_t *ids_s = reinterpret_cast<int32_t *>(sm + f.ids());
     float *coef = reinterpret_cast<float *>(sm + f.coef());
     float *red = reinterpret_cast<float *>(sm + f.red());
     volatile int *abort_s = reinterpret_cast<volatile int *>(sm + f.abort_flag());
     float *act_s = reinterpret_cast<float *>(sm + f.act());
-    uint16_t *dn_s = reinterpret_cast<uint16_t *>(sm + f.dn_sb(0, D)), *dn_b = reinterpret_cast<uint16_t *>(sm + f.dn_sb(1, D));
     constexpr int cpd = D / 16, cpw = cpd / kWarps;  // chunks of h; S4: chunks per warp
     const int cl = lane & (cpw - 1), slot = lane / cpw, my_c = warp * cpw + cl;
 
@@ -315,6 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
     constexpr uint32_t kDnBytes = (uint32_t)D * kDnRowBytes;
     constexpr int kGuCopies = kGroups * 6;  // per group: gate and up codes, scales, biases
     constexpr int kCopies = kGuCopies + D / kDnBox;
+    static_assert(kCopies <= 32, "one warp issues the copies");
     constexpr int kDescWords = (int)sizeof(StackLayer) / 4;
 
     if (tid == 0) {
@@ -324,9 +324,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
     }
     if (tid < kDescWords)
         reinterpret_cast<uint32_t *>(sm + f.desc_off)[tid] = reinterpret_cast<const uint32_t *>(p.layers)[tid];
-    // layer 0 adds into acc[0]: clear this CTA's slice before its first arrival (the fence below
-    // orders the stores before it); acc[1] is cleared during layer 0
-    if (tid < nd) p.acc[d_lo + tid] = 0ull;
+    // layer 0 adds into acc[0]: clear this CTA's slice of its copies before its first arrival (the
+    // fence below orders the stores before it); acc[1] is cleared during layer 0
+    if (tid < kAccCopies * nd) p.acc[(size_t)(tid / nd) * D + d_lo + tid % nd] = 0ull;
     // every CTA reads the generation base before its first exchange write; CTA 0 advances it at
     // its end, which is after the first exchange (so after every CTA has read it)
     const uint32_t base = *reinterpret_cast<const volatile uint32_t *>(p.gen_base);
@@ -361,25 +361,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                             e * D + b * kDnBox, &bar[kGroups]);
             }
         };
-        // the down rows' scale and bias of the unit's group: thread t takes rows t + 512 a (the
-        // stores wait for the loads, which are issued back to back, as the unit's copies stream)
-        auto load_down_sb = [&](int e) {
-            const QView &W = shared_unit ? Ly.SD : Ly.Dn;
-            const int gsel = uk * kSlice / 64;
-            uint16_t s[D / kThreads], b[D / kThreads];
-#pragma unroll
-            for (int a = 0; a < D / kThreads; ++a) {
-                const size_t o = ((size_t)e * D + tid + a * kThreads) * (I / 64) + gsel;
-                s[a] = __ldg(W.scales + o);
-                b[a] = __ldg(W.biases + o);
-            }
-#pragma unroll
-            for (int a = 0; a < D / kThreads; ++a) {
-                dn_s[tid + a * kThreads] = s[a];
-                dn_b[tid + a * kThreads] = b[a];
-            }
-        };
-        const int my_k = lane * kWarps + warp;  // the copy this thread issues, if below kCopies
+        // lane k of the last warp issues copy k: one warp issues them all, in order (gate/up group 0
+        // first, the down columns last)
+        const int my_k = warp == kWarps - 1 ? lane : kCopies;
         // ---- S0: token-independent copies (the shared expert's unit, the router rows)
         fence_proxy_async_smem();  // this layer's copies overwrite what the last one read
         if (shared_unit && tid == 0) {
@@ -434,9 +418,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
             }
             __syncthreads();
             if (*abort_s) break;
-            const unsigned long long *y = p.acc + (size_t)((l - 1) & 1) * D;
+            const unsigned long long *y = p.acc + (size_t)((l - 1) & 1) * kAccCopies * D;
+            unsigned long long yv[D / kThreads][kAccCopies];
 #pragma unroll
-            for (int a = 0; a < D / kThreads; ++a) xv[a] += acc_value(__ldcg(y + tid + a * kThreads));
+            for (int a = 0; a < D / kThreads; ++a)
+#pragma unroll
+                for (int k = 0; k < kAccCopies; ++k) yv[a][k] = __ldcg(y + k * D + tid + a * kThreads);
+#pragma unroll
+            for (int a = 0; a < D / kThreads; ++a) {
+                unsigned long long t = 0ull;
+#pragma unroll
+                for (int k = 0; k < kAccCopies; ++k) t += yv[a][k];
+                xv[a] += acc_value(t);
+            }
         }
         float ss = 0.f;
 #pragma unroll
@@ -537,14 +531,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         if (*abort_s) break;
         // every CTA has read y_{l-1} (before its logits): clear this CTA's slice of the buffer that
         // layer l + 1 adds into
-        if (tid < nd) p.acc[(size_t)((l + 1) & 1) * D + d_lo + tid] = 0ull;
+        if (tid < kAccCopies * nd) p.acc[(size_t)(((l + 1) & 1) * kAccCopies + tid / nd) * D + d_lo + tid % nd] = 0ull;
         if (has_unit) {
             const int e = routed_unit ? ids_s[uj] : 0;
             if (routed_unit && my_k < kCopies) issue_copy(my_k, e);
-            load_down_sb(e);
-        }
+            // the scale (even lane) or bias (odd lane) of the unit's group of down rows
+            // (tid >> 1) + 256 a, requested now and used in S5 (they stream behind the copies)
+            uint32_t dsb[D / 256];
+            {
+                const QView &W = shared_unit ? Ly.SD : Ly.Dn;
+                const uint16_t *src = ((lane & 1) ? W.biases : W.scales) + (size_t)e * D * (I / 64) + uk * kSlice / 64;
+#pragma unroll
+                for (int a = 0; a < D / 256; ++a) dsb[a] = ld_nc_u16(src + (size_t)((tid >> 1) + 256 * a) * (I / 64));
+            }
 
-        if (has_unit) {
             // ---- S4: act of the unit's 32 pairs, group by group
             float4 x4[4];
 #pragma unroll
@@ -554,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
             }
             const float xcv = xcs[my_c];
             // partial (gate, up) dots of chunk my_c for the group's pairs slot + slots*k; summed over
-            // the warp's chunks (butterfly within the slot's lanes) into part[g & 1][warp][pair][gate/up]
+            // the warp's chunks (butterfly within the slot's lanes) into part[warp][pair][gate/up]
             auto group_partials = [&](int g) {
                 constexpr int kSlots = 32 / cpw, kRounds = (kGroupPairs + kSlots - 1) / kSlots;
                 float gp[kRounds], up[kRounds];
@@ -587,38 +587,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                     for (int k = 0; k < kRounds; ++k) {
                         const int ql = slot + kSlots * k;
                         if (ql < kGroupPairs) {
-                            float *pp = part + (((g & 1) * kWarps + warp) * kGroupPairs + ql) * 2;
+                            float *pp = part + (warp * kSlice + g * kGroupPairs + ql) * 2;
                             pp[0] = gp[k];
                             pp[1] = up[k];
                         }
                     }
-            };
-            // warp 0: pair (lane >> 1) of the group, lane & 1 gate / up: the 16 warp partials in order
-            auto group_act = [&](int g) {
-                if (warp != 0) return;
-                const int ql = lane >> 1;
-                float s = 0.f;
-                if (ql < kGroupPairs)
-#pragma unroll
-                    for (int w = 0; w < kWarps; ++w) s += part[(((g & 1) * kWarps + w) * kGroupPairs + ql) * 2 + (lane & 1)];
-                const float u = __shfl_down_sync(kFull, s, 1);
-                if (ql < kGroupPairs && !(lane & 1)) act_s[g * kGroupPairs + ql] = silu_ref(s) * u;
             };
             bool ok = true;
 #pragma unroll 1
             for (int g = 0; g < kGroups; ++g) {
                 ok = mbar_wait(&bar[g], ph, p.err, kErrTimeout) && ok;
                 if (ok) group_partials(g);
-                __syncthreads();
-                if (ok) group_act(g);
             }
             ok = mbar_wait(&bar[kGroups], ph, p.err, kErrTimeout) && ok;
             if (!ok) *abort_s = 1;
-            __syncthreads();  // the unit's act values are complete
+            __syncthreads();
             if (*abort_s) break;
+            // thread 2q + m (q < 32): pair q's 16 warp partials of gate (m = 0) or up (m = 1) in order
+            if (tid < 2 * kSlice) {
+                float sv = 0.f;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) sv += part[(w * kSlice + (tid >> 1)) * 2 + (tid & 1)];
+                const float u = __shfl_down_sync(kFull, sv, 1);
+                if (!(tid & 1)) act_s[tid >> 1] = silu_ref(sv) * u;
+            }
+            __syncthreads();  // the unit's act values are complete
 
             // ---- S5: lane pair (row r, half hf): 16 columns of down row r against act, pairs summed;
-            // c_slot * sum rounded to the accumulator's grid and added into y_l[r]
+            // c_slot * sum rounded to the accumulator's grid into the unit's output vector, which one
+            // bulk reduction adds into y_l
             const int hf = lane & 1;
             float4 a4[4];
             float asum = 0.f;
@@ -629,14 +626,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                 a4[q] = make_float4(av.x * kXScale, av.y * kXScale, av.z * kXScale, av.w * kXScale);
             }
             const float cj = coef[uj];
-            unsigned long long *y = p.acc + (size_t)(l & 1) * D;
+            unsigned long long *vec = reinterpret_cast<unsigned long long *>(sm + f.gu_off);  // gate/up consumed
             bool range = false;
-#pragma unroll 2
+#pragma unroll
             for (int a = 0; a < D / 256; ++a) {
                 const int r = (tid >> 1) + 256 * a;
                 float w[16];
                 chunk_denormals<BITS>(sm + f.dn_off + r * kDnRowBytes + dn_delta, hf, w);
-                const float sc = bf16_bits_to_f32(dn_s[r]), bi = bf16_bits_to_f32(dn_b[r]);
+                const float sc = bf16_bits_to_f32(__shfl_sync(kFull, dsb[a], lane & ~1));
+                const float bi = bf16_bits_to_f32(__shfl_sync(kFull, dsb[a], lane | 1));
                 float v = fmaf(sc, chunk_dot(w, a4) * kDotScale, bi * asum);
                 v += __shfl_xor_sync(kFull, v, 1);
                 const float c = cj * v;
@@ -646,14 +644,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                         qv = __float2ll_rn(c * kAccScale);
                     else
                         range = true;  // also NaN
-                    atomicAdd(y + r, (unsigned long long)qv);
+                    vec[r] = (unsigned long long)qv;
                 }
             }
+            fence_proxy_async_smem();  // the vector, for the copy engine
             if (range) atomicOr(p.err, kErrRange);
             armed = false;  // every copy of the layer has landed
         }
-        __syncthreads();  // the regions are reused by the next layer's copies; the additions are issued
+        __syncthreads();  // the regions are reused by the next layer's copies; the vector is complete
         if (tid == 0) {
+            if (has_unit) {
+                bulk_reduce_add_u64(p.acc + (size_t)((l & 1) * kAccCopies + cta % kAccCopies) * D, sm + f.gu_off,
+                                    (uint32_t)D * 8u);
+                bulk_commit();
+                bulk_wait<0>();  // added at L2 (and the vector read: the next copies may overwrite it)
+                fence_proxy_async_global();
+            }
             __threadfence();  // this CTA's additions (and its accumulator clears) before its arrival
             atomicAdd(p.ctr_y, 1u);
         }
@@ -673,10 +679,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         }
         __syncthreads();
         if (!*abort_s) {
-            const unsigned long long *y = p.acc + (size_t)((p.n_layers - 1) & 1) * D;
+            const unsigned long long *y = p.acc + (size_t)((p.n_layers - 1) & 1) * kAccCopies * D;
 #pragma unroll
-            for (int a = 0; a < D / kThreads; ++a)
-                p.x[tid + a * kThreads] = xv[a] + acc_value(__ldcg(y + tid + a * kThreads));
+            for (int a = 0; a < D / kThreads; ++a) {
+                unsigned long long t = 0ull;
+#pragma unroll
+                for (int k = 0; k < kAccCopies; ++k) t += __ldcg(y + k * D + tid + a * kThreads);
+                p.x[tid + a * kThreads] = xv[a] + acc_value(t);
+            }
         }
     }
     if (tid == 0) {

@@ -280,8 +280,8 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
     const Layer *L0 = static_cast<const Layer *>(layers[0]);
     const int D = L0->D, I = L0->I, E = L0->E;
     // exchange words: [0] the generation counter and the y arrivals, [1] the logit arrivals, then
-    // the accumulators y [2][D], logits [E + 1]
-    const size_t words = 2 + 2 * (size_t)D + E + 1;
+    // the accumulators y [2][kAccCopies][D], logits [E + 1]
+    const size_t words = 2 + 2 * (size_t)ds::kAccCopies * D + E + 1;
     if (c->ll_words < words) {
         if (c->ll) CK(cudaFree(c->ll));
         c->ll = nullptr;
@@ -357,7 +357,7 @@ void enqueue_stack(Context *c, void *const *layers, int n, const float *norms, f
     sp.ctr_y = sp.gen_base + 1;
     sp.ctr_logit = sp.gen_base + 2;
     sp.acc = c->ll + 2;
-    sp.ll_logit = sp.acc + 2 * (size_t)D;
+    sp.ll_logit = sp.acc + 2 * (size_t)ds::kAccCopies * D;
     sp.err = c->d_err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c->sms);
