@@ -168,13 +168,13 @@ def test_stack_teacher_forced_layers(ctx):
 
 @pytest.mark.parametrize("bits", [8, 5])
 def test_full_geometry_decode_stack(ctx, bits):
-    # one token through two full-size layers: the fused decode FFN (one CTA per SM, grid barrier
-    # per layer) inside the captured decode graph, checked layer by layer like the test above
+    # one token through two full-size layers in the persistent stack kernel (one launch for both),
+    # checked layer by layer like the test above; a second call must give the same result
     n, D, T = 2, 2048, 1
     pairs = [layer_pair(ctx, 42, bits, 256, D, 512, layer=l) for l in range(n)]
     norms = (1.0 + 0.05 * np.cos(np.arange(n * D))).astype(np.float32).reshape(n, D)
     x0 = O.bf16_to_f32(O.gen_bf16(16, O.ACT_STREAM, T * D)).reshape(T, D)
-    for _ in range(2):  # first call captures the graph, the second replays it
+    for _ in range(2):
         xg, ht, it, _ = di.moe_stack(ctx, [p[1] for p in pairs], norms, x0, 1e-6, di.PATH_GEMV, trace=True)
         x = x0.copy()
         for l, (L, _) in enumerate(pairs):
@@ -303,3 +303,56 @@ def test_decode_stack_graph_replays_match(ctx):
     b = di.moe_stack(ctx, layers, norms, x0, 1e-6, di.PATH_GEMV)[0]
     c = di.moe_stack(ctx, layers, norms, x0 * 0.5, 1e-6, di.PATH_GEMV)[0]
     assert np.array_equal(a, b) and not np.array_equal(a, c)
+
+
+def _oracle_rows(L, x, rows):
+    # the oracle's block output and ids for a subset of rows (each token is independent)
+    rc, out, ids, _, _ = O.moe_block(L, x[rows], O.MODE_F32)
+    assert rc == 0
+    return out, ids
+
+
+def test_cfg3_zipf_32k_prefill_5bit(ctx):
+    # BASELINE configs[3] on one GPU: one 5-bit full-geometry layer, 32K tokens, router logits
+    # biased by -1.1 ln(e + 1) so a few experts take most routes (ragged, imbalanced grouped GEMMs).
+    # Sampled rows against the oracle; the same rows alone give the same bits.
+    E, D, T = 256, 2048, 32768
+    bias = (-1.1 * np.log(np.arange(E) + 1.0)).astype(np.float32)
+    L = O.Layer(50, bits=5, E=E, D=D, I=512, router_bias=bias)
+    G = di.MoeLayer.from_oracle(ctx, L)
+    x = O.gen_bf16(19, O.ACT_STREAM, T * D).reshape(T, D)
+    y, ids, _, _ = di.moe_block(G, x, di.PATH_GROUPED)
+    counts = np.bincount(ids.reshape(-1), minlength=E)
+    assert counts.max() > 8 * counts.mean() and counts[:8].sum() > 0.1 * ids.size
+    rows = np.random.default_rng(3).choice(T, 48, replace=False)
+    rows.sort()
+    out, oids = _oracle_rows(L, x, rows)
+    assert np.array_equal(ids[rows], oids)
+    ma, rl = O.tolerance_report(O.bf16_to_f32(y[rows]), out)
+    assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
+    y_s, ids_s, _, _ = di.moe_block(G, np.ascontiguousarray(x[rows]), di.PATH_GROUPED)
+    assert np.array_equal(ids_s, ids[rows]) and np.array_equal(y_s, y[rows])
+    G.close()
+
+
+def test_cfg4_ragged_packed_batch_matches_unpacked_requests(ctx):
+    # BASELINE configs[4] on one GPU: 16 requests of lengths drawn in [1, 4096] plus 48 single-token
+    # rows packed into one batch through one 8-bit full-geometry layer; every request run on its own
+    # gives the same bits row for row, and sampled rows match the oracle
+    E, D = 256, 2048
+    L, G = layer_pair(ctx, 1, 8, E, D, 512)
+    rng = np.random.default_rng(4)
+    lengths = list(rng.integers(1, 4097, 16)) + [1] * 48
+    T = int(sum(lengths))
+    x = O.gen_bf16(20, O.ACT_STREAM, T * D).reshape(T, D)
+    y, ids, _, _ = di.moe_block(G, x, di.PATH_GROUPED)
+    start = 0
+    for n in lengths:
+        y_r, ids_r, _, _ = di.moe_block(G, np.ascontiguousarray(x[start:start + n]), di.PATH_GROUPED)
+        assert np.array_equal(ids_r, ids[start:start + n]) and np.array_equal(y_r, y[start:start + n]), (start, n)
+        start += n
+    rows = np.sort(rng.choice(T, 48, replace=False))
+    out, oids = _oracle_rows(L, x, rows)
+    assert np.array_equal(ids[rows], oids)
+    ma, rl = O.tolerance_report(O.bf16_to_f32(y[rows]), out)
+    assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
