@@ -138,6 +138,18 @@ __device__ __forceinline__ void bulk_reduce_add_u64(void *dst, const void *src, 
                  "r"(smem_u32(src)), "r"(bytes)
                  : "memory");
 }
+// Acquire load at device scope: later loads of this thread (and, through a CTA barrier, of the
+// CTA) see every write that preceded the release it reads from.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Release reduction at device scope: every write ordered before it (this thread's, and the CTA's
+// through a preceding barrier) is visible to a reader that acquires the new value.
+__device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 // A 16-bit load (zero-extended into a 32-bit register, so no instruction touches the value until
 // it is used) through the read-only path that the compiler may not move or merge: its latency
 // overlaps whatever runs until then.

@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                     atomicOr(p.err, kErrTimeout);
                     *abort_s = 1;
                 } else {
-                    __threadfence();  // every CTA's additions into y_{l-1} precede its arrival
+                    ld_acquire_gpu(p.ctr_y);  // every CTA's additions into y_{l-1} precede its (release) arrival
                     if (*reinterpret_cast<const volatile uint32_t *>(p.err) & kErrRange) *abort_s = 1;
                 }
             }
@@ -660,8 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                 bulk_wait<0>();  // added at L2 (and the vector read: the next copies may overwrite it)
                 fence_proxy_async_global();
             }
-            __threadfence();  // this CTA's additions (and its accumulator clears) before its arrival
-            atomicAdd(p.ctr_y, 1u);
+            red_release_gpu_add(p.ctr_y, 1u);  // after this CTA's additions and accumulator clears
         }
     }
     cp_async_wait<0>();  // an abandoned layer may still be copying its router rows
@@ -673,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                 atomicOr(p.err, kErrTimeout);
                 *abort_s = 1;
             } else {
-                __threadfence();
+                ld_acquire_gpu(p.ctr_y);
                 if (*reinterpret_cast<const volatile uint32_t *>(p.err) & kErrRange) *abort_s = 1;
             }
         }
