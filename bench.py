@@ -226,8 +226,11 @@ def run_ours(args):
         threads = os.cpu_count() or 1
         tok = 64
         t = cpu_sample(tok, threads)
+        t1 = cpu_sample(8, 1)  # the same port on one core (a smaller sample)
         cpu = {"value": tok / (t * LAYERS), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{tok} tokens x 1 of 40 layers (full geometry, 8-bit) on the oracle port, extrapolated x40"}
+               "sample": f"{tok} tokens x 1 of 40 layers (full geometry, 8-bit) on the oracle port, extrapolated x40",
+               "single_core": {"value": 8 / (t1 * LAYERS), "unit": "tokens/s", "cores": 1,
+                               "sample": "8 tokens x 1 of 40 layers on one core, extrapolated x40"}}
     total_flops = FLOPS_TOKEN_LAYER * TOKENS * LAYERS
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
