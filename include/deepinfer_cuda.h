@@ -127,7 +127,11 @@ int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint16_t
 /* n_layers stacked blocks over an f32 residual stream x [T, D] (in/out):
      h = bf16(RMSNorm(x) * norms[l]);  x += block_l(h)      (gpu_graph.mm:48-61)
    norms: f32 [n_layers, D]. h_trace (bf16 [n_layers, T, D]) and ids_trace (int32 [n_layers, T, 8])
-   are optional per-layer dumps for teacher-forced checks. Decode-sized T runs as CUDA graph. */
+   are optional per-layer dumps for teacher-forced checks. One token on the GEMV path runs the whole
+   stack as one persistent kernel when the layers share D in {512, 1024, 2048}, I = 512 and E <= 256
+   (its output is exact to 2^-32 per contribution; an output beyond its fixed-point range is
+   recomputed by the per-layer kernels); other decode-sized T run as a CUDA graph of per-layer
+   kernels. */
 int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_layers, float eps, float *x, int tokens,
                  uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error, int capacity);
 
