@@ -256,7 +256,9 @@ def run_ours(args):
             "gbs": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9,
             "hbm_frac": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9 / pk["hbm_gbs"]},
         "clocks": clk.summary(),
-        "gpu_launches": args.steps * LAYERS * 8,
+        # per layer: router tiles, router GEMM, router select, scan, scatter, permute, gate_up, down,
+        # combine (+ next RMSNorm); one RMSNorm before the first layer (router norms are cached per layer)
+        "gpu_launches": args.steps * (LAYERS * 9 + 1),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -337,7 +339,9 @@ def run_expert_parallel(args, di, torch, rank, local, world):
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": Tl * D * 4 * world + LAYERS * D * 4 * world,
                 "d2h_bytes_per_step": Tl * D * 4 * world},
         "clocks": clk.summary(),
-        "gpu_launches": args.steps * LAYERS * 12,
+        # per layer: router tiles, router GEMM, router select, layout, dispatch, receive, scan, scatter,
+        # permute, gate_up, down, partial-row send, combine; one RMSNorm before the first layer
+        "gpu_launches": args.steps * (LAYERS * 13 + 1),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -59,6 +59,8 @@ struct Matrix {
     void *h[3] = {nullptr, nullptr, nullptr};
     size_t bytes[3] = {0, 0, 0};
     bool dirty[3] = {false, false, false};
+    uint64_t version = 1;  // bumped whenever the library changes the device bytes
+    bool exposed = false;  // the device buffers were handed out: writes to them are not seen
     int refs = 1;  // the caller's handle plus one per layer binding it
     bool destroyed = false;
     QView view() const {
@@ -73,6 +75,8 @@ struct Layer {
     int E = 0, D = 0, I = 0, bits = 0;
     uint64_t gen = 0;       // unique per layer object, for graph cache keys
     int E_local = 0, E_off = 0;  // expert-parallel shard: experts [E_off, E_off + E_local) are local
+    float *router_rn = nullptr;  // device: router row norms [2E] then f32 router rows [E, D]
+    uint64_t router_rn_version = 0;  // the router matrix version they were computed from
 };
 uint64_t g_layer_gen = 0;
 
@@ -163,6 +167,7 @@ void sync_matrix(Matrix *m) {
         if (m->dirty[i]) {
             CK(cudaMemcpyAsync(m->d[i], m->h[i], m->bytes[i], cudaMemcpyHostToDevice, m->ctx->stream));
             m->dirty[i] = false;
+            m->version++;
         }
 }
 
@@ -554,11 +559,34 @@ size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b,
 // Routing of a prefill-sized batch (E a multiple of 128) in two steps (route.cuh): approximate
 // logits on the tensor cores (approx: scratch of T*E bf16) with the router rows' norms, then the
 // exact canonical logits of the candidates only -> ids, probs, gate logits, per-block route counts.
-void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, float *wn, float *wf, Tile *rtiles, int32_t *rnt,
-                           uint16_t *approx, int grid, uint32_t *err, cudaStream_t st) {
+// The router rows' norms and f32 weights (router_row_norms_kernel) depend only on the router matrix:
+// each layer keeps them and recomputes them when the matrix version changes. A matrix whose device
+// buffer was handed out may change unseen, so its norms are computed into the call's scratch
+// (ws_wn, ws_wf) every time.
+void router_norms(Layer *L, cudaStream_t st, float *ws_wn, float *ws_wf, const float **wn, const float **wf) {
+    const int E = L->E, D = L->D;
+    Matrix *R = L->m[0];
+    if (R->exposed) {
+        router_row_norms_kernel<<<(E + 7) / 8, 256, 0, st>>>(R->view(), E, D, ws_wn, ws_wf);
+        *wn = ws_wn;
+        *wf = ws_wf;
+        return;
+    }
+    if (!L->router_rn) {
+        CK(cudaMalloc(&L->router_rn, sizeof(float) * (2 * (size_t)E + (size_t)E * D)));
+        L->router_rn_version = 0;
+    }
+    if (L->router_rn_version != R->version) {
+        router_row_norms_kernel<<<(E + 7) / 8, 256, 0, st>>>(R->view(), E, D, L->router_rn, L->router_rn + 2 * E);
+        L->router_rn_version = R->version;
+    }
+    *wn = L->router_rn;
+    *wf = L->router_rn + 2 * E;
+}
+void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, Tile *rtiles, int32_t *rnt, uint16_t *approx,
+                           int grid, uint32_t *err, cudaStream_t st) {
     const int E = L->E, D = L->D;
     const QView R = L->m[0]->view();
-    router_row_norms_kernel<<<(E + 7) / 8, 256, 0, st>>>(R, E, D, wn, wf);
     router_tiles_kernel<<<1, 256, 0, st>>>(T, rtiles, rnt);
     launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, R, R, R, R, x, T, nullptr, 0, nullptr, rtiles, rnt, T,
                                                  0, D, E, 1, approx, T, err),
@@ -654,9 +682,11 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (!gemv && router_tc_fits(L)) {
         // tensor-core approximate logits + exact canonical logits of the candidates
         uint16_t *approx = reinterpret_cast<uint16_t *>(b.logits);
-        enqueue_router_approx(L, x, T, b.wn, b.wf, b.rtiles, b.rnt, approx, c->sms, c->d_err, st);
+        const float *wn = nullptr, *wf = nullptr;
+        router_norms(const_cast<Layer *>(L), st, b.wn, b.wf, &wn, &wf);
+        enqueue_router_approx(L, x, T, b.rtiles, b.rnt, approx, c->sms, c->d_err, st);
         if (profile) stage_mark(c, S_TOPK);
-        enqueue_router_select(L, x, T, forced_ids, ids, probs, b.gate, b.block_counts, b.nblocks, b.wn, b.wf, approx,
+        enqueue_router_select(L, x, T, forced_ids, ids, probs, b.gate, b.block_counts, b.nblocks, wn, wf, approx,
                               c->d_err, st);
     } else {
         // every logit in the canonical f32 order
@@ -905,6 +935,7 @@ API void *di_quant_matrix_buffer(void *matrix, int index) {
 
 API void *di_quant_matrix_device_buffer(void *matrix, int index) {
     if (!live_matrix(matrix) || index < 0 || index > 2) return nullptr;
+    static_cast<Matrix *>(matrix)->exposed = true;
     return static_cast<Matrix *>(matrix)->d[index];
 }
 
@@ -924,6 +955,7 @@ API int di_quant_matrix_upload(void *matrix, int index, const void *src, uint64_
         CK(cudaStreamSynchronize(m->ctx->stream));
         if (m->h[index]) std::memcpy(m->h[index], src, bytes);
         m->dirty[index] = false;
+        m->version++;
     } catch (const CudaFail &f) {
         set_error(error, capacity, "%s", f.what.c_str());
         return -1;
@@ -952,6 +984,7 @@ API int di_quant_matrix_generate(void *matrix, uint64_t seed, uint64_t stream, f
             m->dirty[i] = false;
             if (m->h[i]) CK(cudaMemcpy(m->h[i], m->d[i], m->bytes[i], cudaMemcpyDeviceToHost));
         }
+        m->version++;
     } catch (const CudaFail &f) {
         set_error(error, capacity, "%s", f.what.c_str());
         return -1;
@@ -1202,6 +1235,7 @@ API void di_moe_layer_destroy(void *layer) {
     DeviceGuard dg(L->ctx->device);
     cudaStreamSynchronize(L->ctx->stream);
     if (L->bias) cudaFree(L->bias);
+    if (L->router_rn) cudaFree(L->router_rn);
     for (int i = 0; i < 8; ++i) release_matrix(L->m[i]);
     delete L;
 }
@@ -1960,8 +1994,10 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             if (l == 0) rmsnorm_kernel<<<T, 256, 0, st>>>(dx, dn, D, eps, h, nullptr);
             if (router_tc_fits(L)) {
                 uint16_t *approx = reinterpret_cast<uint16_t *>(logits);
-                enqueue_router_approx(L, h, T, wn, wf, rtiles, rnt, approx, grid, c->d_err, st);
-                enqueue_router_select(L, h, T, nullptr, ids, probs, gate, bc, nb_l, wn, wf, approx, c->d_err, st);
+                const float *rwn = nullptr, *rwf = nullptr;
+                router_norms(L, st, wn, wf, &rwn, &rwf);
+                enqueue_router_approx(L, h, T, rtiles, rnt, approx, grid, c->d_err, st);
+                enqueue_router_select(L, h, T, nullptr, ids, probs, gate, bc, nb_l, rwn, rwf, approx, c->d_err, st);
             } else {
                 router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
                                        router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);

@@ -356,3 +356,20 @@ def test_cfg4_ragged_packed_batch_matches_unpacked_requests(ctx):
     assert np.array_equal(ids[rows], oids)
     ma, rl = O.tolerance_report(O.bf16_to_f32(y[rows]), out)
     assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
+
+
+def test_router_weights_changed_after_a_call_are_used(ctx):
+    # the tensor-core router keeps each layer's router-row norms and f32 rows between calls; new
+    # router weights, uploaded or written through the host staging buffer, must reach the next call
+    E, D = 256, 512
+    L = O.Layer(48, bits=8, E=E, D=D, I=64)
+    G = di.MoeLayer.from_oracle(ctx, L)
+    check_block(ctx, L, G, 96, di.PATH_GROUPED)
+    L.m["router"] = O.Layer(49, bits=8, E=E, D=D, I=64).m["router"]
+    G.mats["router"].load(L.m["router"])
+    check_block(ctx, L, G, 96, di.PATH_GROUPED)
+    L.m["router"] = O.Layer(50, bits=8, E=E, D=D, I=64).m["router"]
+    for i, a in enumerate((L.m["router"].packed, L.m["router"].scales, L.m["router"].biases)):
+        G.mats["router"].write(i, a)
+    check_block(ctx, L, G, 96, di.PATH_GROUPED)
+    G.close()
