@@ -328,7 +328,7 @@ def run_expert_parallel(args, di, torch, rank, local, world):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "prefill 8192 tokens (16 x 512 chunks) x 40 MoE layers, 8-bit g64",
                    "tokens": TOKENS, "layers": LAYERS, "experts": E, "top_k": 8, "intermediate": I, "hidden": D,
-                   "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)", "tokens_per_gpu": Tl,
+                   "parallelism": f"ep{world} (dispatch and combine by peer-memory stores over NVLink; NCCL bootstraps the group)", "tokens_per_gpu": Tl,
                    "l2": "inputs larger than L2 (34.4 GB of weights per step over the node)"},
         "tensor_frac_step": total_flops / (ms * 1e-3) / (world * pk["bf16_tflops_sustained"] * 1e12),
         "roofline": {"kernel": "whole expert-parallel step", "bound": "tensor",
