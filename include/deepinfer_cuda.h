@@ -84,7 +84,9 @@ int di_quant_experts(void *ctx, void *gate, void *up, void *down, void *shared, 
 int di_quant_embedding(void *matrix, int token, float *out);
 
 /* Device-side access (no reference counterpart: Metal buffers are host-visible, CUDA device
-   memory is not). */
+   memory is not). The library does not see writes through this pointer: once it has been handed
+   out for a router matrix, the tensor-core router recomputes that matrix's row norms on every call
+   instead of keeping them per layer. */
 void *di_quant_matrix_device_buffer(void *matrix, int index);
 /* Copies `bytes` from host memory into buffer `index` (bytes must equal the buffer size). */
 int di_quant_matrix_upload(void *matrix, int index, const void *src, uint64_t bytes, char *error, int capacity);
