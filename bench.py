@@ -269,7 +269,8 @@ def run_ours(args):
 
 def run_expert_parallel(args, di, torch, rank, local, world):
     """configs[2] at N GPUs: 256/N experts per GPU, the 8192 tokens sharded 8192/N per GPU,
-    token dispatch and combine over NCCL inside the library (di_moe_ep_stack)."""
+    token rows dispatched to the experts' GPUs and partial rows returned by the library's own
+    peer-memory stores over NVLink (di_moe_ep_stack; NCCL only bootstraps the group)."""
     import datetime
 
     import numpy as np

@@ -83,6 +83,17 @@ int di_quant_experts(void *ctx, void *gate, void *up, void *down, void *shared, 
 /* quantized.mm:384-397: dequantised row `token` of a one-expert matrix into out[columns]. */
 int di_quant_embedding(void *matrix, int token, float *out);
 
+/* Dense quantised projection of a token batch on the tensor cores: y[t, r] = sum_c x[t, c] *
+   W[expert, r, c] for t < tokens, with bf16 operands (W dequantised as q*scale + bias and rounded
+   to bf16) and f32 accumulation -- the arithmetic of the reference's batched prefill projections
+   (native/DeepInfer.Metal/gpu_prefill.mm:603-614 with prefill_bf16.mm:47-53;
+   native/DeepInfer.Cuda/prefill_batch.cuh:16-52), which serve every non-expert weight of a layer.
+   x: bf16 [tokens, columns]; y: bf16 [tokens, rows]; host pointers, or device pointers with
+   DI_MOE_DEVICE_IO (the only flag). Needs columns <= 2048 (a multiple of 128 for 5-bit) and rows
+   a multiple of 8; expert in [0, experts). tokens in [1, 1048576]. */
+int di_quant_gemm(void *ctx, void *matrix, int expert, const uint16_t *x, int tokens, uint16_t *y, int flags,
+                  double *ms, char *error, int capacity);
+
 /* Device-side access (no reference counterpart: Metal buffers are host-visible, CUDA device
    memory is not). The library does not see writes through this pointer: once it has been handed
    out for a router matrix, the tensor-core router recomputes that matrix's row norms on every call
@@ -116,6 +127,9 @@ int di_moe_layer_set_router_bias(void *layer, const float *bias, char *error, in
 #define DI_MOE_PATH_GEMV 4      /* force the decode GEMV path */
 #define DI_MOE_PATH_GROUPED 8   /* force the grouped tensor-core path */
 #define DI_MOE_PROFILE 16       /* di_moe_stack: record per-stage CUDA events (read by di_moe_last_profile) */
+#define DI_MOE_ROUTER_EXACT 32  /* grouped path: every router logit in the canonical f32 order instead of
+                                   tensor-core logits with an exact check of the near-boundary candidates
+                                   (the same ids and probabilities; a checking aid, slower) */
 
 /* y[t] = sigmoid(x_t . w_sr) * shared(x_t) + sum_j p[t,j] * expert_{ids[t,j]}(x_t)
    (Qwen36Model.cs:218-245). x: bf16 [T, D] (the normalised layer input); y: bf16 [T, D].
@@ -142,14 +156,25 @@ int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_layer
    returns the number written. */
 int di_moe_last_profile(void *ctx, double *stage_ms, int n);
 
+/* The expert-grouped permutation built by the last grouped-path di_moe_block on this context (for a
+   stack: by its last layer), as prefill_build_groups orders it (native/DeepInfer.Metal/
+   prefill_moe.mm:8-17): route r = t*8 + slot of expert e sits at position seg_offsets[e] + i, routes
+   of one expert in ascending r. perm_route receives 8T route ids (max_routes >= 8T), seg_offsets and
+   seg_counts E + 1 entries (entry E is the shared expert's segment: offset 8T, T rows). Returns 8T,
+   or -1 when the last call built no permutation (decode path, failed call). */
+int di_moe_last_routes(void *ctx, int32_t *perm_route, int32_t *seg_offsets, int32_t *seg_counts, int max_routes,
+                       char *error, int capacity);
+
 /* ------------------------------------------------------------------------------------
  * Part 3. Expert parallelism across the GPUs of one node (no reference counterpart: the
  * reference has no expert, tensor or collective parallelism, docs/ARCHITECTURE.md:63).
  * One process per GPU. GPU r of G owns experts [r*E/G, (r+1)*E/G) of every layer and a
  * contiguous shard of the tokens (shards in rank order); the router, shared expert and its
- * gate are replicated. Token rows travel to the GPUs that own their experts and partial
- * expert sums travel back over NCCL (NVLink / NVSwitch). Results equal di_moe_stack on the
- * concatenated tokens up to f32 summation order; routing ids are identical.
+ * gate are replicated. Token rows travel to the GPUs that own their experts, and partial
+ * expert sums travel back, as stores of the library's own kernels into the other GPUs' memory
+ * over NVLink / NVSwitch (CUDA IPC mappings; NCCL only bootstraps the group and exchanges the
+ * mapping handles). Results equal di_moe_stack on the concatenated tokens up to f32 summation
+ * order; routing ids are identical.
  * ---------------------------------------------------------------------------------- */
 #define DI_EP_ID_BYTES 128
 /* Fills a 128-byte NCCL unique id on rank 0; the caller broadcasts it to every rank. */
@@ -162,24 +187,27 @@ void di_moe_ep_destroy(void *ep);
 void *di_moe_ep_layer_create(void *ep, void *router, void *gate, void *up, void *down, void *shared_gate,
                              void *shared_up, void *shared_down, void *shared_route, char *error, int capacity);
 /* di_moe_stack semantics on this rank's tokens x [tokens, D] (f32 residual, in/out); every rank
-   calls it with the same layers. Flags: DI_MOE_DEVICE_IO. */
+   calls it with the same layers. h_trace (bf16 [n_layers, tokens, D]) and ids_trace (int32
+   [n_layers, tokens, 8]) are optional per-layer dumps of this rank's tokens, as in di_moe_stack.
+   Flags: DI_MOE_DEVICE_IO. */
 int di_moe_ep_stack(void *ep, void *const *layers, const float *norms, int n_layers, float eps, float *x, int tokens,
-                    int flags, double *ms, char *error, int capacity);
+                    uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error, int capacity);
 
-/* Allocation-free small-batch block. No counterpart in the reference; it exists for callers
-   that must not allocate GPU memory once they are running: code recording a CUDA graph
-   (cudaMalloc is not allowed while a stream is being captured), serving loops with a
-   no-allocation rule after start-up, and processes whose device memory is already reserved
-   by another allocator, where a late cudaMalloc would fail. It computes what di_moe_block
-   computes with the decode (GEMV) path and device pointers only: x bf16 [T,D] in, y bf16
-   [T,D] out, ids int32 [T,8] and probs f32 [T,8] optional outputs, T in [1, 16].
-   Its scratch is one fixed device array of DI_MOE_STATIC_SCRATCH_BYTES per GPU that loads
-   the library (held until process exit); a call that would need more (T*E*4 + T*9*I*4 + a
-   few KB) is rejected with an error before any GPU work, and the call itself allocates
-   nothing. The first call on a device resolves that array's device address, so make it
-   before any stream capture. Every call on a device shares the array and it keeps the last
-   call's contents: calls that overlap on the GPU (other threads, other contexts on the same
-   device) race and must be serialised by the caller. */
+/* Allocation-free small-batch block. No counterpart in the reference. Some callers cannot call
+   cudaMalloc once they are running: serving loops that forbid device allocation after start-up
+   (cudaMalloc synchronises the device and its latency is unbounded), and processes whose device
+   memory is already reserved by another allocator (a framework's caching pool), where a late
+   cudaMalloc fails. di_moe_block's per-context workspace grows on demand, so it may allocate;
+   this entry never does. It computes what di_moe_block computes on the decode (GEMV) path, with
+   device pointers only: x bf16 [T,D] in, y bf16 [T,D] out, ids int32 [T,8] and probs f32 [T,8]
+   optional outputs, T in [1, 16], T*D <= 49152. All of them must be device memory of the
+   context's GPU; anything else is refused before any GPU work.
+   Its scratch is one fixed device array of DI_MOE_STATIC_SCRATCH_BYTES on every GPU that loads
+   the library (held until the process exits); a call that would need more (T*E*4 + T*9*I*4 + a
+   few KB) is refused with an error before any GPU work. The first call on a device looks up that
+   array's device address (a driver call, once per device). Every call on a device shares the
+   array and it keeps the last call's contents: calls that overlap on the GPU (other threads,
+   other contexts on the same device) race on it and must be serialised by the caller. */
 #define DI_MOE_STATIC_MAX_TOKENS 16
 #define DI_MOE_STATIC_SCRATCH_BYTES (512u * 1024u)
 int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int tokens, uint16_t *y, int32_t *ids,

@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <set>
 #include <string>
@@ -47,7 +48,10 @@ struct CudaFail {
 #define CK(call)                                                                                        \
     do {                                                                                                \
         cudaError_t e_ = (call);                                                                        \
-        if (e_ != cudaSuccess) throw CudaFail{std::string(#call) + ": " + cudaGetErrorString(e_)};      \
+        if (e_ != cudaSuccess) {                                                                        \
+            cudaGetLastError(); /* a later call's launch check must not report this failure */          \
+            throw CudaFail{std::string(#call) + ": " + cudaGetErrorString(e_)};                         \
+        }                                                                                               \
     } while (0)
 
 struct Context;
@@ -114,6 +118,10 @@ struct Context {
     size_t stack_cap = 0;
     std::vector<ds::StackLayer> h_stack;
     std::vector<uint64_t> stack_key;
+    // the expert-grouped permutation of the last grouped-path block (of the last layer of a stack):
+    // device pointers into the workspace, valid until the next call on this context
+    const int32_t *last_perm = nullptr, *last_seg_off = nullptr, *last_seg_count = nullptr;
+    int last_routes_T = 0, last_routes_E = 0;
 };
 
 std::mutex g_registry;
@@ -201,6 +209,27 @@ T *at(Context *c, size_t off) {
     return reinterpret_cast<T *>(static_cast<uint8_t *>(c->ws.base) + off);
 }
 
+// True when p is memory that the context's kernels may be handed as a device pointer: device
+// memory of that GPU, or managed memory. Pageable or pinned host memory and other GPUs' memory
+// are refused before any GPU work (the reference validates every argument before submission,
+// native/DeepInfer.Metal/quantized.mm:323-331), instead of faulting inside a kernel.
+bool device_pointer_ok(const void *p, int device) {
+    if (!p) return false;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (a.type == cudaMemoryTypeManaged) return true;
+    return a.type == cudaMemoryTypeDevice && a.device == device;
+}
+// The optional pointers of a device-I/O call: each one given must pass device_pointer_ok.
+bool device_pointers_ok(int device, std::initializer_list<const void *> ptrs) {
+    for (const void *p : ptrs)
+        if (p && !device_pointer_ok(p, device)) return false;
+    return true;
+}
+
 int launch_check(char *error, int capacity) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -227,6 +256,24 @@ void launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStre
     CK(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
 }
 
+// Cooperative launch: every CTA of the grid is resident at once, or the launch fails. Kernels
+// whose CTAs wait on one another (a grid barrier) need it; other work on the GPU may otherwise
+// hold SMs that a waiting CTA's partner needs.
+template <typename... KArgs, typename... Args>
+void launch_cooperative(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CK(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
+
 constexpr int kDecodeSmemMax = 96 * 1024;  // decode_route_kernel: T*D bf16 rows
 
 uint64_t eps_bits(float eps) {
@@ -239,7 +286,16 @@ uint64_t eps_bits(float eps) {
 // per-CTA weight share to fit in shared memory.
 bool ffn_fits(const Context *c, const Layer *L) {
     if (L->D % 512 || L->I % 512) return false;
-    return ffn_layout(L->D, L->I, L->bits, c->sms).total <= 227 * 1024;
+    const int smem = ffn_layout(L->D, L->I, L->bits, c->sms).total;
+    if (smem > 227 * 1024) return false;
+    // the cooperative launch needs one resident CTA per SM
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, L->bits == 8 ? decode_ffn_kernel<8> : decode_ffn_kernel<5>,
+                                                      kFfnThreads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return per_sm >= 1;
 }
 
 // The persistent one-token stack kernel of a geometry (null when none is built for it).
@@ -500,6 +556,7 @@ struct BlockBuffers {
     uint32_t *counter;  // [0] last-CTA ticket of decode_route_kernel (kept at zero between launches),
                         // [1] grid-barrier arrivals of decode_ffn_kernel (zeroed per call)
     int nblocks, max_tiles;
+    bool router_exact;  // grouped path: every router logit in the canonical order (no tensor-core bound)
 };
 
 size_t plan_block(Context *c, const Layer *L, int T, Carve &cv, BlockBuffers &b, bool host_io, bool gemv) {
@@ -638,16 +695,19 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
             stage_mark(c, S_GATE_UP);
         }
         if (T == 1 && ffn_fits(c, L)) {
-            // one token: the fused gate/up + down kernel (one CTA per SM, weights staged in smem)
+            // one token: the fused gate/up + down kernel (one CTA per SM, weights staged in smem);
+            // its CTAs meet at a grid barrier, so it is launched cooperatively
             const FfnLayout f = ffn_layout(D, I, L->bits, c->sms);
             if (L->bits == 8)
-                launch(decode_ffn_kernel<8>, dim3(c->sms), dim3(kFfnThreads), (size_t)f.total, st, true, (const uint16_t *)x, D, I,
-                       G, U, SG, SU, Dn, SD, (const int32_t *)ids, (const float *)probs, (const float *)b.gate, b.act32, y,
-                       stacked ? resid : nullptr, b.counter + 1, gen, c->d_err);
+                launch_cooperative(decode_ffn_kernel<8>, dim3(c->sms), dim3(kFfnThreads), (size_t)f.total, st,
+                                   (const uint16_t *)x, D, I, G, U, SG, SU, Dn, SD, (const int32_t *)ids,
+                                   (const float *)probs, (const float *)b.gate, b.act32, y, stacked ? resid : nullptr,
+                                   b.counter + 1, gen, c->d_err);
             else
-                launch(decode_ffn_kernel<5>, dim3(c->sms), dim3(kFfnThreads), (size_t)f.total, st, true, (const uint16_t *)x, D, I,
-                       G, U, SG, SU, Dn, SD, (const int32_t *)ids, (const float *)probs, (const float *)b.gate, b.act32, y,
-                       stacked ? resid : nullptr, b.counter + 1, gen, c->d_err);
+                launch_cooperative(decode_ffn_kernel<5>, dim3(c->sms), dim3(kFfnThreads), (size_t)f.total, st,
+                                   (const uint16_t *)x, D, I, G, U, SG, SU, Dn, SD, (const int32_t *)ids,
+                                   (const float *)probs, (const float *)b.gate, b.act32, y, stacked ? resid : nullptr,
+                                   b.counter + 1, gen, c->d_err);
             if (profile) {
                 stage_mark(c, S_DOWN);
                 stage_mark(c, S_COMBINE);
@@ -679,7 +739,7 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
         return;
     }
     // 1-2. router logits, top-8, probabilities, shared gate logit, per-block expert counts
-    if (!gemv && router_tc_fits(L)) {
+    if (!gemv && router_tc_fits(L) && !b.router_exact) {
         // tensor-core approximate logits + exact canonical logits of the candidates
         uint16_t *approx = reinterpret_cast<uint16_t *>(b.logits);
         const float *wn = nullptr, *wf = nullptr;
@@ -731,6 +791,11 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
     scatter_routes_kernel<<<b.nblocks, kScatterWarps * 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos);
+    c->last_perm = b.perm;
+    c->last_seg_off = b.seg_off;
+    c->last_seg_count = b.seg_count;
+    c->last_routes_T = T;
+    c->last_routes_E = E;
     // token rows in expert order for the gate/up B operand (timed with the scatter)
     permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(x, b.perm, b.seg_off + E, D, b.xp);
     if (profile) stage_mark(c, S_GATE_UP);
@@ -1168,6 +1233,85 @@ API int di_quant_embedding(void *matrix, int token, float *out) {
     return 0;
 }
 
+API int di_quant_gemm(void *ctx, void *matrix, int expert, const uint16_t *x, int tokens, uint16_t *y, int flags,
+                      double *ms, char *error, int capacity) {
+    if (!live_context(ctx) || !live_matrix(matrix)) {
+        set_error(error, capacity, "Invalid context or quantized matrix");
+        return -1;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    Matrix *m = static_cast<Matrix *>(matrix);
+    const bool dev_io = flags & DI_MOE_DEVICE_IO;
+    if (m->ctx != c) {
+        set_error(error, capacity, "Quantized matrix must belong to this device.");
+        return -1;
+    }
+    if (!x || !y || tokens < 1 || tokens > 1048576 || (flags & ~DI_MOE_DEVICE_IO)) {
+        set_error(error, capacity, "Invalid quantized GEMM arguments");
+        return -1;
+    }
+    if (expert < 0 || expert >= m->experts) {
+        set_error(error, capacity, "Expert ID out of bounds");
+        return -1;
+    }
+    // the GEMM kernel's limits: at most 32 scale groups per row (its per-unit scale buffer),
+    // 16-byte rows of codes and of output for the tensor copies
+    if (m->cols > 2048 || m->rows % 8 || (m->bits == 5 && m->cols % 128)) {
+        set_error(error, capacity,
+                  "Unsupported quantized GEMM shape: columns <= 2048 (a multiple of 128 for 5-bit), rows a multiple of 8");
+        return -1;
+    }
+    if (dev_io && !device_pointers_ok(c->device, {x, y})) {
+        set_error(error, capacity, "With DI_MOE_DEVICE_IO, x and y must be device memory of the context's GPU");
+        return -1;
+    }
+    const int T = tokens, K = m->cols, N = m->rows;
+    DeviceGuard dg(c->device);
+    try {
+        sync_matrix(m);
+        Carve cv;
+        const size_t o_x = dev_io ? 0 : cv.take<uint16_t>((size_t)T * K);
+        const size_t o_y = dev_io ? 0 : cv.take<uint16_t>((size_t)T * N);
+        const size_t o_t = cv.take<Tile>((size_t)(T + 255) / 256 + 1), o_nt = cv.take<int32_t>(1);
+        ensure_workspace(c, cv.off + 256);
+        const uint16_t *dx = dev_io ? x : at<uint16_t>(c, o_x);
+        uint16_t *dy = dev_io ? y : at<uint16_t>(c, o_y);
+        QView w = m->view();  // the chosen expert as a one-expert matrix
+        w.packed += (size_t)expert * N * w.words_per_row();
+        w.scales += (size_t)expert * N * w.groups_per_row();
+        w.biases += (size_t)expert * N * w.groups_per_row();
+        w.experts = 1;
+        CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
+        CK(cudaEventRecord(c->ev_start, c->stream));
+        if (!dev_io) CK(cudaMemcpyAsync(const_cast<uint16_t *>(dx), x, (size_t)T * K * 2, cudaMemcpyHostToDevice, c->stream));
+        router_tiles_kernel<<<1, 256, 0, c->stream>>>(T, at<Tile>(c, o_t), at<int32_t>(c, o_nt));
+        launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, w, w, w, w, dx, T, nullptr, 0, nullptr,
+                                                     at<Tile>(c, o_t), at<int32_t>(c, o_nt), T, 0, K, N, 1, dy, T,
+                                                     c->d_err),
+                                      m->bits, c->sms, c->stream);
+        if (launch_check(error, capacity)) return -1;
+        CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+        if (dev_io) CK(cudaEventRecord(c->ev_stop, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        if (*c->h_err) {
+            set_error(error, capacity, "%s", device_error_text(*c->h_err));
+            return -1;
+        }
+        if (!dev_io) {
+            CK(cudaMemcpyAsync(y, dy, (size_t)T * N * 2, cudaMemcpyDeviceToHost, c->stream));
+            CK(cudaEventRecord(c->ev_stop, c->stream));
+            CK(cudaStreamSynchronize(c->stream));
+        }
+        float t = 0;
+        CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
+        if (ms) *ms = t;
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return 0;
+}
+
 // ============================================================================ Part 2
 
 API void *di_moe_layer_create(void *ctx, void *router, void *gate, void *up, void *down, void *shared_gate,
@@ -1289,7 +1433,8 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
         set_error(error, capacity, "MoE layer must belong to this device.");
         return -1;
     }
-    if (!x || !y || tokens < 1 || tokens > 65536 || (flags & ~15) ||
+    if (!x || !y || tokens < 1 || tokens > 65536 ||
+        (flags & ~(DI_MOE_DEVICE_IO | DI_MOE_FORCE_ROUTES | DI_MOE_PATH_GEMV | DI_MOE_PATH_GROUPED | DI_MOE_ROUTER_EXACT)) ||
         ((flags & DI_MOE_PATH_GEMV) && (flags & DI_MOE_PATH_GROUPED)) || (forced && !ids) ||
         ((flags & DI_MOE_PATH_GEMV) && tokens > kDecodeMaxTokens)) {
         set_error(error, capacity, "Invalid MoE block arguments");
@@ -1306,6 +1451,10 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
                 set_error(error, capacity, "Expert ID out of bounds");
                 return -1;
             }
+    if (dev_io && !device_pointers_ok(c->device, {x, y, ids, probs})) {
+        set_error(error, capacity, "With DI_MOE_DEVICE_IO, x, y, ids and probs must be device memory of the context's GPU");
+        return -1;
+    }
     const int T = tokens, D = L->D;
     const bool gemv = pick_gemv(T, flags);
     if (gemv && !forced && (size_t)T * D * 2 > (size_t)kDecodeSmemMax) {
@@ -1320,8 +1469,10 @@ API int di_moe_block(void *ctx, void *layer, const uint16_t *x, int tokens, uint
     DeviceGuard dg(c->device);
     try {
         for (int i = 0; i < 8; ++i) sync_matrix(L->m[i]);
+        c->last_routes_T = 0;
         Carve cv;
         BlockBuffers b{};
+        b.router_exact = (flags & DI_MOE_ROUTER_EXACT) != 0;
         size_t o_ids_io = 0, o_probs_io = 0;
         if (!dev_io) {
             o_ids_io = cv.take<int32_t>((size_t)T * 8);
@@ -1385,7 +1536,7 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
                      uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error, int capacity) {
     if (!live_context(ctx) || !layers || n_layers < 1 || n_layers > 1024 || !norms || !x || tokens < 1 ||
         tokens > 65536 || !(eps > 0.0f) ||
-        (flags & ~(DI_MOE_DEVICE_IO | DI_MOE_PATH_GEMV | DI_MOE_PATH_GROUPED | DI_MOE_PROFILE)) ||
+        (flags & ~(DI_MOE_DEVICE_IO | DI_MOE_PATH_GEMV | DI_MOE_PATH_GROUPED | DI_MOE_PROFILE | DI_MOE_ROUTER_EXACT)) ||
         ((flags & DI_MOE_PATH_GEMV) && (flags & DI_MOE_PATH_GROUPED)) ||
         ((flags & DI_MOE_PATH_GEMV) && tokens > kDecodeMaxTokens)) {
         set_error(error, capacity, "Invalid MoE stack arguments");
@@ -1411,6 +1562,11 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
             }
     }
     const bool dev_io = flags & DI_MOE_DEVICE_IO, profile = flags & DI_MOE_PROFILE;
+    if (dev_io && !device_pointers_ok(c->device, {x, norms, h_trace, ids_trace})) {
+        set_error(error, capacity,
+                  "With DI_MOE_DEVICE_IO, x, norms and the traces must be device memory of the context's GPU");
+        return -1;
+    }
     const int T = tokens;
     const bool gemv = pick_gemv(T, flags);
     if (gemv && (size_t)T * D * 2 > (size_t)kDecodeSmemMax) {
@@ -1444,7 +1600,9 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
             Emax = std::max(Emax, static_cast<Layer *>(layers[l])->E);
             Imax = std::max(Imax, static_cast<Layer *>(layers[l])->I);
         }
+        c->last_routes_T = 0;
         BlockBuffers b{};
+        b.router_exact = (flags & DI_MOE_ROUTER_EXACT) != 0;
         // size the block buffers for the widest layer (layers of one stack share E and I in practice)
         Layer probe = *static_cast<Layer *>(layers[0]);
         probe.E = Emax;
@@ -1595,6 +1753,37 @@ API int di_moe_last_profile(void *ctx, double *stage_ms, int n) {
     return k;
 }
 
+
+API int di_moe_last_routes(void *ctx, int32_t *perm_route, int32_t *seg_offsets, int32_t *seg_counts, int max_routes,
+                           char *error, int capacity) {
+    if (!live_context(ctx) || !perm_route || !seg_offsets || !seg_counts) {
+        set_error(error, capacity, "Invalid route readback arguments");
+        return -1;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    if (c->last_routes_T < 1) {
+        set_error(error, capacity, "The last call on this context built no expert-grouped permutation");
+        return -1;
+    }
+    const int n = 8 * c->last_routes_T;
+    if (max_routes < n) {
+        set_error(error, capacity, "The permutation holds %d routes; the buffer takes %d", n, max_routes);
+        return -1;
+    }
+    DeviceGuard dg(c->device);
+    try {
+        CK(cudaMemcpyAsync(perm_route, c->last_perm, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaMemcpyAsync(seg_offsets, c->last_seg_off, (size_t)(c->last_routes_E + 1) * 4, cudaMemcpyDeviceToHost,
+                           c->stream));
+        CK(cudaMemcpyAsync(seg_counts, c->last_seg_count, (size_t)(c->last_routes_E + 1) * 4, cudaMemcpyDeviceToHost,
+                           c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+    } catch (const CudaFail &f) {
+        set_error(error, capacity, "%s", f.what.c_str());
+        return -1;
+    }
+    return n;
+}
 
 // ============================================================================ Part 3: expert parallelism
 
@@ -1877,7 +2066,8 @@ API void *di_moe_ep_layer_create(void *ep_, void *router, void *gate, void *up, 
 }
 
 API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int n_layers, float eps, float *x,
-                        int tokens, int flags, double *ms, char *error, int capacity) {
+                        int tokens, uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error,
+                        int capacity) {
     if (!live_ep(ep_) || !layers || n_layers < 1 || n_layers > 1024 || !norms || !x || tokens < 1 ||
         tokens > 65536 || !(eps > 0.0f) || (flags & ~DI_MOE_DEVICE_IO)) {
         set_error(error, capacity, "Invalid expert-parallel stack arguments");
@@ -1914,6 +2104,11 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         }
     }
     const bool dev_io = flags & DI_MOE_DEVICE_IO;
+    if (dev_io && !device_pointers_ok(c->device, {x, norms, h_trace, ids_trace})) {
+        set_error(error, capacity,
+                  "With DI_MOE_DEVICE_IO, x, norms and the traces must be device memory of the context's GPU");
+        return -1;
+    }
     if (ep->broken) {
         set_error(error, capacity, "Expert-parallel group failed in an earlier call; create it again");
         return -1;
@@ -1961,7 +2156,11 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         const size_t o_xp = cv.take<uint16_t>((size_t)RC * 8 * D + 8);
         const size_t o_wn = cv.take<float>(2 * (size_t)E), o_rt = cv.take<Tile>((size_t)(T + 255) / 256 + 1);
         const size_t o_rnt = cv.take<int32_t>(1), o_wf = cv.take<float>((size_t)E * D);
+        const size_t o_ht = (!dev_io && h_trace) ? cv.take<uint16_t>((size_t)n_layers * T * D) : 0;
+        const size_t o_it = (!dev_io && ids_trace) ? cv.take<int32_t>((size_t)n_layers * T * 8) : 0;
         ensure_workspace(c, cv.off + 256);
+        uint16_t *dht = dev_io ? h_trace : (h_trace ? at<uint16_t>(c, o_ht) : nullptr);
+        int32_t *dit = dev_io ? ids_trace : (ids_trace ? at<int32_t>(c, o_it) : nullptr);
         float *dx = dev_io ? x : at<float>(c, o_x);
         const float *dn = dev_io ? norms : at<float>(c, o_n);
         uint16_t *h = at<uint16_t>(c, o_h), *act = at<uint16_t>(c, o_act), *y = at<uint16_t>(c, o_y);
@@ -2004,6 +2203,10 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                 topk_count_kernel<<<nb_l, topk::WARPS * 32, 0, st>>>(logits, T, E, h, D, SR, nullptr, ids, probs, gate,
                                                                       bc, c->d_err);
             }
+            if (dht)
+                CK(cudaMemcpyAsync(dht + (size_t)l * T * D, h, (size_t)T * D * 2, cudaMemcpyDeviceToDevice, st));
+            if (dit)
+                CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, st));
             // 2. one row per (token, destination rank), written into the destinations over NVLink
             ep_layout_kernel<<<1, 1024, 0, st>>>(ids, T, El, G, sidx, sc, so);
             ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
@@ -2049,6 +2252,10 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         }
         if (!dev_io) {
             CK(cudaMemcpyAsync(x, dx, (size_t)T * D * 4, cudaMemcpyDeviceToHost, st));
+            if (h_trace)
+                CK(cudaMemcpyAsync(h_trace, dht, (size_t)n_layers * T * D * 2, cudaMemcpyDeviceToHost, st));
+            if (ids_trace)
+                CK(cudaMemcpyAsync(ids_trace, dit, (size_t)n_layers * T * 8 * 4, cudaMemcpyDeviceToHost, st));
             CK(cudaEventRecord(c->ev_stop, st));
             CK(cudaStreamSynchronize(st));
         }
@@ -2101,6 +2308,15 @@ API int di_moe_block_static(void *ctx, void *layer, const uint16_t *x, int token
         }
     if (c->device < 0 || c->device >= kMaxStaticDevices) {
         set_error(error, capacity, "Device ordinal %d is outside the allocation-free entry's table", c->device);
+        return -1;
+    }
+    if (!device_pointers_ok(c->device, {x, y, ids, probs})) {
+        set_error(error, capacity, "Allocation-free MoE block: x, y, ids and probs must be device memory of the context's GPU");
+        return -1;
+    }
+    // the route kernel stages the T input rows in shared memory (the same limit di_moe_block applies)
+    if ((size_t)tokens * L->D * 2 > (size_t)kDecodeSmemMax) {
+        set_error(error, capacity, "Decode path supports T*D <= %d; use the grouped path", kDecodeSmemMax / 2);
         return -1;
     }
     const int T = tokens, E = L->E, I = L->I;

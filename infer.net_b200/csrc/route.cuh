@@ -678,16 +678,20 @@ __global__ void combine_kernel(const uint16_t *__restrict__ yp, const int32_t *_
 // The routing ids must be those of the canonical f32 logits, which the tensor cores cannot
 // produce. But they can bound them. Approximate logits a[t, e] come from the grouped GEMM (DOWN
 // mode, one "expert" = the router matrix, bf16 output): its weights are W' = bf16(W), W = fma(q,
-// s, b) as the canonical order computes them, its products are exact and its f32 accumulation
-// over K <= 2048 errs by far less than 2^-13 sum|W x|. With r_e = W'_e - W_e (known from the
-// weights),
-//   |a[t,e] - logit[t,e]| <= ||r_e|| ||x_t|| + 2^-13 ||W_e|| ||x_t|| + 2^-8 |a[t,e]|  =: eps[t,e]
-// (Cauchy-Schwarz; the last term covers the bf16 output rounding, 2^-9 |A|, twice over; the
-// canonical order's own f32 error is below 2^-17 ||W|| ||x||). An expert can be among the true
-// top-8 only if a + eps >= L8, the 8th largest a - eps. Those candidates (about 10 of 256) are
-// recomputed in the canonical order and the top-8 is selected from the exact values, so ids,
-// ties and probabilities equal the all-exact router's.
-constexpr float kRouterAccumRel = 0x1p-13f;
+// s, b) as the canonical order computes them, and its bf16 x bf16 products are exact in f32. With
+// r_e = W'_e - W_e (known from the weights),
+//   |a[t,e] - logit[t,e]| <= ||r_e|| ||x_t|| + 2^-12 ||W_e|| ||x_t|| + 2^-8 |a[t,e]|  =: eps[t,e]
+// (Cauchy-Schwarz for the weight rounding). 2^-12 = K * 2^-23 for K = 2048 is the worst case of
+// adding the K products one at a time with truncation (an error below one f32 ulp, 2^-23
+// relative, per addition) -- no rounding mode or internal order of the MMA accumulation is
+// assumed. Any blocked order (K = 16 per instruction, 128 instruction results added into TMEM)
+// errs far less, and the margin absorbs the canonical order's own f32 error (< 70 roundings to
+// nearest per lane chain and butterfly, 2^-17.8 relative). The last term covers the bf16 output
+// rounding, 2^-9 |A|, twice over. An expert can be among the true top-8 only if a + eps >= L8,
+// the 8th largest a - eps. Those candidates (about 12 of 256) are recomputed in the canonical
+// order and the top-8 is selected from the exact values, so ids, ties and probabilities equal
+// the all-exact router's.
+constexpr float kRouterAccumRel = 0x1p-12f;
 constexpr float kRouterOutRel = 0x1p-8f;
 constexpr float kNormMargin = 1.0f + 0x1p-10f;  // f32 rounding of the norms themselves
 constexpr int kRouterMaxCand = 64;             // above this a token falls back to all experts

@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdeepinfer_cuda.so")
 CSRC = os.path.join(HERE, "csrc")
 
-DEVICE_IO, FORCE_ROUTES, PATH_GEMV, PATH_GROUPED, PROFILE = 1, 2, 4, 8, 16
+DEVICE_IO, FORCE_ROUTES, PATH_GEMV, PATH_GROUPED, PROFILE, ROUTER_EXACT = 1, 2, 4, 8, 16, 32
 STAGES = ("router", "top8", "scan", "scatter", "gate_up", "down", "combine", "rmsnorm")
 
 _lib = None
@@ -54,6 +54,8 @@ SIGNATURES = {
     "di_quant_experts": (C.c_int, [C.c_void_p] * 5 + [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                                       C.c_void_p, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
     "di_quant_embedding": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    "di_quant_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                C.POINTER(C.c_double), C.c_char_p, C.c_int]),
     "di_quant_matrix_device_buffer": (C.c_void_p, [C.c_void_p, C.c_int]),
     "di_quant_matrix_upload": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_uint64, C.c_char_p, C.c_int]),
     "di_quant_matrix_generate": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_float, C.c_int, C.c_char_p,
@@ -66,12 +68,13 @@ SIGNATURES = {
     "di_moe_stack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_int,
                                C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
     "di_moe_last_profile": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.c_int]),
+    "di_moe_last_routes": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_char_p, C.c_int]),
     "di_moe_ep_unique_id": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "di_moe_ep_create": (C.c_void_p, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.c_int]),
     "di_moe_ep_destroy": (None, [C.c_void_p]),
     "di_moe_ep_layer_create": (C.c_void_p, [C.c_void_p] * 9 + [C.c_char_p, C.c_int]),
     "di_moe_ep_stack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_int,
-                                  C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
+                                  C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
     "di_moe_block_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
 }
@@ -170,6 +173,17 @@ class Context:
             raise DeepInferError(err.value.decode())
         return ms.value
 
+    def last_routes(self, tokens: int, experts: int):
+        """(perm_route [8T], seg_offsets [E+1], seg_counts [E+1]) of the last grouped-path block."""
+        perm = np.zeros(8 * tokens, np.int32)
+        off = np.zeros(experts + 1, np.int32)
+        cnt = np.zeros(experts + 1, np.int32)
+        err = C.create_string_buffer(2048)
+        n = lib().di_moe_last_routes(self.h, _p(perm), _p(off), _p(cnt), perm.size, err, 2048)
+        if n < 0:
+            raise DeepInferError(err.value.decode())
+        return perm[:n], off, cnt
+
     def last_profile(self):
         out = (C.c_double * len(STAGES))()
         n = lib().di_moe_last_profile(self.h, out, len(STAGES))
@@ -230,6 +244,17 @@ class Matrix:
         if rc:
             raise DeepInferError(err.value.decode())
         return ms.value
+
+    def gemm(self, x, expert: int = 0, flags: int = 0, y=None):
+        """Dense projection of a bf16 token batch: returns (y bf16 [T, rows], ms)."""
+        T = (x.numel() if hasattr(x, "numel") else x.size) // self.cols
+        if y is None:
+            y = np.zeros((T, self.rows), np.uint16)
+        ms = C.c_double()
+        err = C.create_string_buffer(2048)
+        if lib().di_quant_gemm(self.ctx.h, self.h, expert, _p(x), T, _p(y), flags, C.byref(ms), err, 2048):
+            raise DeepInferError(err.value.decode())
+        return y, ms.value
 
     def embedding(self, token):
         out = np.zeros(self.cols, np.float32)
@@ -340,12 +365,12 @@ class ExpertParallel:
         obj.ctx, obj.h, obj.mats = self.ctx, h, mats
         return obj
 
-    def stack(self, layers, norms, x, tokens, eps=1e-6, flags=0):
+    def stack(self, layers, norms, x, tokens, eps=1e-6, flags=0, h_trace=None, ids_trace=None):
         arr = (C.c_void_p * len(layers))(*[l.h for l in layers])
         ms = C.c_double()
         err = C.create_string_buffer(2048)
         rc = lib().di_moe_ep_stack(self.h, C.cast(arr, C.c_void_p), _p(norms), len(layers), eps, _p(x), tokens,
-                                   flags, C.byref(ms), err, 2048)
+                                   _p(h_trace), _p(ids_trace), flags, C.byref(ms), err, 2048)
         if rc:
             raise DeepInferError(err.value.decode())
         return ms.value
