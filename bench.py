@@ -9,8 +9,11 @@ The batch-1 decode of configs[1] (same 40 layers, one token) is reported in "dec
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
---impl reference times the CPU restatement of the reference's C# block arithmetic
-(oracle/, Qwen36Model.cs:218-262 semantics) on the host cores with the same metric.
+--impl reference times the reference's CPU path for this block, restated in C in its own loop
+shape (oracle/cpu_block.c: Qwen36Model.Moe over CpuMatrix.Multiply's Vector<float> row dots,
+src/DeepInfer.Backends/Models/Qwen36Model.cs:218-262, Compute/MatVec.cs:44-54; .NET is not on the
+machine), on all host cores with the same metric: each step is BASELINE configs[0] (one full-size
+8-bit layer, 512 tokens) timed whole; the per-token path makes the 8K x 40-layer time 16 x 40 of it.
 """
 from __future__ import annotations
 
@@ -44,19 +47,6 @@ def peaks():
         return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
                 "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
-
-
-def profiled_traffic():
-    """DRAM bytes (read + write) per launch of the 8K-token gate/up kernel, from the committed ncu
-    summary (profiles/grouped_gemm_gate_up_8k.md); None when absent."""
-    import re
-    path = os.path.join(ROOT, "profiles", "grouped_gemm_gate_up_8k.md")
-    try:
-        with open(path) as f:
-            m = re.search(r"traffic per launch \(read \+ write\) \| ([0-9.]+) MB", f.read())
-        return float(m.group(1)) * 1e6 if m else None
-    except OSError:
-        return None
 
 
 class ClockSampler:
@@ -101,24 +91,85 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------------- reference arm
 
-_CPU_LAYER = []
+_CPU = {}
 
 
-def cpu_sample(tokens: int, threads: int):
-    """Time the oracle port of the reference block on `tokens` tokens of one full-size layer
-    (the layer's weights are generated once and kept for later samples)."""
+def _cpu_oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    if not _CPU_LAYER:
-        _CPU_LAYER.append(O.Layer(SEED, layer=0, bits=8))
-    L = _CPU_LAYER[0]
+    return O
+
+
+def cpu_layers(n: int):
+    """n full-size 8-bit layers of the benchmark's weights on the host, prepared for the CPU path
+    (generated once per process and kept)."""
+    O = _cpu_oracle()
+    layers = _CPU.setdefault("layers", [])
+    while len(layers) < n:
+        layers.append(O.CpuLayer(O.Layer(SEED, layer=len(layers), bits=8)))
+    return layers[:n]
+
+
+def cpu_cfg0(threads: int, tokens: int = 512):
+    """Seconds for one pass of BASELINE configs[0] (`tokens` tokens through one full-size 8-bit
+    layer) on the CPU path with `threads` threads."""
+    O = _cpu_oracle()
+    cl = cpu_layers(1)[0]
     x = O.gen_bf16(SEED, O.ACT_STREAM, tokens * D).reshape(tokens, D)
-    O.moe_block(L, x[:4], O.MODE_F32, threads=threads)  # warm
     t0 = time.perf_counter()
-    rc, *_ = O.moe_block(L, x, O.MODE_F32, threads=threads)
+    rc, *_ = O.cpu_block(cl, x, threads)
     dt = time.perf_counter() - t0
     assert rc == 0
     return dt
+
+
+def cpu_decode_us(threads: int, layers: int, steps: int = 5):
+    """Microseconds per token of batch-1 decode through `layers` distinct full-size layers."""
+    O = _cpu_oracle()
+    import numpy as np
+    cls = cpu_layers(layers)
+    norms = np.ones((layers, D), np.float32)
+    x0 = O.bf16_to_f32(O.gen_bf16(SEED, O.ACT_STREAM + 1, D)).reshape(1, D)
+    O.cpu_stack(cls, norms, x0, 1e-6, threads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        rc, _, _ = O.cpu_stack(cls, norms, x0, 1e-6, threads)
+        assert rc == 0
+    return (time.perf_counter() - t0) / steps * 1e6
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_baseline_block(threads: int, steps: int, warmup: int, decode_layers: int = 8):
+    """The CPU baseline: configs[0] timed whole on all cores (mean of `steps` after `warmup`), the
+    prefill metric derived from it, the same on one core (64 tokens), and batch-1 decode."""
+    O = _cpu_oracle()
+    for _ in range(warmup):
+        cpu_cfg0(threads)
+    t = sum(cpu_cfg0(threads) for _ in range(steps)) / steps
+    t1 = cpu_cfg0(1, 64)
+    dec = cpu_decode_us(threads, decode_layers)
+    return t, {
+        "value": 512 / (t * LAYERS), "unit": "tokens/s", "cores": threads, "kind": "port",
+        "isa": O.cpu_isa(), "cpu": cpu_model(),
+        "sample": ("configs[0] timed whole per step: 512 tokens through one full-size 8-bit layer "
+                   f"({t * 1e3:.1f} ms on {threads} threads); the reference's per-token path makes the "
+                   "8192-token x 40-layer step 16 x 40 such passes"),
+        "single_core": {"value": 64 / (t1 * LAYERS), "unit": "tokens/s", "cores": 1,
+                        "sample": f"64 tokens through one layer in {t1 * 1e3:.1f} ms on one core, x40 layers"},
+        "decode": {"us_per_token": dec / decode_layers * LAYERS, "cores": threads,
+                   "sample": f"batch-1 decode through {decode_layers} distinct layers "
+                             f"({dec:.0f} us), scaled to 40 layers"},
+    }
 
 
 def run_reference(args):
@@ -126,20 +177,15 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    tokens = 64
-    for _ in range(args.warmup):
-        cpu_sample(tokens, threads)
-    times = [cpu_sample(tokens, threads) for _ in range(args.steps)]
-    t = sum(times) / len(times)
-    value = tokens / (t * LAYERS)  # tokens/s through 40 layers, extrapolated from one layer
-    sample = f"{tokens} tokens x 1 of 40 layers per step (full geometry, 8-bit), extrapolated x40"
+    t, cpu = cpu_baseline_block(threads, args.steps, args.warmup, args.cpu_decode_layers)
+    value = cpu["value"]
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "prefill 8192 tokens x 40 MoE layers (CPU sample)", "tokens": TOKENS, "layers": LAYERS,
-                   "bits": 8, "experts": E, "top_k": 8},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "config": {"workload": "prefill 8192 tokens x 40 MoE layers, 8-bit g64 (CPU: configs[0] per step)",
+                   "tokens": TOKENS, "layers": LAYERS, "bits": 8, "experts": E, "top_k": 8},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -223,14 +269,7 @@ def run_ours(args):
     achieved = gu_flops / (gate_up_ms * 1e-3) / 1e12 if gate_up_ms > 0 else None
     cpu = None
     if rank == 0 and not args.no_cpu:
-        threads = os.cpu_count() or 1
-        tok = 64
-        t = cpu_sample(tok, threads)
-        t1 = cpu_sample(8, 1)  # the same port on one core (a smaller sample)
-        cpu = {"value": tok / (t * LAYERS), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{tok} tokens x 1 of 40 layers (full geometry, 8-bit) on the oracle port, extrapolated x40",
-               "single_core": {"value": 8 / (t1 * LAYERS), "unit": "tokens/s", "cores": 1,
-                               "sample": "8 tokens x 1 of 40 layers on one core, extrapolated x40"}}
+        _, cpu = cpu_baseline_block(os.cpu_count() or 1, 2, 1, args.cpu_decode_layers)
     total_flops = FLOPS_TOKEN_LAYER * TOKENS * LAYERS
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -243,8 +282,7 @@ def run_ours(args):
         "roofline": {"kernel": "grouped_gemm<gate_up,8bit>", "bound": "tensor", "achieved": achieved,
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
-                     "traffic": profiled_traffic() if TOKENS == 8192 else None,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 8K-token launch",
+                     "traffic": None,
                      "peak_source": pk["source"] + " sustained bf16"},
         "stage_ms_per_step": {k: v / args.steps for k, v in stage_tot.items()},
         "cpu_baseline": cpu,
@@ -385,6 +423,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-decode-layers", type=int, default=8,
+                    help="distinct layers the CPU decode leg runs (its time is scaled to 40 layers)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling case: fewer stacked layers")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="profiling case: fewer prefill tokens")
     ap.add_argument("--only-prefill", action="store_true", help="profiling case: skip the e2e and decode legs")

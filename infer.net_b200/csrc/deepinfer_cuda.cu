@@ -2272,6 +2272,19 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
     return 0;
 }
 
+#ifdef DI_GG_TIMING
+// Profiling build only (-DDI_GG_TIMING): the grouped GEMMs' per-role cycle counters
+// [4 kinds][256 CTAs][gg::T_COUNT], copied to out and cleared when reset != 0.
+API int di_debug_gg_timing(unsigned long long *out, int reset) {
+    if (cudaMemcpyFromSymbol(out, gg::g_gg_timing, sizeof(gg::g_gg_timing)) != cudaSuccess) return -1;
+    if (reset) {
+        static unsigned long long zero[4 * 256 * gg::T_COUNT];
+        if (cudaMemcpyToSymbol(gg::g_gg_timing, zero, sizeof(zero)) != cudaSuccess) return -1;
+    }
+    return 0;
+}
+#endif
+
 // ============================================================================ allocation-free block
 
 namespace {

@@ -154,6 +154,32 @@ __device__ __forceinline__ void a_row(int m, int &mat, int &r) {
 template <int BITS>
 __device__ __forceinline__ int code_x(int kb) { return BITS == 8 ? kb * 64 : ((kb * 40) & ~15); }
 
+// Per-role cycle counters, compiled in only with -DDI_GG_TIMING (a profiling build; read by
+// di_debug_gg_timing): for each kernel kind (0 gate_up, 1 down, 3 the router's approximate
+// logits) and CTA, the SM cycles lane 0 of one warp of each role spends in each barrier wait and
+// in its whole loop.
+enum GgTimer : int {
+    T_KERNEL = 0,
+    T_DQ_CODES, T_DQ_EMPTY, T_DQ_SCALES, T_DQ_LOOP,  // dequantiser warp 8
+    T_CP_EMPTY, T_CP_SCALE_EMPTY, T_CP_LOOP,         // code + scale producer
+    T_BP_EMPTY, T_BP_LOOP,                           // B producer
+    T_MMA_B, T_MMA_A, T_MMA_ACC, T_MMA_LOOP,         // MMA issue
+    T_EPI_WAIT, T_EPI_LOOP,                          // epilogue warp 0
+    T_MMA_ISSUE, T_MMA_COMMIT,                       // MMA issue: the MMA instructions, the stage commit
+    T_COUNT = 18
+};
+#ifdef DI_GG_TIMING
+__device__ unsigned long long g_gg_timing[4][256][T_COUNT];
+__device__ __forceinline__ void gg_time(int kind, int slot, long long t0) {
+    if (lane_id() == 0 && blockIdx.x < 256)
+        atomicAdd(&g_gg_timing[kind][blockIdx.x][slot], (unsigned long long)(clock64() - t0));
+}
+__device__ __forceinline__ long long gg_now() { return clock64(); }
+#else
+__device__ __forceinline__ void gg_time(int, int, long long) {}
+__device__ __forceinline__ long long gg_now() { return 0; }
+#endif
+
 // Accumulator slots alternate between units; every role derives the same assignment.
 struct SlotPlan {
     int next = 0;
@@ -193,6 +219,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     const int nk = p.K / BK;  // K is a multiple of 64
     const int gpr = p.K / 64;
     const int n_units = (*p.n_tiles) * RB;
+    const int tkind = MODE + (p.E == 1 ? 2 : 0);  // timing build: gate_up, down, router logits
+    const long long t_kernel = gg_now();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -237,6 +265,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         // group g takes the stages of the flat index with it % 2 == g (each stage is one
         // quantisation group); thread m of the group converts A row m.
         const int g = (warp - 8) >> 2, m = threadIdx.x - 256 - 128 * g;  // 0..127
+        const bool timed = warp == 8;
+        const long long t_loop = gg_now();
         int mat, r;
         a_row<MODE>(m, mat, r);
         const bool fast_scales = (gpr & 7) == 0;  // rows of scales are 16-byte aligned
@@ -244,7 +274,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         for (int ul = 0, u = blockIdx.x; u < n_units && ok; ++ul, u += gridDim.x, it0 += nk) {
             const int rb = u % RB, sb = ul & 1;
             const bool live = rb * RPU + r < p.rows;
+            const long long t_s = gg_now();
             if (!mbar_wait(&sfull[sb], (ul >> 1) & 1, p.err, kErrTimeout)) { ok = false; break; }
+            if (timed) gg_time(tkind, T_DQ_SCALES, t_s);
             const uint16_t *s_row =
                 reinterpret_cast<const uint16_t *>(scale_buf + sb * kScaleBuf) + ((mat * 2) * RPU + r) * gpr;
             const uint16_t *b_row = s_row + RPU * gpr;
@@ -268,7 +300,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                     bi = bf16_bits_to_f32(b_row[kb]);
                 }
                 const int it = it0 + kb, s = it % STAGES, cs = it % CSTAGES;
+                const long long t_c = gg_now();
                 if (!mbar_wait(&cfull[cs], (it / CSTAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
+                if (timed) gg_time(tkind, T_DQ_CODES, t_c);
                 const uint8_t *crow = c_tile(cs) + mat * (RPU * 64);
                 uint4 cw[4];
 #pragma unroll
@@ -293,7 +327,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[i] = 0;
                 // the A tile is free once the MMA of the stage's previous use has completed
+                const long long t_e = gg_now();
                 if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
+                if (timed) gg_time(tkind, T_DQ_EMPTY, t_e);
                 uint8_t *t = a_tile(s);
 #pragma unroll
                 for (int c = 0; c < 8; ++c)
@@ -306,9 +342,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[sb]);
         }
+        if (timed) gg_time(tkind, T_DQ_LOOP, t_loop);
     } else if (warp == 5) {
         // ---------------------------------------------------------------- code and scale producer
         int it = 0, ul = 0;
+        const long long t_loop = gg_now();
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ul) {
             const Tile tl = p.tiles[u / RB];
             const int rb = u % RB, sb = ul & 1;
@@ -316,7 +354,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             const int expert = shared ? 0 : tl.seg;
             // scales and biases of the unit's rows
             if (lane == 0) {
+                const long long t_s = gg_now();
                 ok = mbar_wait(&sempty[sb], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeout);
+                gg_time(tkind, T_CP_SCALE_EMPTY, t_s);
                 if (ok) {
                     const int nrows = min(RPU, p.rows - rb * RPU);
                     const uint32_t bytes = (uint32_t)(nrows * gpr * 2);
@@ -336,7 +376,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             for (int kb = 0; kb < nk; ++kb, ++it) {
                 const int cs = it % CSTAGES;
                 if (lane == 0) {
+                    const long long t_c = gg_now();
                     ok = mbar_wait(&cempty[cs], ((it / CSTAGES) & 1) ^ 1, p.err, kErrTimeout);
+                    gg_time(tkind, T_CP_EMPTY, t_c);
                     if (ok) mbar_arrive_expect_tx(&cfull[cs], kCode);
                 }
                 ok = __shfl_sync(kFull, ok, 0);
@@ -346,6 +388,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                                 &cfull[cs]);
             }
         }
+        gg_time(tkind, T_CP_LOOP, t_loop);
         if (!ok && lane == 0) {
             // copies still in flight must land before the CTA's shared memory is released
             for (int k = max(0, it - CSTAGES); k < it; ++k)
@@ -355,6 +398,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     } else if (warp == 6) {
         // ---------------------------------------------------------------- B producer
         int it = 0;
+        const long long t_loop = gg_now();
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const Tile tl = p.tiles[u / RB];
             const bool shared = tl.seg >= p.E;
@@ -369,7 +413,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             for (int kb = 0; kb < nk; ++kb, ++it) {
                 const int s = it % STAGES;
                 if (lane == 0) {
+                    const long long t_e = gg_now();
                     ok = mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.err, kErrTimeout);
+                    gg_time(tkind, T_BP_EMPTY, t_e);
                     if (ok) mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u);
                 }
                 ok = __shfl_sync(kFull, ok, 0);
@@ -377,6 +423,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 if (box_mine) tma_load_2d(b_tile(s) + box_off * 128, bm, kb * BK, row0, &bfull[s]);
             }
         }
+        gg_time(tkind, T_BP_LOOP, t_loop);
         if (!ok && lane == 0)
             for (int k = max(0, it - STAGES); k < it; ++k)
                 mbar_wait(&bfull[k % STAGES], (k / STAGES) & 1, p.err, kErrTimeout);
@@ -385,32 +432,48 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         if (lane == 0) {
             int it = 0;
             SlotPlan plan;
+            const long long t_loop = gg_now();
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const Tile tl = p.tiles[u / RB];
                 const int N = round16(tl.n);
                 uint32_t phase;
                 const int slot = plan.take(phase);
+                const long long t_a = gg_now();
                 if (!mbar_wait(&acce[slot], (phase & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
+                gg_time(tkind, T_MMA_ACC, t_a);
                 tc_fence_after();
                 const uint32_t d = tmem + slot * 256;
                 const uint32_t id = idesc_bf16_f32(BM, N);
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&bfull[s], ph, p.err, kErrTimeout) || !mbar_wait(&full[s], ph, p.err, kErrTimeout)) {
+                    const long long t_b = gg_now();
+                    if (!mbar_wait(&bfull[s], ph, p.err, kErrTimeout)) {
                         ok = false;
                         break;
                     }
+                    const long long t_f = gg_now();
+                    gg_time(tkind, T_MMA_B, t_b);
+                    if (!mbar_wait(&full[s], ph, p.err, kErrTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    gg_time(tkind, T_MMA_A, t_f);
                     tc_fence_after();
                     const uint64_t adesc = smem_desc_sw128(smem_u32(a_tile(s)));
                     const uint64_t bdesc = smem_desc_sw128(smem_u32(b_tile(s)));
+                    const long long t_i = gg_now();
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) tc_mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, id, (kb | k) != 0);
+                    const long long t_c = gg_now();
+                    gg_time(tkind, T_MMA_ISSUE, t_i);
                     tc_commit(&empty[s]);
+                    gg_time(tkind, T_MMA_COMMIT, t_c);
                 }
                 if (!ok) break;
                 tc_commit(&accf[slot]);
             }
+            gg_time(tkind, T_MMA_LOOP, t_loop);
         }
         __syncwarp();
     } else if (warp < 4) {
@@ -419,13 +482,16 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         uint8_t *so = stage_out + q * 2 * 16 * 64;
         int chunk_no = 0;  // DOWN: staging buffer of a chunk = chunk_no & 1
         SlotPlan plan;
+        const long long t_loop = gg_now();
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const Tile tl = p.tiles[u / RB];
             const int rb = u % RB;
             const int N = round16(tl.n);
             uint32_t phase;
             const int slot = plan.take(phase);
+            const long long t_w = gg_now();
             if (!mbar_wait(&accf[slot], phase & 1, p.err, kErrTimeout)) { ok = false; break; }
+            if (q == 0) gg_time(tkind, T_EPI_WAIT, t_w);
             tc_fence_after();
             const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + slot * 256;
             // software pipeline: the TMEM columns of chunk c + 16 are requested while chunk c is
@@ -493,11 +559,13 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[slot]);
         }
+        if (q == 0) gg_time(tkind, T_EPI_LOOP, t_loop);
         if constexpr (MODE == MODE_DOWN)
             if (lane == 0) bulk_wait<0>();  // tensor stores complete before the CTA exits
     }
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) gg_time(tkind, T_KERNEL, t_kernel);
     if (warp == 4) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);

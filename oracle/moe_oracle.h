@@ -103,6 +103,18 @@ int oc_moe_stack(const oc_layer *layers, const float *norms, int n_layers, float
 /* RMSNorm of one row rounded to bf16 (gpu_graph.mm:48-61 arithmetic, single accumulator) */
 void oc_rmsnorm_bf16(const float *x, const float *w, int D, float eps, uint16_t *out);
 
+/* CPU baseline in the reference's CPU loop shape (cpu_block.c): one Vector<float> accumulator per
+   GEMV row (CpuMatrix.Multiply, MatVec.cs:44-54) with the weights dequantised per 64-group, the
+   router in the canonical order (ids equal oc_moe_block's), SIMD width chosen at run time. */
+typedef struct oc_cpu_layer oc_cpu_layer;
+oc_cpu_layer *oc_cpu_prepare(const oc_layer *L);  /* keeps pointers into L's matrices */
+void oc_cpu_release(oc_cpu_layer *P);
+const char *oc_cpu_isa(void);                     /* "avx512", "avx2" or "scalar" */
+int oc_cpu_block(const oc_cpu_layer *P, const uint16_t *x, int T, float *out, int32_t *ids, float *probs,
+                 int threads);
+int oc_cpu_stack(const oc_cpu_layer *const *P, const float *norms, int n_layers, float eps, float *x, int T,
+                 int32_t *ids_out, int threads);
+
 #ifdef __cplusplus
 }
 #endif

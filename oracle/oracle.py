@@ -66,6 +66,11 @@ def lib():
             "oc_moe_block": (I, [P, P, I, I, P, P, P, P, P, I]),
             "oc_moe_stack": (I, [P, P, I, F, P, I, I, P, I]),
             "oc_rmsnorm_bf16": (None, [P, P, I, F, P]),
+            "oc_cpu_prepare": (P, [P]),
+            "oc_cpu_release": (None, [P]),
+            "oc_cpu_isa": (C.c_char_p, []),
+            "oc_cpu_block": (I, [P, P, I, P, P, P, I]),
+            "oc_cpu_stack": (I, [P, P, I, F, P, I, P, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -279,3 +284,51 @@ def tolerance_report(actual: np.ndarray, expected: np.ndarray):
     max_abs = float(np.max(np.abs(a - e))) if a.size else 0.0
     rel_l2 = float(np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30))
     return max_abs, rel_l2
+
+
+# ------------------------------------------------------------------ CPU baseline (reference loop shape)
+
+class CpuLayer:
+    """A layer prepared for the CPU baseline (cpu_block.c): router rows dequantised once, the
+    expert GEMVs in CpuMatrix's Vector<float> row-dot shape. Keeps the Layer alive."""
+
+    def __init__(self, layer: Layer):
+        self.layer = layer
+        self._lc = layer.c()
+        self.h = lib().oc_cpu_prepare(C.byref(self._lc))
+        if not self.h:
+            raise MemoryError("oc_cpu_prepare failed")
+
+    def close(self):
+        if self.h:
+            lib().oc_cpu_release(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def cpu_isa() -> str:
+    return lib().oc_cpu_isa().decode()
+
+
+def cpu_block(cl: CpuLayer, x_bf16: np.ndarray, threads: int = 0):
+    D = cl.layer.D
+    x = np.ascontiguousarray(x_bf16, np.uint16).reshape(-1, D)
+    T = x.shape[0]
+    out = np.zeros((T, D), np.float32)
+    ids = np.zeros((T, 8), np.int32)
+    probs = np.zeros((T, 8), np.float32)
+    rc = lib().oc_cpu_block(cl.h, ptr(x), T, ptr(out), ptr(ids), ptr(probs), threads)
+    return rc, out, ids, probs
+
+
+def cpu_stack(layers, norms: np.ndarray, x: np.ndarray, eps: float = 1e-6, threads: int = 0, trace: bool = False):
+    x = np.ascontiguousarray(x, np.float32).copy()
+    D = x.shape[-1]
+    T = x.size // D
+    arr = (C.c_void_p * len(layers))(*[l.h for l in layers])
+    norms = np.ascontiguousarray(norms, np.float32)
+    ids = np.zeros((len(layers), T, 8), np.int32) if trace else None
+    rc = lib().oc_cpu_stack(C.cast(arr, C.c_void_p), ptr(norms), len(layers), eps, ptr(x), T, ptr(ids), threads)
+    return rc, x, ids

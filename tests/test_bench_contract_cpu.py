@@ -12,7 +12,7 @@ sys.path.insert(0, ROOT)
 def _run(env_extra):
     env = dict(os.environ, **env_extra)
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
-                        "--warmup", "0"], capture_output=True, text=True, env=env, timeout=600)
+                        "--warmup", "0", "--cpu-decode-layers", "1"], capture_output=True, text=True, env=env, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     return [l for l in r.stdout.splitlines() if l.startswith("{")]
 
@@ -27,6 +27,8 @@ def test_reference_arm_prints_the_contract_line():
     assert d["value"] > 0 and d["ms_per_step"] > 0
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"] and cb["value"] == d["value"]
+    assert cb["isa"] in ("avx512", "avx2", "scalar") and cb["single_core"]["cores"] == 1
+    assert cb["decode"]["us_per_token"] > 0
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
