@@ -121,6 +121,22 @@ void di_moe_layer_destroy(void *layer);
 /* Optional per-expert logit bias (host f32[E]); NULL clears it. Used by the Zipf load config. */
 int di_moe_layer_set_router_bias(void *layer, const float *bias, char *error, int capacity);
 
+/* MLX checkpoints (Qwen36Weights.cs:55-100 over SafeTensors.cs:13-46): `directory` holds config.json
+   (text_config: hidden_size, num_experts, moe_intermediate_size, num_experts_per_tok = 8,
+   num_hidden_layers, norm_topk_prob; quantization: affine, group 64, 5 or 8 bits, per-matrix
+   overrides), model.safetensors.index.json and the shards its weight_map names. Layer l's block
+   is read from language_model.model.layers.{l}.mlp.gate (router, 8-bit), mlp.switch_mlp.{gate,up,
+   down}_proj, mlp.shared_expert.{gate,up,down}_proj and mlp.shared_expert_gate (8-bit), each as
+   .weight (U32 packed), .scales and .biases (BF16), and its RMSNorm weights from
+   post_attention_layernorm.weight (BF16 or F32). Every header, dtype, shape, byte range and shard
+   name is validated before anything is allocated or uploaded; a shard name must be a plain file
+   name inside the directory. */
+/* Validates layer `layer` of a checkpoint without a GPU; geometry receives {E, D, I, bits}. */
+int di_moe_checkpoint_probe(const char *directory, int layer, int32_t *geometry, char *error, int capacity);
+/* Loads and binds layer `layer`'s MoE block on ctx (the layer owns its eight matrices: destroy it
+   with di_moe_layer_destroy); norm (optional, f32 [D]) receives the layer's RMSNorm weights. */
+void *di_moe_layer_load(void *ctx, const char *directory, int layer, float *norm, char *error, int capacity);
+
 /* flags for di_moe_block / di_moe_stack */
 #define DI_MOE_DEVICE_IO 1      /* x, y, ids, probs (and norms/traces) are device pointers */
 #define DI_MOE_FORCE_ROUTES 2   /* ids is an INPUT [T,8]: forced expert ids (gpu_graph.mm:153-159) */

@@ -19,6 +19,7 @@
 #include <string>
 #include <vector>
 
+#include "checkpoint.h"
 #include "common.cuh"
 #include "decode.cuh"
 #include "decode_stack.cuh"
@@ -445,6 +446,14 @@ void configure_kernels() {
                          gg::SMEM);
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          gg::SMEM);
+    cudaFuncSetAttribute(gg::grouped_gemm_pair_kernel<gg::MODE_GATE_UP, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::P_SMEM);
+    cudaFuncSetAttribute(gg::grouped_gemm_pair_kernel<gg::MODE_GATE_UP, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::P_SMEM);
+    cudaFuncSetAttribute(gg::grouped_gemm_pair_kernel<gg::MODE_DOWN, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::P_SMEM);
+    cudaFuncSetAttribute(gg::grouped_gemm_pair_kernel<gg::MODE_DOWN, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gg::P_SMEM);
     cudaFuncSetAttribute(decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecodeSmemMax);
     cudaFuncSetAttribute(decode_ffn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(decode_ffn_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -499,7 +508,7 @@ gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QVie
                           const uint16_t *src, int src_rows, const uint16_t *shared_src, int shared_rows,
                           const int32_t *perm, const Tile *tiles,
                           const int32_t *n_tiles, int shared_pos0, int shared_src0, int K, int rows, int E,
-                          uint16_t *out, int out_rows, uint32_t *err) {
+                          uint16_t *out, int out_rows, uint32_t *err, bool pair = false) {
     gg::Params p;
     std::memset(&p, 0, sizeof(p));
     const QView ws[4] = {w0, w1, s0, s1};
@@ -511,12 +520,14 @@ gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QVie
         encode_2d(&p.code[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, ws[i].packed, row_bytes,
                   (uint64_t)ws[i].experts * ws[i].rows, row_bytes, 64, rpu, CU_TENSOR_MAP_SWIZZLE_64B);
     }
+    // B boxes of 16 << i rows (the single-CTA kernel) or 8 << i (a CTA pair: each CTA loads half a tile)
+    const uint32_t box0 = pair ? 8u : 16u;
     for (int i = 0; i < gg::kBoxes; ++i) {
         encode_2d(&p.bmap[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, src, (uint64_t)K, (uint64_t)std::max(src_rows, 1),
-                  (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_128B);
+                  (uint64_t)K * 2, gg::BK, box0 << i, CU_TENSOR_MAP_SWIZZLE_128B);
         if (shared_src)
             encode_2d(&p.smap[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, shared_src, (uint64_t)K,
-                      (uint64_t)std::max(shared_rows, 1), (uint64_t)K * 2, gg::BK, 16u << i, CU_TENSOR_MAP_SWIZZLE_128B);
+                      (uint64_t)std::max(shared_rows, 1), (uint64_t)K * 2, gg::BK, box0 << i, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     p.perm_route = perm;
     p.tiles = tiles;
@@ -538,6 +549,36 @@ template <int MODE>
 void launch_grouped(const gg::Params &p, int bits, int grid, cudaStream_t st) {
     if (bits == 8) gg::grouped_gemm_kernel<MODE, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
     else gg::grouped_gemm_kernel<MODE, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+}
+
+// The CTA-pair grouped GEMM: clusters of two CTAs, one per SM of a pair of SMs (grid = the even
+// number of SMs at most `sms`); its B maps hold 8 << i-row boxes (grouped_params(..., pair)).
+template <int MODE>
+void launch_grouped_pair(const gg::Params &p, int bits, int sms, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(sms & ~1));
+    cfg.blockDim = dim3(gg::THREADS);
+    cfg.dynamicSmemBytes = gg::P_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (bits == 8) CK(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel<MODE, 8>, p));
+    else CK(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel<MODE, 5>, p));
+}
+
+// The expert GEMMs of the block run on CTA pairs when DEEPINFER_GROUPED_PAIR=1 (the single-CTA
+// kernel otherwise; it also serves the router's and the dense projections' GEMMs).
+bool use_pair_gemm() {
+    static const bool pair = [] {
+        const char *v = std::getenv("DEEPINFER_GROUPED_PAIR");
+        return v && std::strcmp(v, "1") == 0;
+    }();
+    return pair;
 }
 
 // ------------------------------------------------------------------------ the block
@@ -801,14 +842,17 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_GATE_UP);
     // 5. grouped gate/up + SwiGLU (routed experts and the shared expert)
     const int grid = c->sms;
-    launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, G, U, SG, SU, b.xp, 8 * T, x, T, b.perm,
-                                                    b.tiles, b.n_tiles, 8 * T, 0, D, I, E, b.act, 9 * T, c->d_err),
-                                     L->bits, grid, st);
+    const bool pair = use_pair_gemm();
+    const gg::Params pgu = grouped_params(gg::MODE_GATE_UP, G, U, SG, SU, b.xp, 8 * T, x, T, b.perm, b.tiles,
+                                         b.n_tiles, 8 * T, 0, D, I, E, b.act, 9 * T, c->d_err, pair);
+    if (pair) launch_grouped_pair<gg::MODE_GATE_UP>(pgu, L->bits, grid, st);
+    else launch_grouped<gg::MODE_GATE_UP>(pgu, L->bits, grid, st);
     if (profile) stage_mark(c, S_DOWN);
     // 6. grouped down -> expert rows in route order, shared rows
-    launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dn, Dn, SD, SD, b.act, 9 * T, nullptr, 0, b.perm,
-                                                 b.tiles, b.n_tiles, 8 * T, 0, I, D, E, b.yr, 9 * T, c->d_err),
-                                  L->bits, grid, st);
+    const gg::Params pdn = grouped_params(gg::MODE_DOWN, Dn, Dn, SD, SD, b.act, 9 * T, nullptr, 0, b.perm, b.tiles,
+                                         b.n_tiles, 8 * T, 0, I, D, E, b.yr, 9 * T, c->d_err, pair);
+    if (pair) launch_grouped_pair<gg::MODE_DOWN>(pdn, L->bits, grid, st);
+    else launch_grouped<gg::MODE_DOWN>(pdn, L->bits, grid, st);
     if (profile) stage_mark(c, S_COMBINE);
     // 7. combine (stacks: fused with the residual update and the next layer's RMSNorm)
     if (resid && !y) {
@@ -1410,6 +1454,89 @@ API int di_moe_layer_set_router_bias(void *layer, const float *bias, char *error
         return -1;
     }
     return 0;
+}
+
+// ---------------------------------------------------------------------------- MLX checkpoints
+
+API int di_moe_checkpoint_probe(const char *directory, int layer, int32_t *geometry, char *error, int capacity) {
+    if (!directory || !geometry) {
+        set_error(error, capacity, "Invalid checkpoint probe arguments");
+        return -1;
+    }
+    try {
+        ckpt::LayerPlan P;
+        ckpt::plan_layer(directory, layer, P);
+        ckpt::read_norm(P);
+        geometry[0] = P.E;
+        geometry[1] = P.D;
+        geometry[2] = P.I;
+        geometry[3] = P.bits;
+    } catch (const std::exception &e) {
+        set_error(error, capacity, "%s", e.what());
+        return -1;
+    }
+    return 0;
+}
+
+API void *di_moe_layer_load(void *ctx, const char *directory, int layer, float *norm, char *error, int capacity) {
+    if (!live_context(ctx) || !directory) {
+        set_error(error, capacity, "Invalid context or checkpoint directory");
+        return nullptr;
+    }
+    Context *c = static_cast<Context *>(ctx);
+    ckpt::LayerPlan P;
+    std::vector<float> nw;
+    try {
+        ckpt::plan_layer(directory, layer, P);  // every tensor validated before any allocation
+        nw = ckpt::read_norm(P);
+    } catch (const std::exception &e) {
+        set_error(error, capacity, "%s", e.what());
+        return nullptr;
+    }
+    void *mats[8] = {};
+    auto drop = [&]() {
+        for (void *m : mats)
+            if (m) di_quant_matrix_destroy(m);
+    };
+    for (int i = 0; i < 8; ++i) {
+        const ckpt::PlannedMatrix &M = P.m[i];
+        mats[i] = di_quant_matrix_create(c, M.experts, M.rows, M.cols, M.bits, 64, error, capacity);
+        if (!mats[i]) {
+            drop();
+            return nullptr;
+        }
+        Matrix *m = static_cast<Matrix *>(mats[i]);
+        for (int j = 0; j < 3; ++j) {
+            if (M.t[j].bytes != m->bytes[j]) {
+                set_error(error, capacity, "Tensor %s has %llu bytes; the matrix buffer holds %zu", M.t[j].name.c_str(),
+                          (unsigned long long)M.t[j].bytes, m->bytes[j]);
+                drop();
+                return nullptr;
+            }
+            std::vector<uint8_t> host(M.t[j].bytes);
+            try {
+                M.shard[j]->read(M.t[j], host.data());
+            } catch (const std::exception &e) {
+                set_error(error, capacity, "%s", e.what());
+                drop();
+                return nullptr;
+            }
+            if (di_quant_matrix_upload(mats[i], j, host.data(), host.size(), error, capacity)) {
+                drop();
+                return nullptr;
+            }
+        }
+    }
+    void *layer_h = di_moe_layer_create(c, mats[0], mats[1], mats[2], mats[3], mats[4], mats[5], mats[6], mats[7],
+                                        error, capacity);
+    if (!layer_h) {
+        drop();
+        return nullptr;
+    }
+    // the layer holds the only references: its matrices are freed with it
+    for (void *m : mats) release_matrix(static_cast<Matrix *>(m));
+    if (norm) std::memcpy(norm, nw.data(), sizeof(float) * nw.size());
+    return layer_h;
 }
 
 namespace {

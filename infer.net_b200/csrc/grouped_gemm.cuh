@@ -572,5 +572,381 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     }
 }
 
+// ------------------------------------------------------------------ CTA-pair kernel
+//
+// The same grouped GEMM on CTA pairs (2-CTA clusters): one pair unit is a token tile (<= 256
+// tokens) x 256 A rows, the even CTA's 128 rows and the odd CTA's 128 rows (two consecutive row
+// blocks of the single-CTA kernel), and one pair MMA (cta_group::2, M = 256) issued by the even
+// CTA computes both CTAs' accumulators. Each CTA dequantises its own A rows and loads its half of
+// the unit's B rows, so per SM the B operand -- copied into and read from shared memory -- is half
+// as large, and one MMA-issuing thread drives two tensor cores.
+//
+// Synchronisation across the pair (the even CTA, rank 0, owns the stage and accumulator
+// barriers the MMA waits on):
+//   - A ready: both CTAs' dequantiser warps arrive on the even CTA's full[s] (8 arrivals), the odd
+//     CTA's through its shared::cluster address, after fence.proxy.async;
+//   - B ready: the even CTA's B producer arms bfull[s] with both halves' bytes; both CTAs' tensor
+//     copies complete on it (cta_group::2 copies, no multicast);
+//   - stage and accumulator free: the MMA thread's commits arrive on empty[s] / accf[slot] in both
+//     CTAs (a multicast commit);
+//   - accumulator drained: both CTAs' epilogue warps arrive on the even CTA's acce[slot] (8).
+// Barrier initialisation and the kernel's end are cluster-wide barriers, so no CTA signals a
+// barrier its partner has not initialised or has already left.
+constexpr int P_STAGES = 4;
+constexpr int kBh = 128 * 128;   // bytes of one CTA's half of a B stage tile (<= 128 token rows)
+constexpr int P_STAGE_BYTES = kA + kBh;
+constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE_BYTES + CSTAGES * kCode + 2 * kScaleBuf + kStageOut + 512;
+static_assert(P_SMEM <= 227 * 1024, "pair grouped GEMM shared memory");
+
+template <int MODE, int BITS>
+__global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
+    uint8_t *smem = smem_raw + pad;
+    uint8_t *code_ring = smem + P_STAGES * P_STAGE_BYTES;
+    uint8_t *scale_buf = code_ring + CSTAGES * kCode;
+    uint8_t *stage_out = scale_buf + 2 * kScaleBuf;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
+    uint64_t *full = bars, *bfull = bars + P_STAGES, *empty = bars + 2 * P_STAGES;
+    uint64_t *cfull = bars + 3 * P_STAGES, *cempty = cfull + CSTAGES;
+    uint64_t *sfull = cempty + CSTAGES, *sempty = sfull + 2;
+    uint64_t *accf = sempty + 2, *acce = accf + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
+    auto a_tile = [&](int s) { return smem + s * P_STAGE_BYTES; };
+    auto b_tile = [&](int s) { return smem + s * P_STAGE_BYTES + kA; };
+    auto c_tile = [&](int cs) { return code_ring + cs * kCode; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = (int)cluster_id_x(), npairs = (int)nclusters_x();
+    constexpr int RPU = rows_per_unit<MODE>();
+    constexpr int NMAT = MODE == MODE_GATE_UP ? 2 : 1;
+    const int RB = (p.rows + RPU - 1) / RPU;  // row blocks of one CTA
+    const int PRB = (RB + 1) / 2;             // pair row blocks
+    const int nk = p.K / BK;
+    const int gpr = p.K / 64;
+    const int n_units = (*p.n_tiles) * PRB;
+    // CTA row block of pair unit u
+    auto cta_rb = [&](int u) { return 2 * (u % PRB) + (int)rank; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(&full[s], 8);   // the dequantiser warps of the stage's group, in both CTAs
+            mbar_init(&bfull[s], 1);  // the even CTA's B producer arrive + both CTAs' B bytes
+            mbar_init(&empty[s], 1);  // the pair MMA's commit
+        }
+        for (int c = 0; c < CSTAGES; ++c) {
+            mbar_init(&cfull[c], 1);
+            mbar_init(&cempty[c], 4);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&sfull[a], 1);
+            mbar_init(&sempty[a], 8);
+            mbar_init(&accf[a], 1);
+            mbar_init(&acce[a], 8);  // the epilogue warps of both CTAs
+        }
+        fence_mbarrier_init();
+    }
+    if (warp == 4) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);  // the same warp in both CTAs
+        tmem_relinquish_pair();
+    }
+    if (warp == 6 && lane == 0)
+        for (int i = 0; i < kBoxes; ++i) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&p.bmap[i]) : "memory");
+            if constexpr (MODE == MODE_GATE_UP) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.smap[i]) : "memory");
+        }
+    if (warp == 5 && lane == 0)
+        for (int i = 0; i < 4; ++i) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.code[i]) : "memory");
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised and the tensor memory is allocated
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp >= 8) {
+        // ---------------------------------------------------------------- A dequantisers
+        const int g = (warp - 8) >> 2, m = threadIdx.x - 256 - 128 * g;  // 0..127
+        int mat, r;
+        a_row<MODE>(m, mat, r);
+        const bool fast_scales = (gpr & 7) == 0;
+        const uint32_t full_leader = mapa_shared(full, 0);  // full[0] of the even CTA
+        int it0 = 0;
+        for (int ul = 0, u = pair; u < n_units && ok; ++ul, u += npairs, it0 += nk) {
+            const int rb = cta_rb(u), sb = ul & 1;
+            const bool live = rb * RPU + r < p.rows;
+            if (!mbar_wait(&sfull[sb], (ul >> 1) & 1, p.err, kErrTimeout)) { ok = false; break; }
+            const uint16_t *s_row =
+                reinterpret_cast<const uint16_t *>(scale_buf + sb * kScaleBuf) + ((mat * 2) * RPU + r) * gpr;
+            const uint16_t *b_row = s_row + RPU * gpr;
+            uint4 swin = make_uint4(0, 0, 0, 0), bwin = swin;
+            int win = -1;
+            for (int kb = (g - it0) & 1; kb < nk; kb += 2) {
+                float sc, bi;
+                if (fast_scales) {
+                    if ((kb >> 3) != win) {
+                        win = kb >> 3;
+                        swin = *reinterpret_cast<const uint4 *>(s_row + 8 * win);
+                        bwin = *reinterpret_cast<const uint4 *>(b_row + 8 * win);
+                    }
+                    const int e = kb & 7;
+                    const uint32_t sw = e < 2 ? swin.x : e < 4 ? swin.y : e < 6 ? swin.z : swin.w;
+                    const uint32_t bw = e < 2 ? bwin.x : e < 4 ? bwin.y : e < 6 ? bwin.z : bwin.w;
+                    sc = (e & 1) ? bf16_hi(sw) : bf16_lo(sw);
+                    bi = (e & 1) ? bf16_hi(bw) : bf16_lo(bw);
+                } else {
+                    sc = bf16_bits_to_f32(s_row[kb]);
+                    bi = bf16_bits_to_f32(b_row[kb]);
+                }
+                const int it = it0 + kb, s = it % P_STAGES, cs = it % CSTAGES;
+                if (!mbar_wait(&cfull[cs], (it / CSTAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
+                const uint8_t *crow = c_tile(cs) + mat * (RPU * 64);
+                uint4 cw[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) cw[c] = *reinterpret_cast<const uint4 *>(crow + sw64_offset(r, c));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&cempty[cs]);
+                uint32_t o[32];
+                if constexpr (BITS == 8) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) dequant16_8bit(cw[c], sc, bi, o + 8 * c);
+                } else {
+                    const uint32_t w16[16] = {cw[0].x, cw[0].y, cw[0].z, cw[0].w, cw[1].x, cw[1].y, cw[1].z, cw[1].w,
+                                              cw[2].x, cw[2].y, cw[2].z, cw[2].w, cw[3].x, cw[3].y, cw[3].z, cw[3].w};
+                    const bool odd = ((kb * 40) & 15) != 0;
+                    uint32_t w10[10];
+#pragma unroll
+                    for (int i = 0; i < 10; ++i) w10[i] = odd ? w16[i + 2] : w16[i];
+                    dequant32_5bit(w10, sc, bi, o);
+                    dequant32_5bit(w10 + 5, sc, bi, o + 16);
+                }
+                if (!live)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = 0;
+                // the A tile is free once the pair MMA of the stage's previous use has completed
+                if (!mbar_wait(&empty[s], ((it / P_STAGES) & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
+                uint8_t *t = a_tile(s);
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4 *>(t + sw128_offset(m, c)) =
+                        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (leader) mbar_arrive(&full[s]);
+                    else mbar_arrive_cluster(full_leader + s * 8u);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sempty[sb]);
+        }
+    } else if (warp == 5) {
+        // ---------------------------------------------------------------- code and scale producer
+        int it = 0, ul = 0;
+        for (int u = pair; u < n_units && ok; u += npairs, ++ul) {
+            const Tile tl = p.tiles[u / PRB];
+            const int rb = cta_rb(u), sb = ul & 1;
+            const bool shared = tl.seg >= p.E;
+            const int expert = shared ? 0 : tl.seg;
+            const bool rows_live = rb * RPU < p.rows;  // the odd CTA's rows may lie past the matrix
+            if (lane == 0) {
+                ok = mbar_wait(&sempty[sb], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeout);
+                if (ok) {
+                    const int nrows = rows_live ? min(RPU, p.rows - rb * RPU) : 0;
+                    const uint32_t bytes = (uint32_t)(nrows * gpr * 2);
+                    mbar_arrive_expect_tx(&sfull[sb], bytes * 2 * NMAT);
+                    if (nrows > 0)
+                        for (int mt = 0; mt < NMAT; ++mt) {
+                            const QView &W = p.w[mt + 2 * shared];
+                            const size_t r0 = (size_t)expert * W.rows + rb * RPU;
+                            uint8_t *dst = scale_buf + sb * kScaleBuf + (size_t)(mt * 2) * RPU * gpr * 2;
+                            bulk_load(dst, W.scales + r0 * gpr, bytes, &sfull[sb]);
+                            bulk_load(dst + RPU * gpr * 2, W.biases + r0 * gpr, bytes, &sfull[sb]);
+                        }
+                }
+            }
+            ok = __shfl_sync(kFull, ok, 0);
+            if (!ok) break;
+            // rows past the matrix read the last valid block's codes (their A rows are zeroed)
+            const int crb = rows_live ? rb : rb - 1;
+            const int row0 = expert * p.w[(lane & 1) + 2 * shared].rows + crb * RPU;
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                const int cs = it % CSTAGES;
+                if (lane == 0) {
+                    ok = mbar_wait(&cempty[cs], ((it / CSTAGES) & 1) ^ 1, p.err, kErrTimeout);
+                    if (ok) mbar_arrive_expect_tx(&cfull[cs], kCode);
+                }
+                ok = __shfl_sync(kFull, ok, 0);
+                if (!ok) break;
+                if (lane < NMAT)
+                    tma_load_2d(c_tile(cs) + lane * (RPU * 64), &p.code[lane + 2 * shared], code_x<BITS>(kb), row0,
+                                &cfull[cs]);
+            }
+        }
+        if (!ok && lane == 0) {
+            for (int k = max(0, it - CSTAGES); k < it; ++k)
+                mbar_wait(&cfull[k % CSTAGES], (k / CSTAGES) & 1, p.err, kErrTimeout);
+            for (int k = max(0, ul - 1); k <= ul; ++k) mbar_wait(&sfull[k & 1], (k >> 1) & 1, p.err, kErrTimeout);
+        }
+    } else if (warp == 6) {
+        // ---------------------------------------------------------------- B producer (this CTA's half)
+        const uint32_t bfull_leader = mapa_shared(bfull, 0);
+        int it = 0;
+        for (int u = pair; u < n_units && ok; u += npairs) {
+            const Tile tl = p.tiles[u / PRB];
+            const bool shared = tl.seg >= p.E;
+            const int N = round16(tl.n), Nh = N >> 1;  // Nh is a multiple of 8
+            // lane i < kBoxes copies 8 << i rows when bit i of Nh/8 is set, larger boxes first
+            const int nb8 = Nh >> 3;
+            const bool box_mine = lane < kBoxes && ((nb8 >> lane) & 1);
+            const int box_off = box_mine ? 8 * ((nb8 >> (lane + 1)) << (lane + 1)) : 0;
+            const bool shared_src = MODE == MODE_GATE_UP && shared;
+            const int row0 = (shared_src ? p.shared_src0 + (tl.p0 - p.shared_pos0) : tl.p0) + (int)rank * Nh + box_off;
+            const CUtensorMap *bm = shared_src ? &p.smap[box_mine ? lane : 0] : &p.bmap[box_mine ? lane : 0];
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                const int s = it % P_STAGES;
+                if (lane == 0) {
+                    ok = mbar_wait(&empty[s], ((it / P_STAGES) & 1) ^ 1, p.err, kErrTimeout);
+                    if (ok && leader) mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u);  // both halves
+                }
+                ok = __shfl_sync(kFull, ok, 0);
+                if (!ok) break;
+                if (box_mine)
+                    tma_load_2d_pair(b_tile(s) + box_off * 128, bm, kb * BK, row0, bfull_leader + s * 8u);
+            }
+        }
+        // copies in flight complete on the even CTA's barriers, which the MMA waits for; the final
+        // cluster barrier keeps both CTAs alive until then
+    } else if (warp == 4) {
+        // ---------------------------------------------------------------- MMA issue (even CTA)
+        if (leader && lane == 0) {
+            int it = 0;
+            SlotPlan plan;
+            for (int u = pair; u < n_units && ok; u += npairs) {
+                const Tile tl = p.tiles[u / PRB];
+                const int N = round16(tl.n);
+                uint32_t phase;
+                const int slot = plan.take(phase);
+                if (!mbar_wait(&acce[slot], (phase & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d = tmem + slot * 256;
+                const uint32_t id = idesc_bf16_f32(2 * BM, N);
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % P_STAGES;
+                    const uint32_t ph = (it / P_STAGES) & 1;
+                    if (!mbar_wait(&bfull[s], ph, p.err, kErrTimeout) || !mbar_wait(&full[s], ph, p.err, kErrTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(a_tile(s)));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(b_tile(s)));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        tc_mma_bf16_pair(d, adesc + 2 * k, bdesc + 2 * k, id, (kb | k) != 0);
+                    tc_commit_pair(&empty[s], 0x3);
+                }
+                if (!ok) break;
+                tc_commit_pair(&accf[slot], 0x3);
+            }
+            if (!ok) {
+                // copies still in flight land on this CTA's bfull barriers: wait for the last stages'
+                for (int k = max(0, it - P_STAGES); k < it; ++k)
+                    mbar_wait(&bfull[k % P_STAGES], (k / P_STAGES) & 1, p.err, kErrTimeout);
+            }
+        }
+        __syncwarp();
+    } else if (warp < 4) {
+        // ---------------------------------------------------------------- epilogue (this CTA's rows)
+        const int q = warp;
+        uint8_t *so = stage_out + q * 2 * 16 * 64;
+        int chunk_no = 0;
+        SlotPlan plan;
+        const uint32_t acce_leader = mapa_shared(acce, 0);
+        for (int u = pair; u < n_units && ok; u += npairs) {
+            const Tile tl = p.tiles[u / PRB];
+            const int rb = cta_rb(u);
+            const int N = round16(tl.n);
+            uint32_t phase;
+            const int slot = plan.take(phase);
+            if (!mbar_wait(&accf[slot], phase & 1, p.err, kErrTimeout)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + slot * 256;
+            float v[16], vn[16];
+            tmem_ld16(lane_base, vn);
+            for (int c = 0; c < N; c += 16) {
+                tc_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = vn[j];
+                if (c + 16 < N) tmem_ld16(lane_base + c + 16, vn);
+                if constexpr (MODE == MODE_GATE_UP) {
+                    const bool lo = lane < 16;
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const float a = v[jj], b = v[jj + 8];
+                        const float oa = __shfl_xor_sync(kFull, a, 16), ob = __shfl_xor_sync(kFull, b, 16);
+                        const float gt = lo ? a : ob, up = lo ? oa : b;
+                        const float act = __fdividef(gt, 1.0f + __expf(-gt)) * up;
+                        reinterpret_cast<uint16_t *>(so)[(jj + (lo ? 0 : 8)) * 16 + (lane & 15)] = f32_to_bf16_bits(act);
+                    }
+                    __syncwarp();
+                    const int tk = lane >> 1, half = lane & 1, n = c + tk;
+                    const int i = rb * 64 + 16 * q + half * 8;
+                    if (n < tl.n && i < p.rows) {
+                        const uint4 val = *reinterpret_cast<const uint4 *>(so + tk * 32 + half * 16);
+                        *reinterpret_cast<uint4 *>(p.out + (size_t)(tl.p0 + n) * p.rows + i) = val;
+                    }
+                    __syncwarp();
+                } else {
+                    uint8_t *sb = so + (chunk_no & 1) * 1024;
+                    ++chunk_no;
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) reinterpret_cast<uint16_t *>(sb)[j * 32 + lane] = f32_to_bf16_bits(v[j]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    const int d0 = rb * 128 + 32 * q;
+                    if (d0 < p.rows) {
+                        if (tl.n - c >= 16) {
+                            if (lane == 0) {
+                                tma_store_2d(&p.ymap, sb, d0, tl.p0 + c);
+                                bulk_commit();
+                            }
+                        } else {
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
+                                const int d = d0 + part * 8;
+                                if (n < tl.n && d < p.rows)
+                                    *reinterpret_cast<uint4 *>(p.out + (size_t)(tl.p0 + n) * p.rows + d) =
+                                        *reinterpret_cast<const uint4 *>(sb + tk * 64 + part * 16);
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (leader) mbar_arrive(&acce[slot]);
+                else mbar_arrive_cluster(acce_leader + slot * 8u);
+            }
+        }
+        if constexpr (MODE == MODE_DOWN)
+            if (lane == 0) bulk_wait<0>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // neither CTA leaves while its partner may still signal it or read its memory
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, TMEM_COLS);
+    }
+}
+
 }  // namespace gg
 }  // namespace di

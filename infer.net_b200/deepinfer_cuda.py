@@ -62,6 +62,8 @@ SIGNATURES = {
                                            C.c_int]),
     "di_moe_layer_create": (C.c_void_p, [C.c_void_p] * 9 + [C.c_char_p, C.c_int]),
     "di_moe_layer_destroy": (None, [C.c_void_p]),
+    "di_moe_checkpoint_probe": (C.c_int, [C.c_char_p, C.c_int, C.c_void_p, C.c_char_p, C.c_int]),
+    "di_moe_layer_load": (C.c_void_p, [C.c_void_p, C.c_char_p, C.c_int, C.c_void_p, C.c_char_p, C.c_int]),
     "di_moe_layer_set_router_bias": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_int]),
     "di_moe_block": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_int]),
@@ -298,6 +300,19 @@ class MoeLayer:
         """Synthetic weights generated on the device (same bits as oracle.Layer(seed, layer, ...))."""
         return cls(ctx, generate_layer_matrices(ctx, seed, layer, bits, E, D, I, stddev))
 
+    @classmethod
+    def load(cls, ctx: Context, directory: str, layer: int):
+        """Layer `layer` of an MLX checkpoint directory: (MoeLayer, RMSNorm weights f32 [D])."""
+        geo = probe_checkpoint(directory, layer)
+        norm = np.zeros(geo["D"], np.float32)
+        err = C.create_string_buffer(2048)
+        h = lib().di_moe_layer_load(ctx.h, directory.encode(), layer, _p(norm), err, 2048)
+        if not h:
+            raise DeepInferError(err.value.decode())
+        obj = cls.__new__(cls)
+        obj.ctx, obj.h, obj.mats = ctx, h, {}
+        return obj, norm
+
     def set_router_bias(self, bias):
         err = C.create_string_buffer(2048)
         b = None if bias is None else np.ascontiguousarray(bias, np.float32)
@@ -320,6 +335,15 @@ class MoeLayer:
         if matrices:
             for m in self.mats.values():
                 m.close()
+
+
+def probe_checkpoint(directory: str, layer: int) -> dict:
+    """Validate layer `layer` of an MLX checkpoint without a GPU: {E, D, I, bits}."""
+    geo = np.zeros(4, np.int32)
+    err = C.create_string_buffer(2048)
+    if lib().di_moe_checkpoint_probe(directory.encode(), layer, _p(geo), err, 2048):
+        raise DeepInferError(err.value.decode())
+    return dict(zip(("E", "D", "I", "bits"), (int(v) for v in geo)))
 
 
 def generate_layer_matrices(ctx, seed, layer, bits=8, E=256, D=2048, I=512, stddev=0.02, shard=(0, 1)):
