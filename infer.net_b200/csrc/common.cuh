@@ -327,9 +327,47 @@ __device__ __forceinline__ uint32_t mapa_shared(const void *p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
     return r;
 }
-// Arrive on an mbarrier of a CTA of the cluster (default release semantics).
+// Arrive on an mbarrier of a CTA of the cluster, releasing at cluster scope: every write of this
+// thread (and, through a preceding warp or CTA barrier, of its warp or CTA) is visible to a thread
+// of the cluster that acquires the phase.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// mbar_wait with acquire at cluster scope (phases completed by the other CTA of a pair).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+            atomicOr(err, code);
+            return false;
+        }
+    }
+}
+// Bulk copy of `bytes` from this CTA's shared memory into another CTA's (shared::cluster addresses
+// of the destination and of an mbarrier there, whose transaction count it completes).
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void *src, uint32_t bytes,
+                                                     uint32_t bar_cluster) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst_cluster),
+                 "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+                 : "memory");
+}
+// Named barrier among `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 // Every thread of both CTAs: a cluster-wide barrier (release / acquire).
 __device__ __forceinline__ void cluster_sync() {

@@ -583,10 +583,13 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
 //
 // Synchronisation across the pair (the even CTA, rank 0, owns the stage and accumulator
 // barriers the MMA waits on):
-//   - A ready: both CTAs' dequantiser warps arrive on the even CTA's full[s] (8 arrivals), the odd
-//     CTA's through its shared::cluster address, after fence.proxy.async;
-//   - B ready: the even CTA's B producer arms bfull[s] with both halves' bytes; both CTAs' tensor
-//     copies complete on it (cta_group::2 copies, no multicast);
+//   - A ready: the even CTA's dequantiser warps arrive on its full[s]; the odd CTA's, after their
+//     fence.proxy.async and a named barrier among the group, signal through the async proxy: one
+//     thread copies 16 bytes into the even CTA's shared memory with a bulk copy that completes its
+//     bytes on the even CTA's bfull[s] (a per-stage release of four warps' writes at cluster scope
+//     that costs the writers no wait);
+//   - B ready: the even CTA's B producer arms bfull[s] with both halves' bytes and those 16; both
+//     CTAs' tensor copies complete on it (cta_group::2 copies, no multicast);
 //   - stage and accumulator free: the MMA thread's commits arrive on empty[s] / accf[slot] in both
 //     CTAs (a multicast commit);
 //   - accumulator drained: both CTAs' epilogue warps arrive on the even CTA's acce[slot] (8).
@@ -613,6 +616,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
     uint64_t *sfull = cempty + CSTAGES, *sempty = sfull + 2;
     uint64_t *accf = sempty + 2, *acce = accf + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
+    uint64_t *aready = reinterpret_cast<uint64_t *>(tmem_slot + 2);  // odd CTA: its group's A rows written
+    uint8_t *sig_src = reinterpret_cast<uint8_t *>(bars) + 320;  // 16 bytes the odd CTA sends per stage
+    uint8_t *sig_dst = sig_src + 16;                              // where they land in the even CTA
     auto a_tile = [&](int s) { return smem + s * P_STAGE_BYTES; };
     auto b_tile = [&](int s) { return smem + s * P_STAGE_BYTES + kA; };
     auto c_tile = [&](int cs) { return code_ring + cs * kCode; };
@@ -633,8 +639,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
-            mbar_init(&full[s], 8);   // the dequantiser warps of the stage's group, in both CTAs
-            mbar_init(&bfull[s], 1);  // the even CTA's B producer arrive + both CTAs' B bytes
+            mbar_init(&full[s], 4);   // the even CTA's dequantiser warps of the stage's group
+            mbar_init(&bfull[s], 1);  // the even CTA's B producer arrive + both CTAs' B bytes + 16 signal bytes
             mbar_init(&empty[s], 1);  // the pair MMA's commit
         }
         for (int c = 0; c < CSTAGES; ++c) {
@@ -647,6 +653,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
             mbar_init(&accf[a], 1);
             mbar_init(&acce[a], 8);  // the epilogue warps of both CTAs
         }
+        for (int s = 0; s < P_STAGES; ++s) mbar_init(&aready[s], 4);
         fence_mbarrier_init();
     }
     if (warp == 4) {
@@ -673,7 +680,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
         int mat, r;
         a_row<MODE>(m, mat, r);
         const bool fast_scales = (gpr & 7) == 0;
-        const uint32_t full_leader = mapa_shared(full, 0);  // full[0] of the even CTA
+        const uint32_t bfull_leader = mapa_shared(bfull, 0), sig_leader = mapa_shared(sig_dst, 0);
         int it0 = 0;
         for (int ul = 0, u = pair; u < n_units && ok; ++ul, u += npairs, it0 += nk) {
             const int rb = cta_rb(u), sb = ul & 1;
@@ -735,9 +742,19 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
                         make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    if (leader) mbar_arrive(&full[s]);
-                    else mbar_arrive_cluster(full_leader + s * 8u);
+                if (leader) {
+                    if (lane == 0) mbar_arrive(&full[s]);
+                } else {
+                    if (lane == 0) mbar_arrive(&aready[s]);
+                    // the group's first warp: once all 128 rows are written and fenced, signal the even CTA
+                    if (m == 0) {
+                        if (mbar_wait(&aready[s], (it / P_STAGES) & 1, p.err, kErrTimeout))
+                            bulk_copy_to_cluster(sig_leader, sig_src, 16, bfull_leader + s * 8u);
+                        else
+                            ok = false;
+                    }
+                    ok = __shfl_sync(kFull, ok, 0);
+                    if (!ok) break;
                 }
             }
             __syncwarp();
@@ -810,7 +827,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
                 const int s = it % P_STAGES;
                 if (lane == 0) {
                     ok = mbar_wait(&empty[s], ((it / P_STAGES) & 1) ^ 1, p.err, kErrTimeout);
-                    if (ok && leader) mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u);  // both halves
+                    if (ok && leader) mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u + 16u);  // both halves
                 }
                 ok = __shfl_sync(kFull, ok, 0);
                 if (!ok) break;
@@ -830,14 +847,15 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
                 const int N = round16(tl.n);
                 uint32_t phase;
                 const int slot = plan.take(phase);
-                if (!mbar_wait(&acce[slot], (phase & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
+                if (!mbar_wait_cluster(&acce[slot], (phase & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d = tmem + slot * 256;
                 const uint32_t id = idesc_bf16_f32(2 * BM, N);
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % P_STAGES;
                     const uint32_t ph = (it / P_STAGES) & 1;
-                    if (!mbar_wait(&bfull[s], ph, p.err, kErrTimeout) || !mbar_wait(&full[s], ph, p.err, kErrTimeout)) {
+                    if (!mbar_wait_cluster(&bfull[s], ph, p.err, kErrTimeout) ||
+                        !mbar_wait_cluster(&full[s], ph, p.err, kErrTimeout)) {
                         ok = false;
                         break;
                     }

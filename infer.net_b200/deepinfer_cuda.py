@@ -282,6 +282,7 @@ class MoeLayer:
         if not h:
             raise DeepInferError(err.value.decode())
         self.ctx, self.h, self.mats = ctx, h, mats
+        self.D = mats["gate"].cols
 
     @classmethod
     def from_oracle(cls, ctx: Context, layer) -> "MoeLayer":
@@ -310,7 +311,7 @@ class MoeLayer:
         if not h:
             raise DeepInferError(err.value.decode())
         obj = cls.__new__(cls)
-        obj.ctx, obj.h, obj.mats = ctx, h, {}
+        obj.ctx, obj.h, obj.mats, obj.D = ctx, h, {}, geo["D"]
         return obj, norm
 
     def set_router_bias(self, bias):
@@ -386,7 +387,7 @@ class ExpertParallel:
         if not h:
             raise DeepInferError(err.value.decode())
         obj = MoeLayer.__new__(MoeLayer)
-        obj.ctx, obj.h, obj.mats = self.ctx, h, mats
+        obj.ctx, obj.h, obj.mats, obj.D = self.ctx, h, mats, mats["gate"].cols
         return obj
 
     def stack(self, layers, norms, x, tokens, eps=1e-6, flags=0, h_trace=None, ids_trace=None):
@@ -408,7 +409,7 @@ class ExpertParallel:
 def moe_block(layer: MoeLayer, x_bf16: np.ndarray, flags: int = 0, forced: np.ndarray | None = None):
     """Host-buffer convenience call: returns (y bf16 [T,D], ids [T,8], probs [T,8], ms)."""
     x = np.ascontiguousarray(x_bf16, np.uint16)
-    T = x.size // layer.mats["gate"].cols
+    T = x.size // layer.D
     y = np.zeros_like(x)
     ids = np.zeros((T, 8), np.int32) if forced is None else np.ascontiguousarray(forced, np.int32).copy()
     probs = np.zeros((T, 8), np.float32)
