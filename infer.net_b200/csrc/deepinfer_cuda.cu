@@ -439,13 +439,13 @@ void configure_kernels() {
     if (kernels_configured) return;
     cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(router::Smem));
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::SMEM);
+                         gg::smem_bytes<gg::MODE_GATE_UP>());
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_GATE_UP, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::SMEM);
+                         gg::smem_bytes<gg::MODE_GATE_UP>());
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::SMEM);
+                         gg::smem_bytes<gg::MODE_DOWN>());
     cudaFuncSetAttribute(gg::grouped_gemm_kernel<gg::MODE_DOWN, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         gg::SMEM);
+                         gg::smem_bytes<gg::MODE_DOWN>());
     cudaFuncSetAttribute(gg::grouped_gemm_pair_kernel<gg::MODE_GATE_UP, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          gg::P_SMEM);
     cudaFuncSetAttribute(gg::grouped_gemm_pair_kernel<gg::MODE_GATE_UP, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -547,8 +547,8 @@ gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QVie
 
 template <int MODE>
 void launch_grouped(const gg::Params &p, int bits, int grid, cudaStream_t st) {
-    if (bits == 8) gg::grouped_gemm_kernel<MODE, 8><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
-    else gg::grouped_gemm_kernel<MODE, 5><<<grid, gg::THREADS, gg::SMEM, st>>>(p);
+    if (bits == 8) gg::grouped_gemm_kernel<MODE, 8><<<grid, gg::THREADS, gg::smem_bytes<MODE>(), st>>>(p);
+    else gg::grouped_gemm_kernel<MODE, 5><<<grid, gg::THREADS, gg::smem_bytes<MODE>(), st>>>(p);
 }
 
 // The CTA-pair grouped GEMM: clusters of two CTAs, one per SM of a pair of SMs (grid = the even

@@ -48,17 +48,26 @@ constexpr int MODE_GATE_UP = 0, MODE_DOWN = 1;
 constexpr int BM = 128;          // A rows per unit (one MMA M)
 constexpr int BN = 256;          // max tokens per unit (one 256-column accumulator slot)
 constexpr int BK = 64;           // K per pipeline stage: 128-byte bf16 rows, one group of 64 codes
-constexpr int STAGES = 3;
+// Pipeline depths per mode (measured): gate/up units run 32 stages and gain from a fourth A/B
+// stage; down units run 8 and gain more from a fourth code slot. Both fit 227 KB.
+template <int MODE>
+__host__ __device__ constexpr int stages() { return MODE == 0 ? 4 : 3; }
+template <int MODE>
+__host__ __device__ constexpr int cstages() { return MODE == 0 ? 3 : 4; }
 constexpr int THREADS = 512;
 constexpr int kA = BM * 128;     // bytes of one A stage tile (bf16)
 constexpr int kB = BN * 128;     // bytes of one B stage tile (bf16)
 constexpr int kCode = BM * 64;   // bytes of one stage's code window (64 bytes per A row)
 constexpr int STAGE_BYTES = kA + kB;
-constexpr int CSTAGES = 4;       // code ring slots
-constexpr int kScaleBuf = 16384; // scales + biases of one unit's rows (<= 32 groups per row)
+constexpr int CSTAGES = 4;       // code ring slots of the pair kernel
+constexpr int kScaleBuf = 16384; // pair kernel: scales + biases of one unit's rows (<= 32 groups per row)
 constexpr int kStageOut = 4 * 2 * 16 * 64;  // epilogue staging: 4 warps x 2 buffers x 16 tokens x 64 bytes
 constexpr int kBoxes = 5;               // down B boxes of 16 << i rows, i < kBoxes
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + CSTAGES * kCode + 2 * kScaleBuf + kStageOut + 512;
+template <int MODE>
+__host__ __device__ constexpr int smem_bytes() {
+    return 1024 + stages<MODE>() * STAGE_BYTES + cstages<MODE>() * kCode + kStageOut + 512;
+}
+static_assert(smem_bytes<0>() <= 227 * 1024 && smem_bytes<1>() <= 227 * 1024, "grouped GEMM shared memory");
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int MODE>
@@ -195,18 +204,17 @@ struct SlotPlan {
 
 template <int MODE, int BITS>
 __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+    constexpr int STAGES = stages<MODE>(), CSTAGES = cstages<MODE>();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
     uint8_t *smem = smem_raw + pad;
     uint8_t *code_ring = smem + STAGES * STAGE_BYTES;
-    uint8_t *scale_buf = code_ring + CSTAGES * kCode;
-    uint8_t *stage_out = scale_buf + 2 * kScaleBuf;
+    uint8_t *stage_out = code_ring + CSTAGES * kCode;
     uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kStageOut);
-    uint64_t *full = bars, *bfull = bars + STAGES, *empty = bars + 2 * STAGES;
-    uint64_t *cfull = bars + 3 * STAGES, *cempty = cfull + CSTAGES;
-    uint64_t *sfull = cempty + CSTAGES, *sempty = sfull + 2;
-    uint64_t *accf = sempty + 2, *acce = accf + 2;
+    uint64_t *full = bars, *empty = bars + STAGES;
+    uint64_t *cfull = bars + 2 * STAGES, *cempty = cfull + CSTAGES;
+    uint64_t *accf = cempty + CSTAGES, *acce = accf + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
     auto a_tile = [&](int s) { return smem + s * STAGE_BYTES; };
     auto b_tile = [&](int s) { return smem + s * STAGE_BYTES + kA; };
@@ -224,8 +232,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 4);   // the dequantiser warps of the stage's group
-            mbar_init(&bfull[s], 1);  // B producer arrive + B bytes
+            mbar_init(&full[s], 5);   // the dequantiser warps of the stage's group + B producer arrive (+ B bytes)
             mbar_init(&empty[s], 1);  // MMA commit
         }
         for (int c = 0; c < CSTAGES; ++c) {
@@ -233,8 +240,6 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             mbar_init(&cempty[c], 4);  // the dequantiser warps holding the codes in registers
         }
         for (int a = 0; a < 2; ++a) {
-            mbar_init(&sfull[a], 1);
-            mbar_init(&sempty[a], 8);
             mbar_init(&accf[a], 1);
             mbar_init(&acce[a], 4);
         }
@@ -263,42 +268,74 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     if (warp >= 8) {
         // ---------------------------------------------------------------- A dequantisers
         // group g takes the stages of the flat index with it % 2 == g (each stage is one
-        // quantisation group); thread m of the group converts A row m.
+        // quantisation group); thread m of the group converts A row m. Its row's scales and biases
+        // come from global memory in windows of 8 groups (16 bytes each), one window ahead of use:
+        // the next unit's first window is requested during the current unit's last.
         const int g = (warp - 8) >> 2, m = threadIdx.x - 256 - 128 * g;  // 0..127
         const bool timed = warp == 8;
         const long long t_loop = gg_now();
         int mat, r;
         a_row<MODE>(m, mat, r);
-        const bool fast_scales = (gpr & 7) == 0;  // rows of scales are 16-byte aligned
-        int it0 = 0;                              // flat index of the unit's first stage
-        for (int ul = 0, u = blockIdx.x; u < n_units && ok; ++ul, u += gridDim.x, it0 += nk) {
-            const int rb = u % RB, sb = ul & 1;
-            const bool live = rb * RPU + r < p.rows;
-            const long long t_s = gg_now();
-            if (!mbar_wait(&sfull[sb], (ul >> 1) & 1, p.err, kErrTimeout)) { ok = false; break; }
-            if (timed) gg_time(tkind, T_DQ_SCALES, t_s);
-            const uint16_t *s_row =
-                reinterpret_cast<const uint16_t *>(scale_buf + sb * kScaleBuf) + ((mat * 2) * RPU + r) * gpr;
-            const uint16_t *b_row = s_row + RPU * gpr;
-            uint4 swin = make_uint4(0, 0, 0, 0), bwin = swin;
+        const bool vec_scales = (gpr & 7) == 0;  // rows of scales are 16-byte aligned
+        // this thread's scale and bias rows in unit u's matrix (live: the row lies inside it)
+        struct RowRef {
+            const uint16_t *s, *b;
+            bool live;
+        };
+        struct Win {
+            uint4 s, b;
+        };
+        auto row_of = [&](int u) -> RowRef {
+            const Tile tl = p.tiles[u / RB];
+            const int rb = u % RB;
+            const bool shared = tl.seg >= p.E;
+            const QView &W = p.w[mat + 2 * shared];
+            if (rb * RPU + r >= p.rows) return RowRef{nullptr, nullptr, false};
+            const size_t row = (size_t)(shared ? 0 : tl.seg) * W.rows + rb * RPU + r;
+            return RowRef{W.scales + row * gpr, W.biases + row * gpr, true};
+        };
+        auto load_win = [&](const RowRef &rr, int w) -> Win {
+            Win v{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+            if (!rr.live) return v;
+            if (vec_scales) {
+                v.s = __ldg(reinterpret_cast<const uint4 *>(rr.s) + w);
+                v.b = __ldg(reinterpret_cast<const uint4 *>(rr.b) + w);
+            } else {
+                auto pair = [&](const uint16_t *q, int g0) {
+                    return (g0 < gpr ? (uint32_t)__ldg(q + g0) : 0u) | (g0 + 1 < gpr ? (uint32_t)__ldg(q + g0 + 1) << 16 : 0u);
+                };
+                v.s = make_uint4(pair(rr.s, 8 * w), pair(rr.s, 8 * w + 2), pair(rr.s, 8 * w + 4), pair(rr.s, 8 * w + 6));
+                v.b = make_uint4(pair(rr.b, 8 * w), pair(rr.b, 8 * w + 2), pair(rr.b, 8 * w + 4), pair(rr.b, 8 * w + 6));
+            }
+            return v;
+        };
+        RowRef cur = blockIdx.x < n_units ? row_of(blockIdx.x) : RowRef{nullptr, nullptr, false};
+        Win pf = load_win(cur, 0);  // the prefetched window
+        int it0 = 0;  // flat index of the unit's first stage
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, it0 += nk) {
+            const int un = u + gridDim.x;  // this CTA's next unit
+            const bool live = cur.live;
+            RowRef nxt{nullptr, nullptr, false};
+            bool nready = false;
+            Win w{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
             int win = -1;
             for (int kb = (g - it0) & 1; kb < nk; kb += 2) {
-                float sc, bi;
-                if (fast_scales) {
-                    if ((kb >> 3) != win) {
-                        win = kb >> 3;
-                        swin = *reinterpret_cast<const uint4 *>(s_row + 8 * win);
-                        bwin = *reinterpret_cast<const uint4 *>(b_row + 8 * win);
+                if ((kb >> 3) != win) {
+                    win = kb >> 3;
+                    w = pf;
+                    if (8 * (win + 1) < gpr) {
+                        pf = load_win(cur, win + 1);
+                    } else if (un < n_units) {
+                        nxt = row_of(un);
+                        pf = load_win(nxt, 0);
+                        nready = true;
                     }
-                    const int e = kb & 7;
-                    const uint32_t sw = e < 2 ? swin.x : e < 4 ? swin.y : e < 6 ? swin.z : swin.w;
-                    const uint32_t bw = e < 2 ? bwin.x : e < 4 ? bwin.y : e < 6 ? bwin.z : bwin.w;
-                    sc = (e & 1) ? bf16_hi(sw) : bf16_lo(sw);
-                    bi = (e & 1) ? bf16_hi(bw) : bf16_lo(bw);
-                } else {
-                    sc = bf16_bits_to_f32(s_row[kb]);
-                    bi = bf16_bits_to_f32(b_row[kb]);
                 }
+                const int e = kb & 7;
+                const uint32_t sw = e < 2 ? w.s.x : e < 4 ? w.s.y : e < 6 ? w.s.z : w.s.w;
+                const uint32_t bw = e < 2 ? w.b.x : e < 4 ? w.b.y : e < 6 ? w.b.z : w.b.w;
+                const float sc = (e & 1) ? bf16_hi(sw) : bf16_lo(sw);
+                const float bi = (e & 1) ? bf16_hi(bw) : bf16_lo(bw);
                 const int it = it0 + kb, s = it % STAGES, cs = it % CSTAGES;
                 const long long t_c = gg_now();
                 if (!mbar_wait(&cfull[cs], (it / CSTAGES) & 1, p.err, kErrTimeout)) { ok = false; break; }
@@ -339,39 +376,23 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sempty[sb]);
+            if (!ok) break;
+            if (!nready && un < n_units) {  // a unit with no stage of this group's parity
+                nxt = row_of(un);
+                pf = load_win(nxt, 0);
+            }
+            cur = nxt;
         }
         if (timed) gg_time(tkind, T_DQ_LOOP, t_loop);
     } else if (warp == 5) {
         // ---------------------------------------------------------------- code and scale producer
-        int it = 0, ul = 0;
+        int it = 0;
         const long long t_loop = gg_now();
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ul) {
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const Tile tl = p.tiles[u / RB];
-            const int rb = u % RB, sb = ul & 1;
+            const int rb = u % RB;
             const bool shared = tl.seg >= p.E;
             const int expert = shared ? 0 : tl.seg;
-            // scales and biases of the unit's rows
-            if (lane == 0) {
-                const long long t_s = gg_now();
-                ok = mbar_wait(&sempty[sb], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeout);
-                gg_time(tkind, T_CP_SCALE_EMPTY, t_s);
-                if (ok) {
-                    const int nrows = min(RPU, p.rows - rb * RPU);
-                    const uint32_t bytes = (uint32_t)(nrows * gpr * 2);
-                    mbar_arrive_expect_tx(&sfull[sb], bytes * 2 * NMAT);
-                    for (int mt = 0; mt < NMAT; ++mt) {
-                        const QView &W = p.w[mt + 2 * shared];
-                        const size_t r0 = (size_t)expert * W.rows + rb * RPU;
-                        uint8_t *dst = scale_buf + sb * kScaleBuf + (size_t)(mt * 2) * RPU * gpr * 2;
-                        bulk_load(dst, W.scales + r0 * gpr, bytes, &sfull[sb]);
-                        bulk_load(dst + RPU * gpr * 2, W.biases + r0 * gpr, bytes, &sfull[sb]);
-                    }
-                }
-            }
-            ok = __shfl_sync(kFull, ok, 0);
-            if (!ok) break;
             const int row0 = expert * p.w[(lane & 1) + 2 * shared].rows + rb * RPU;
             for (int kb = 0; kb < nk; ++kb, ++it) {
                 const int cs = it % CSTAGES;
@@ -393,7 +414,6 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             // copies still in flight must land before the CTA's shared memory is released
             for (int k = max(0, it - CSTAGES); k < it; ++k)
                 mbar_wait(&cfull[k % CSTAGES], (k / CSTAGES) & 1, p.err, kErrTimeout);
-            for (int k = max(0, ul - 1); k <= ul; ++k) mbar_wait(&sfull[k & 1], (k >> 1) & 1, p.err, kErrTimeout);
         }
     } else if (warp == 6) {
         // ---------------------------------------------------------------- B producer
@@ -416,59 +436,59 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                     const long long t_e = gg_now();
                     ok = mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.err, kErrTimeout);
                     gg_time(tkind, T_BP_EMPTY, t_e);
-                    if (ok) mbar_arrive_expect_tx(&bfull[s], (uint32_t)N * 128u);
+                    if (ok) mbar_arrive_expect_tx(&full[s], (uint32_t)N * 128u);
                 }
                 ok = __shfl_sync(kFull, ok, 0);
                 if (!ok) break;
-                if (box_mine) tma_load_2d(b_tile(s) + box_off * 128, bm, kb * BK, row0, &bfull[s]);
+                if (box_mine) tma_load_2d(b_tile(s) + box_off * 128, bm, kb * BK, row0, &full[s]);
             }
         }
         gg_time(tkind, T_BP_LOOP, t_loop);
         if (!ok && lane == 0)
             for (int k = max(0, it - STAGES); k < it; ++k)
-                mbar_wait(&bfull[k % STAGES], (k / STAGES) & 1, p.err, kErrTimeout);
+                mbar_wait(&full[k % STAGES], (k / STAGES) & 1, p.err, kErrTimeout);
     } else if (warp == 4) {
         // ---------------------------------------------------------------- MMA issue
+        // A shared-memory access by this thread (an mbarrier wait included) waits until its
+        // MMAs issued before it have read their operands, so the pipe idles for that latency at
+        // every wait. Gate/up (four stages) therefore waits for two stages at a time and then
+        // issues both stages' eight MMAs, committing each stage separately so its buffers are
+        // released as soon as they are read; down (three stages, eight per unit) measured faster
+        // waiting stage by stage.
         if (lane == 0) {
-            int it = 0;
-            SlotPlan plan;
+            int it = 0, ul = 0;
             const long long t_loop = gg_now();
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ul) {
                 const Tile tl = p.tiles[u / RB];
                 const int N = round16(tl.n);
-                uint32_t phase;
-                const int slot = plan.take(phase);
+                const int slot = ul & 1;  // accumulator slots alternate between units
+                const uint32_t phase = (uint32_t)(ul >> 1);
                 const long long t_a = gg_now();
                 if (!mbar_wait(&acce[slot], (phase & 1) ^ 1, p.err, kErrTimeout)) { ok = false; break; }
                 gg_time(tkind, T_MMA_ACC, t_a);
                 tc_fence_after();
                 const uint32_t d = tmem + slot * 256;
                 const uint32_t id = idesc_bf16_f32(BM, N);
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1;
-                    const long long t_b = gg_now();
-                    if (!mbar_wait(&bfull[s], ph, p.err, kErrTimeout)) {
-                        ok = false;
-                        break;
-                    }
+                constexpr int WG = MODE == MODE_GATE_UP ? 2 : 1;  // stages per wait
+                for (int kb = 0; kb < nk; kb += WG) {
+                    const int n2 = WG == 2 && kb + 1 < nk ? 2 : 1;
                     const long long t_f = gg_now();
-                    gg_time(tkind, T_MMA_B, t_b);
-                    if (!mbar_wait(&full[s], ph, p.err, kErrTimeout)) {
-                        ok = false;
-                        break;
-                    }
+                    for (int j = 0; j < n2 && ok; ++j)
+                        ok = mbar_wait(&full[(it + j) % STAGES], ((it + j) / STAGES) & 1, p.err, kErrTimeout);
+                    if (!ok) break;
                     gg_time(tkind, T_MMA_A, t_f);
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw128(smem_u32(a_tile(s)));
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(b_tile(s)));
                     const long long t_i = gg_now();
+                    for (int j = 0; j < n2; ++j, ++it) {
+                        const int s = it % STAGES;
+                        const uint64_t adesc = smem_desc_sw128(smem_u32(a_tile(s)));
+                        const uint64_t bdesc = smem_desc_sw128(smem_u32(b_tile(s)));
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) tc_mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, id, (kb | k) != 0);
-                    const long long t_c = gg_now();
+                        for (int k = 0; k < BK / 16; ++k)
+                            tc_mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, id, (kb + j) > 0 || k > 0);
+                        tc_commit(&empty[s]);
+                    }
                     gg_time(tkind, T_MMA_ISSUE, t_i);
-                    tc_commit(&empty[s]);
-                    gg_time(tkind, T_MMA_COMMIT, t_c);
                 }
                 if (!ok) break;
                 tc_commit(&accf[slot]);
