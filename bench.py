@@ -295,9 +295,10 @@ def run_ours(args):
             "gbs": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9,
             "hbm_frac": DECODE_BYTES_LAYER * LAYERS / (dec_us * 1e-6) / 1e9 / pk["hbm_gbs"]},
         "clocks": clk.summary(),
-        # per layer: router tiles, router GEMM, router select, scan, scatter, permute, gate_up, down,
-        # combine (+ next RMSNorm); one RMSNorm before the first layer (router norms are cached per layer)
-        "gpu_launches": args.steps * (LAYERS * 9 + 1),
+        # per layer: router tiles, router GEMM, router select, scan, scatter + row permutation, gate_up,
+        # down, combine (+ next RMSNorm); one RMSNorm before the first layer (router norms are cached
+        # per layer)
+        "gpu_launches": args.steps * (LAYERS * 8 + 1),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -831,14 +831,14 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
                                           b.seg_off, b.tiles, b.n_tiles, b.max_tiles, c->d_err);
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
-    scatter_routes_kernel<<<b.nblocks, kScatterWarps * 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos);
+    // ... and the token rows copied into that order for the gate/up B operand
+    scatter_permute_kernel<<<b.nblocks, kScatterWarps * 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm,
+                                                                     b.route_pos, x, D, b.xp);
     c->last_perm = b.perm;
     c->last_seg_off = b.seg_off;
     c->last_seg_count = b.seg_count;
     c->last_routes_T = T;
     c->last_routes_E = E;
-    // token rows in expert order for the gate/up B operand (timed with the scatter)
-    permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(x, b.perm, b.seg_off + E, D, b.xp);
     if (profile) stage_mark(c, S_GATE_UP);
     // 5. grouped gate/up + SwiGLU (routed experts and the shared expert)
     const int grid = c->sms;

@@ -48,12 +48,16 @@ constexpr int MODE_GATE_UP = 0, MODE_DOWN = 1;
 constexpr int BM = 128;          // A rows per unit (one MMA M)
 constexpr int BN = 256;          // max tokens per unit (one 256-column accumulator slot)
 constexpr int BK = 64;           // K per pipeline stage: 128-byte bf16 rows, one group of 64 codes
-// Pipeline depths per mode (measured): gate/up units run 32 stages and gain from a fourth A/B
-// stage; down units run 8 and gain more from a fourth code slot. Both fit 227 KB.
+// Pipeline depths. The two dequantiser groups take alternate stages, so a code slot must belong
+// to one group: an odd number of code slots would let a group's parity wait on a slot match the
+// fill before the one it waits for, while the other group's fill is still in flight. Four code
+// slots and three A/B stages fit 227 KB (four A/B stages would leave room for two code slots
+// only, measured slower).
 template <int MODE>
-__host__ __device__ constexpr int stages() { return MODE == 0 ? 4 : 3; }
+__host__ __device__ constexpr int stages() { return 3; }
 template <int MODE>
-__host__ __device__ constexpr int cstages() { return MODE == 0 ? 3 : 4; }
+__host__ __device__ constexpr int cstages() { return 4; }
+static_assert(cstages<0>() % 2 == 0 && cstages<1>() % 2 == 0, "each code slot belongs to one dequantiser group");
 constexpr int THREADS = 512;
 constexpr int kA = BM * 128;     // bytes of one A stage tile (bf16)
 constexpr int kB = BN * 128;     // bytes of one B stage tile (bf16)
@@ -449,12 +453,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 mbar_wait(&full[k % STAGES], (k / STAGES) & 1, p.err, kErrTimeout);
     } else if (warp == 4) {
         // ---------------------------------------------------------------- MMA issue
-        // A shared-memory access by this thread (an mbarrier wait included) waits until its
-        // MMAs issued before it have read their operands, so the pipe idles for that latency at
-        // every wait. Gate/up (four stages) therefore waits for two stages at a time and then
-        // issues both stages' eight MMAs, committing each stage separately so its buffers are
-        // released as soon as they are read; down (three stages, eight per unit) measured faster
-        // waiting stage by stage.
+        // A shared-memory access by this thread (an mbarrier wait included) waits until the MMAs
+        // it issued before have read their operands, so each stage's wait costs the pipe that
+        // latency. With three stages, waiting for two stages at a time measured slower (the
+        // producers lose a stage of lead), so the loop waits stage by stage (WG = 1).
         if (lane == 0) {
             int it = 0, ul = 0;
             const long long t_loop = gg_now();
@@ -469,7 +471,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 tc_fence_after();
                 const uint32_t d = tmem + slot * 256;
                 const uint32_t id = idesc_bf16_f32(BM, N);
-                constexpr int WG = MODE == MODE_GATE_UP ? 2 : 1;  // stages per wait
+                constexpr int WG = 1;  // stages per wait
                 for (int kb = 0; kb < nk; kb += WG) {
                     const int n2 = WG == 2 && kb + 1 < nk ? 2 : 1;
                     const long long t_f = gg_now();
@@ -558,6 +560,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                     fence_proxy_async_smem();
                     __syncwarp();
                     const int d0 = rb * 128 + 32 * q;
+                    // every chunk commits one bulk group (an empty one for plain stores), so that
+                    // bulk_wait_read<1> above always frees the buffer of the chunk before last
                     if (tl.n - c >= 16) {
                         if (lane == 0) {
                             tma_store_2d(&p.ymap, sb, d0, tl.p0 + c);
@@ -572,6 +576,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                                 *reinterpret_cast<uint4 *>(p.out + (size_t)(tl.p0 + n) * p.rows + d) =
                                     *reinterpret_cast<const uint4 *>(sb + tk * 64 + part * 16);
                         }
+                        if (lane == 0) bulk_commit();
                     }
                 }
             }
@@ -948,13 +953,14 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
                     fence_proxy_async_smem();
                     __syncwarp();
                     const int d0 = rb * 128 + 32 * q;
-                    if (d0 < p.rows) {
-                        if (tl.n - c >= 16) {
-                            if (lane == 0) {
-                                tma_store_2d(&p.ymap, sb, d0, tl.p0 + c);
-                                bulk_commit();
-                            }
-                        } else {
+                    // one bulk group per chunk (empty for plain stores or dead rows), as above
+                    if (d0 < p.rows && tl.n - c >= 16) {
+                        if (lane == 0) {
+                            tma_store_2d(&p.ymap, sb, d0, tl.p0 + c);
+                            bulk_commit();
+                        }
+                    } else {
+                        if (d0 < p.rows) {
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {
                                 const int ck = lane + 32 * h, tk = ck >> 2, part = ck & 3, n = c + tk;
@@ -964,6 +970,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_pair_kernel(const __g
                                         *reinterpret_cast<const uint4 *>(sb + tk * 64 + part * 16);
                             }
                         }
+                        if (lane == 0) bulk_commit();
                     }
                 }
             }

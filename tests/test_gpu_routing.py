@@ -139,3 +139,23 @@ def test_bench_stack_teacher_forced_40_layers(ctx):
             _oracle_rows(O.Layer(BENCH_SEED, layer=l, bits=8), ht[l], y, ids, rows)
     for G in layers:
         G.close()
+
+
+def test_first_call_of_a_fresh_context_equals_later_calls():
+    # A fresh context's first call runs on a freshly allocated workspace with cold caches; its
+    # outputs must equal the next calls' bit for bit (a race that lets a later store overwrite an
+    # expert-row chunk still being copied out would show up here first). Several fresh contexts,
+    # the benchmark's 8K-token 8-bit layer.
+    x = O.gen_bf16(BENCH_SEED, O.ACT_STREAM, 8192 * 2048).reshape(8192, 2048)
+    ref = None
+    for _ in range(4):
+        c = di.Context(resident=0)
+        G = di.MoeLayer.generated(c, BENCH_SEED, 0, bits=8)
+        first = di.moe_block(G, x, di.PATH_GROUPED)[0]
+        second = di.moe_block(G, x, di.PATH_GROUPED)[0]
+        assert np.array_equal(first, second)
+        if ref is None:
+            ref = first
+        assert np.array_equal(first, ref)
+        G.close()
+        c.close()
