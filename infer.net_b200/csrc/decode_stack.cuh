@@ -278,6 +278,23 @@ __device__ __forceinline__ float router_dot_h(const RouterRaw &r, const float4 *
 
 __device__ __forceinline__ float acc_value(unsigned long long v) { return __ll2float_rn((long long)v) * kAccInv; }
 
+// Per-layer timeline of two CTAs (CTA 0, a routed unit, and CTA 143, a shared-expert unit),
+// compiled in only with -DDI_DECODE_TIMELINE (a profiling build; read by di_debug_decode_timeline):
+// %globaltimer at the layer's start (0), after the previous layer's output is complete (1), h
+// ready (2), this CTA's logits published (3), the top-8 known (4), the copies requested (5), the
+// first gate/up group landed (6), every copy landed (7), act complete (8), the output vector
+// complete (9), and the reduction and arrival done (10).
+constexpr int kTlEvents = 11, kTlLayers = 64;
+#ifdef DI_DECODE_TIMELINE
+__device__ unsigned long long g_ds_tl[2][kTlLayers][kTlEvents];
+__device__ __forceinline__ void ds_mark(int ev, int l) {
+    const int c = blockIdx.x == 0 ? 0 : blockIdx.x == kUnits - 1 ? 1 : -1;
+    if (c >= 0 && threadIdx.x == 0 && l < kTlLayers) g_ds_tl[c][l][ev] = global_ns();
+}
+#else
+__device__ __forceinline__ void ds_mark(int, int) {}
+#endif
+
 // The hidden size is a template parameter (512, 1024 or 2048) and I = kI: with the geometry known
 // to the compiler, the loop-invariant state fits in registers (a spill would go to L2 here: the
 // shared-memory carve-out leaves almost no L1).
@@ -339,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
     for (int l = 0; l < p.n_layers; ++l) {
         const StackLayer &Ly = *reinterpret_cast<const StackLayer *>(sm + f.desc_off + (l & 1) * kDescBytes);
         const uint32_t gen = base + (uint32_t)l + 1;
+        ds_mark(0, l);
         ph = (uint32_t)l & 1u;
         // copy k of the unit: k < 24 field k%6 of gate/up group k/6, else down-column box k-24
         auto issue_copy = [&](int k, int e) {
@@ -418,6 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
             }
             __syncthreads();
             if (*abort_s) break;
+            ds_mark(1, l);
             const unsigned long long *y = p.acc + (size_t)((l - 1) & 1) * kAccCopies * D;
             unsigned long long yv[D / kThreads][kAccCopies];
 #pragma unroll
@@ -456,6 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         }
         cp_async_wait<0>();  // the router rows
         __syncthreads();
+        ds_mark(2, l);
 
         // ---- S2: router logits of this CTA's rows (row E: the shared expert's gate logit)
         if (my_row < r_hi) {
@@ -467,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         }
         __syncthreads();
         if (tid == 0) atomicAdd(p.ctr_logit, 1u);
+        ds_mark(3, l);
 
         // ---- S3: all logits -> the same top-8 in every CTA; word 8 of every lane is the gate logit
         if (warp == 0) {
@@ -529,12 +550,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
         }
         __syncthreads();
         if (*abort_s) break;
+        ds_mark(4, l);
         // every CTA has read y_{l-1} (before its logits): clear this CTA's slice of the buffer that
         // layer l + 1 adds into
         if (tid < kAccCopies * nd) p.acc[(size_t)(((l + 1) & 1) * kAccCopies + tid / nd) * D + d_lo + tid % nd] = 0ull;
         if (has_unit) {
             const int e = routed_unit ? ids_s[uj] : 0;
             if (routed_unit && my_k < kCopies) issue_copy(my_k, e);
+            ds_mark(5, l);
             // the scale (even lane) or bias (odd lane) of the unit's group of down rows
             // (tid >> 1) + 256 a, requested now and used in S5 (they stream behind the copies)
             uint32_t dsb[D / 256];
@@ -597,9 +620,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
 #pragma unroll 1
             for (int g = 0; g < kGroups; ++g) {
                 ok = mbar_wait(&bar[g], ph, p.err, kErrTimeout) && ok;
+                if (g == 0) ds_mark(6, l);
                 if (ok) group_partials(g);
             }
             ok = mbar_wait(&bar[kGroups], ph, p.err, kErrTimeout) && ok;
+            ds_mark(7, l);
             if (!ok) *abort_s = 1;
             __syncthreads();
             if (*abort_s) break;
@@ -612,6 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
                 if (!(tid & 1)) act_s[tid >> 1] = silu_ref(sv) * u;
             }
             __syncthreads();  // the unit's act values are complete
+            ds_mark(8, l);
 
             // ---- S5: lane pair (row r, half hf): 16 columns of down row r against act, pairs summed;
             // c_slot * sum rounded to the accumulator's grid into the unit's output vector, which one
@@ -649,6 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
             }
             fence_proxy_async_smem();  // the vector, for the copy engine
             if (range) atomicOr(p.err, kErrRange);
+            ds_mark(9, l);
             armed = false;  // every copy of the layer has landed
         }
         __syncthreads();  // the regions are reused by the next layer's copies; the vector is complete
@@ -662,6 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const StackPa
             }
             red_release_gpu_add(p.ctr_y, 1u);  // after this CTA's additions and accumulator clears
         }
+        ds_mark(10, l);
     }
     cp_async_wait<0>();  // an abandoned layer may still be copying its router rows
     __syncthreads();

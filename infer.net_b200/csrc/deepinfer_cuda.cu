@@ -2399,6 +2399,13 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
     return 0;
 }
 
+#ifdef DI_DECODE_TIMELINE
+// Profiling build only (-DDI_DECODE_TIMELINE): the decode stack kernel's per-layer timeline of two
+// CTAs, [2][ds::kTlLayers][ds::kTlEvents] %globaltimer values of the last call.
+API int di_debug_decode_timeline(unsigned long long *out) {
+    return cudaMemcpyFromSymbol(out, ds::g_ds_tl, sizeof(ds::g_ds_tl)) == cudaSuccess ? 0 : -1;
+}
+#endif
 #ifdef DI_GG_TIMING
 // Profiling build only (-DDI_GG_TIMING): the grouped GEMMs' per-role cycle counters
 // [4 kinds][256 CTAs][gg::T_COUNT], copied to out and cleared when reset != 0.
