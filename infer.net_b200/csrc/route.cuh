@@ -790,10 +790,11 @@ __global__ void __launch_bounds__(256) router_row_norms_kernel(QView R, int E, i
     }
 }
 
-// Work tiles of the approximate-logit GEMM: segment 0, 256 tokens each.
-__global__ void router_tiles_kernel(int T, Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles) {
-    const int n = (T + 255) / 256;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) tiles[i] = Tile{0, i * 256, min(256, T - i * 256)};
+// Work tiles of a one-segment grouped GEMM (the approximate-logit GEMM, dense projections): segment
+// 0, `rows` tokens each (at most 256).
+__global__ void router_tiles_kernel(int T, int rows, Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles) {
+    const int n = (T + rows - 1) / rows;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) tiles[i] = Tile{0, i * rows, min(rows, T - i * rows)};
     if (threadIdx.x == 0) *n_tiles = n;
 }
 
