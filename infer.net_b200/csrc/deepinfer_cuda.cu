@@ -859,7 +859,7 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_COMBINE);
     // 7. combine (stacks: fused with the residual update and the next layer's RMSNorm)
     if (resid && !y) {
-        combine_norm_kernel<<<T, 256, 0, st>>>(b.yr, b.route_pos, b.ys, b.gate, probs, D, resid, next_norm, eps, next_h,
+        combine_norm_kernel<128><<<T, 128, 0, st>>>(b.yr, b.route_pos, b.ys, b.gate, probs, D, resid, next_norm, eps, next_h,
                                                next_trace, c->d_err);
     } else {
         const size_t n = (size_t)T * (D / 8);
