@@ -835,8 +835,9 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
     // ... and the token rows copied into that order for the gate/up B operand
-    scatter_permute_kernel<<<b.nblocks, kScatterWarps * 32, 0, st>>>(ids, T, E, b.block_base, b.seg_off, b.perm,
-                                                                     b.route_pos, x, D, b.xp);
+    // four CTAs per 64-token block share its row copies (measured: 2.26 ms/step against 2.56 for one)
+    scatter_permute_kernel<4><<<b.nblocks * 4, kScatterWarps * 32, 0, st>>>(
+        ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos, x, D, b.xp);
     c->last_perm = b.perm;
     c->last_seg_off = b.seg_off;
     c->last_seg_count = b.seg_count;

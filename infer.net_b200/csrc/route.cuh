@@ -558,9 +558,12 @@ scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32
 }
 
 // scatter_routes_kernel fused with the copy of the block's token rows into expert order: after
-// the positions are known, each warp copies its 4 tokens' rows (read once) to their 8 positions
-// each, so the permuted rows are written without a second pass over the permutation.
-// D % 256 == 0 and D <= 8192.
+// the positions are known, each warp copies its tokens' rows (read once) to their 8 positions
+// each, so the permuted rows are written without a second pass over the permutation. SPLIT CTAs
+// share a block of 64 tokens: each recomputes the block's positions (cheap), the first writes the
+// permutation, and each copies the rows of every SPLIT-th token of its warps, so the copies spread
+// over SPLIT times as many CTAs. D % 256 == 0 and D <= 8192.
+template <int SPLIT>
 __global__ void __launch_bounds__(kScatterWarps * 32)
 scatter_permute_kernel(const int32_t *__restrict__ ids, int T, int E, const int32_t *__restrict__ block_base,
                        const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route,
@@ -570,7 +573,8 @@ scatter_permute_kernel(const int32_t *__restrict__ ids, int T, int E, const int3
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int i = threadIdx.x; i < kScatterWarps * kMaxBuckets; i += blockDim.x) (&cnt[0][0])[i] = 0;
     __syncthreads();
-    const int r = blockIdx.x * topk::TOK_PER_CTA * 8 + warp * 32 + lane;
+    const int blk = blockIdx.x / SPLIT, part = blockIdx.x % SPLIT;
+    const int r = blk * topk::TOK_PER_CTA * 8 + warp * 32 + lane;
     const bool valid = r < T * 8;
     const int e = valid ? ids[r] : -1 - lane;
     const unsigned peers = __match_any_sync(kFull, e);
@@ -589,14 +593,16 @@ scatter_permute_kernel(const int32_t *__restrict__ ids, int T, int E, const int3
     __syncthreads();
     int pos = 0;
     if (valid) {
-        pos = seg_off[e] + block_base[(size_t)blockIdx.x * E + e] + cnt[warp][e] + rank;
-        perm_route[pos] = r;
-        route_pos[r] = pos;
+        pos = seg_off[e] + block_base[(size_t)blk * E + e] + cnt[warp][e] + rank;
+        if (part == 0) {
+            perm_route[pos] = r;
+            route_pos[r] = pos;
+        }
     }
     // rows: lane l's route is token (r >> 3), slot (l & 7); the warp's 4 tokens
     const int chunks = D / 8;  // 16-byte chunks per row
-    for (int k = 0; k < 4; ++k) {
-        const int t = (blockIdx.x * topk::TOK_PER_CTA * 8 + warp * 32) / 8 + k;
+    for (int k = part; k < 4; k += SPLIT) {
+        const int t = (blk * topk::TOK_PER_CTA * 8 + warp * 32) / 8 + k;
         if (t >= T) break;
         const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * D);
         for (int c0 = 0; c0 < chunks; c0 += 256) {
