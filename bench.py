@@ -380,9 +380,9 @@ def run_expert_parallel(args, di, torch, rank, local, world):
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": Tl * D * 4 * world + LAYERS * D * 4 * world,
                 "d2h_bytes_per_step": Tl * D * 4 * world},
         "clocks": clk.summary(),
-        # per layer: router tiles, router GEMM, router select, layout, dispatch, receive, scan, scatter,
-        # permute, gate_up, down, partial-row send, combine; one RMSNorm before the first layer
-        "gpu_launches": args.steps * (LAYERS * 13 + 1),
+        # per layer: router tiles, router GEMM, router select, layout, dispatch, receive, scan, scatter +
+        # row permutation, gate_up, down, partial-row send, combine; one RMSNorm before the first layer
+        "gpu_launches": args.steps * (LAYERS * 12 + 1),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

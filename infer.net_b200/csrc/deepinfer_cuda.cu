@@ -837,7 +837,7 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     // ... and the token rows copied into that order for the gate/up B operand
     // four CTAs per 64-token block share its row copies (measured: 2.26 ms/step against 2.56 for one)
     scatter_permute_kernel<4><<<b.nblocks * 4, kScatterWarps * 32, 0, st>>>(
-        ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos, x, D, b.xp);
+        ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos, x, D, b.xp, E);
     c->last_perm = b.perm;
     c->last_seg_off = b.seg_off;
     c->last_seg_count = b.seg_count;
@@ -2348,8 +2348,9 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                                                        c->d_err);
             scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, RC, T, gg::BN, rbb, sgc, sgo, tiles, nt,
                                                   max_tiles, c->d_err);
-            scatter_routes_kernel<<<nbr, kScatterWarps * 32, 0, st>>>(il, RC, El + 1, rbb, sgo, perm, rpos);
-            permute_rows_kernel<<<c->sms * 4, 256, 0, st>>>(my_rx, perm, sgo + El, D, xp);
+            // stable scatter of the local routes and their received rows copied into expert order
+            scatter_permute_kernel<4><<<nbr * 4, kScatterWarps * 32, 0, st>>>(il, RC, El + 1, rbb, sgo, perm, rpos,
+                                                                              my_rx, D, xp, El);
             // 4. local experts over the received rows, shared expert over the local rows
             launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, Gm, U, SG, SU, xp, 8 * RC, h, T, perm,
                                                             tiles, nt, 8 * RC, 0, D, I, El + 1, act, 8 * RC + T,

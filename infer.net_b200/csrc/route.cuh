@@ -568,7 +568,7 @@ __global__ void __launch_bounds__(kScatterWarps * 32)
 scatter_permute_kernel(const int32_t *__restrict__ ids, int T, int E, const int32_t *__restrict__ block_base,
                        const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route,
                        int32_t *__restrict__ route_pos, const uint16_t *__restrict__ x, int D,
-                       uint16_t *__restrict__ xp) {
+                       uint16_t *__restrict__ xp, int copy_buckets) {
     __shared__ int32_t cnt[kScatterWarps][kMaxBuckets];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int i = threadIdx.x; i < kScatterWarps * kMaxBuckets; i += blockDim.x) (&cnt[0][0])[i] = 0;
@@ -604,6 +604,11 @@ scatter_permute_kernel(const int32_t *__restrict__ ids, int T, int E, const int3
     for (int k = part; k < 4; k += SPLIT) {
         const int t = (blk * topk::TOK_PER_CTA * 8 + warp * 32) / 8 + k;
         if (t >= T) break;
+        // the token's routes whose rows are copied: buckets below copy_buckets (the expert-parallel
+        // path leaves out the routes of other GPUs' experts)
+        const unsigned live = __ballot_sync(kFull, valid && e < copy_buckets);
+        const unsigned mine = (live >> (k * 8)) & 0xffu;
+        if (!mine) continue;
         const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * D);
         for (int c0 = 0; c0 < chunks; c0 += 256) {
             uint4 v[8];
@@ -615,6 +620,7 @@ scatter_permute_kernel(const int32_t *__restrict__ ids, int T, int E, const int3
 #pragma unroll
             for (int sl = 0; sl < 8; ++sl) {
                 const int ps = __shfl_sync(kFull, pos, k * 8 + sl);
+                if (!((mine >> sl) & 1u)) continue;
                 uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)ps * D);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
