@@ -346,6 +346,14 @@ def run_expert_parallel(args, di, torch, rank, local, world):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item()) / args.steps
     value = TOKENS / (ms / 1e3)
+    # one profiled call after the timed ones: this rank's per-stage milliseconds over the 40 layers
+    x.copy_(x0)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ep.stack(layers, norms, x, Tl, 1e-6, di.DEVICE_IO | di.PROFILE)
+    prof = list(ctx.last_profile().values())
+    ep_stage_names = ["route", "dispatch", "receive_scan", "scatter", "gate_up", "down", "send", "combine"]
+    ep_stages = dict(zip(ep_stage_names, prof[:len(ep_stage_names)]))
     # end to end through the host-buffer API
     xh = x0.cpu().pin_memory()
     xo = torch.empty_like(xh).pin_memory()
@@ -377,6 +385,7 @@ def run_expert_parallel(args, di, torch, rank, local, world):
                      "unit": "TFLOP/s per GPU", "frac": total_flops / (ms * 1e-3) / (world * pk["bf16_tflops"] * 1e12),
                      "traffic": None, "peak_source": pk["source"] + " burst bf16"},
         "cpu_baseline": None,
+        "stage_ms_rank0": ep_stages,
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": Tl * D * 4 * world + LAYERS * D * 4 * world,
                 "d2h_bytes_per_step": Tl * D * 4 * world},
         "clocks": clk.summary(),

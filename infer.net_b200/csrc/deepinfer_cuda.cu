@@ -2200,7 +2200,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                         int tokens, uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error,
                         int capacity) {
     if (!live_ep(ep_) || !layers || n_layers < 1 || n_layers > 1024 || !norms || !x || tokens < 1 ||
-        tokens > 65536 || !(eps > 0.0f) || (flags & ~DI_MOE_DEVICE_IO)) {
+        tokens > 65536 || !(eps > 0.0f) || (flags & ~(DI_MOE_DEVICE_IO | DI_MOE_PROFILE))) {
         set_error(error, capacity, "Invalid expert-parallel stack arguments");
         return -1;
     }
@@ -2308,6 +2308,19 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         Tile *rtiles = at<Tile>(c, o_rt);
         int32_t *rnt = at<int32_t>(c, o_rnt);
         float *wf = at<float>(c, o_wf);
+        // DI_MOE_PROFILE: per-layer events at the stage boundaries [route, dispatch, receive + scan,
+        // scatter, gate_up, down, partial-row send, combine], summed over the layers
+        const bool profile = (flags & DI_MOE_PROFILE) != 0;
+        constexpr int kEpStages = 8;
+        const size_t need_events = profile ? (size_t)n_layers * (kEpStages + 1) : 0;
+        while (c->layer_events.size() < need_events) {
+            cudaEvent_t e;
+            CK(cudaEventCreate(&e));
+            c->layer_events.push_back(e);
+        }
+        auto mark = [&](int l, int sidx) {
+            if (profile) CK(cudaEventRecord(c->layer_events[(size_t)l * (kEpStages + 1) + sidx], st));
+        };
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st));
         CK(cudaEventRecord(c->ev_start, st));
         if (!dev_io) {
@@ -2316,6 +2329,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         }
         const int grid = c->sms;
         for (int l = 0; l < n_layers; ++l) {
+            mark(l, 0);
             Layer *L = static_cast<Layer *>(layers[l]);
             const QView R = L->m[0]->view(), Gm = L->m[1]->view(), U = L->m[2]->view(), Dm = L->m[3]->view();
             const QView SG = L->m[4]->view(), SU = L->m[5]->view(), SD = L->m[6]->view(), SR = L->m[7]->view();
@@ -2339,33 +2353,41 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             if (dit)
                 CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, st));
             // 2. one row per (token, destination rank), written into the destinations over NVLink
+            mark(l, 1);
             ep_layout_kernel<<<1, 1024, 0, st>>>(ids, T, El, G, sidx, sc, so);
             ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
                                                                                       cap, sidx, sc, peers,
                                                                                       my_sync + 3 * G + 1);
             // 3. the rows every rank sent here -> local routes, expert segments, GEMM tiles
+            mark(l, 2);
             ep_recv_routes_kernel<<<nbr, 256, 0, st>>>(my_meta, my_sync, target, G, cap, L->E_off, El, peers, il, rbc,
                                                        c->d_err);
             scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, RC, T, gg::BN, rbb, sgc, sgo, tiles, nt,
                                                   max_tiles, c->d_err);
             // stable scatter of the local routes and their received rows copied into expert order
+            mark(l, 3);
             scatter_permute_kernel<4><<<nbr * 4, kScatterWarps * 32, 0, st>>>(il, RC, El + 1, rbb, sgo, perm, rpos,
                                                                               my_rx, D, xp, El);
             // 4. local experts over the received rows, shared expert over the local rows
+            mark(l, 4);
             launch_grouped<gg::MODE_GATE_UP>(grouped_params(gg::MODE_GATE_UP, Gm, U, SG, SU, xp, 8 * RC, h, T, perm,
                                                             tiles, nt, 8 * RC, 0, D, I, El + 1, act, 8 * RC + T,
                                                             c->d_err),
                                              L->bits, grid, st);
+            mark(l, 5);
             launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, Dm, Dm, SD, SD, act, 8 * RC + T, nullptr, 0,
                                                          perm, tiles, nt, 8 * RC, 0, I, D, El + 1, y, 8 * RC + T,
                                                          c->d_err),
                                           L->bits, grid, st);
             // 5. partial row sums straight back into the token owners, then the owner's combine
+            mark(l, 6);
             ep_reduce_send_kernel<<<std::min((RC + 7) / 8, 8 * c->sms), 256, 0, st>>>(
                 y, rpos, il, my_meta, my_sync, G, rank, cap, D, El, peers, my_sync + 3 * G + 2, c->d_err);
+            mark(l, 7);
             ep_combine_kernel<<<T, 256, 0, st>>>(my_back, sidx, G, cap, my_sync, target, peers, y + (size_t)8 * RC * D,
                                                  gate, D, dx, l + 1 < n_layers ? dn + (size_t)(l + 1) * D : nullptr,
                                                  eps, h, c->d_err);
+            mark(l, 8);
             if (launch_check(error, capacity)) {
                 ep->broken = true;  // the ranks' arrival counts no longer agree
                 return -1;
@@ -2394,6 +2416,18 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         float t = 0;
         CK(cudaEventElapsedTime(&t, c->ev_start, c->ev_stop));
         if (ms) *ms = t;
+        if (profile) {
+            for (int k = 0; k < kProfileSlots; ++k) c->last_stage_ms[k] = 0;
+            for (int l = 0; l < n_layers; ++l) {
+                cudaEvent_t *ev = &c->layer_events[(size_t)l * (kEpStages + 1)];
+                for (int k = 0; k < kEpStages; ++k) {
+                    float st_ms = 0;
+                    CK(cudaEventElapsedTime(&st_ms, ev[k], ev[k + 1]));
+                    c->last_stage_ms[k] += st_ms;
+                }
+            }
+            c->have_profile = true;
+        }
     } catch (const CudaFail &f) {
         set_error(error, capacity, "%s", f.what.c_str());
         return -1;
