@@ -2277,8 +2277,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         const size_t o_x = dev_io ? 0 : cv.take<float>((size_t)T * D), o_n = dev_io ? 0 : cv.take<float>((size_t)n_layers * D);
         const size_t o_h = cv.take<uint16_t>((size_t)T * D), o_lg = cv.take<float>((size_t)T * E);
         const size_t o_ids = cv.take<int32_t>((size_t)T * 8), o_p = cv.take<float>((size_t)T * 8), o_g = cv.take<float>(T);
-        const size_t o_bc = cv.take<int32_t>((size_t)nb_l * E), o_sidx = cv.take<int32_t>((size_t)T * G);
-        const size_t o_sc = cv.take<int32_t>(kMaxRanks), o_so = cv.take<int32_t>(kMaxRanks);
+        const size_t o_bc = cv.take<int32_t>((size_t)nb_l * E);
         const size_t o_il = cv.take<int32_t>((size_t)RC * 8 + 8), o_rbc = cv.take<int32_t>((size_t)(nbr + 1) * (El + 1));
         const size_t o_rbb = cv.take<int32_t>((size_t)(nbr + 1) * (El + 1)), o_sgc = cv.take<int32_t>(El + 2);
         const size_t o_sgo = cv.take<int32_t>(El + 2), o_t = cv.take<Tile>(max_tiles), o_nt = cv.take<int32_t>(1);
@@ -2298,8 +2297,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         uint16_t *xp = at<uint16_t>(c, o_xp);
         int32_t *rpos = at<int32_t>(c, o_rp);
         float *logits = at<float>(c, o_lg), *probs = at<float>(c, o_p), *gate = at<float>(c, o_g);
-        int32_t *ids = at<int32_t>(c, o_ids), *bc = at<int32_t>(c, o_bc), *sidx = at<int32_t>(c, o_sidx);
-        int32_t *sc = at<int32_t>(c, o_sc), *so = at<int32_t>(c, o_so);
+        int32_t *ids = at<int32_t>(c, o_ids), *bc = at<int32_t>(c, o_bc);
         int32_t *il = at<int32_t>(c, o_il), *rbc = at<int32_t>(c, o_rbc), *rbb = at<int32_t>(c, o_rbb);
         int32_t *sgc = at<int32_t>(c, o_sgc), *sgo = at<int32_t>(c, o_sgo), *nt = at<int32_t>(c, o_nt);
         int32_t *perm = at<int32_t>(c, o_pm);
@@ -2318,8 +2316,8 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             CK(cudaEventCreate(&e));
             c->layer_events.push_back(e);
         }
-        auto mark = [&](int l, int sidx) {
-            if (profile) CK(cudaEventRecord(c->layer_events[(size_t)l * (kEpStages + 1) + sidx], st));
+        auto mark = [&](int l, int stage) {
+            if (profile) CK(cudaEventRecord(c->layer_events[(size_t)l * (kEpStages + 1) + stage], st));
         };
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st));
         CK(cudaEventRecord(c->ev_start, st));
@@ -2354,9 +2352,8 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                 CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, st));
             // 2. one row per (token, destination rank), written into the destinations over NVLink
             mark(l, 1);
-            ep_layout_kernel<<<1, 1024, 0, st>>>(ids, T, El, G, sidx, sc, so);
             ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
-                                                                                      cap, sidx, sc, peers,
+                                                                                      cap, El, peers,
                                                                                       my_sync + 3 * G + 1);
             // 3. the rows every rank sent here -> local routes, expert segments, GEMM tiles
             mark(l, 2);
@@ -2384,7 +2381,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             ep_reduce_send_kernel<<<std::min((RC + 7) / 8, 8 * c->sms), 256, 0, st>>>(
                 y, rpos, il, my_meta, my_sync, G, rank, cap, D, El, peers, my_sync + 3 * G + 2, c->d_err);
             mark(l, 7);
-            ep_combine_kernel<<<T, 256, 0, st>>>(my_back, sidx, G, cap, my_sync, target, peers, y + (size_t)8 * RC * D,
+            ep_combine_kernel<<<T, 256, 0, st>>>(my_back, ids, El, G, cap, my_sync, target, peers, y + (size_t)8 * RC * D,
                                                  gate, D, dx, l + 1 < n_layers ? dn + (size_t)(l + 1) * D : nullptr,
                                                  eps, h, c->d_err);
             mark(l, 8);

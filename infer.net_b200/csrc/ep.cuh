@@ -24,78 +24,16 @@ struct RowMeta {
     float probs[8];
 };
 
-// Single CTA of 1024 threads: for every local token t and GPU d, send_idx[t*G + d] = position
-// of t among the tokens sent to d (or -1), send_count[d], send_off[d] (exclusive scan). Thread i
-// owns a contiguous token range; the per-destination exclusive scan over threads is a warp
-// shuffle scan plus a scan of the 32 warp totals.
-__global__ void __launch_bounds__(1024)
-ep_layout_kernel(const int32_t *__restrict__ ids, int T, int E_l, int G, int32_t *__restrict__ send_idx,
-                 int32_t *__restrict__ send_count, int32_t *__restrict__ send_off) {
-    __shared__ int32_t wsum[32][kMaxRanks];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int per = (T + 1023) / 1024, t0 = min(tid * per, T), t1 = min(t0 + per, T);
-    int cnt[kMaxRanks] = {};
-    for (int t = t0; t < t1; ++t) {
-        uint32_t mask = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mask |= 1u << (ids[(size_t)t * 8 + j] / E_l);
-#pragma unroll
-        for (int d = 0; d < kMaxRanks; ++d) cnt[d] += (mask >> d) & 1u;
-    }
-    int pos[kMaxRanks];
-#pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) {
-        int v = cnt[d];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int u = __shfl_up_sync(kFull, v, o);
-            if (lane >= o) v += u;
-        }
-        pos[d] = v - cnt[d];  // exclusive within the warp
-        if (lane == 31) wsum[warp][d] = v;
-    }
-    __syncthreads();
-    if (warp == 0) {
-#pragma unroll
-        for (int d = 0; d < kMaxRanks; ++d) {
-            const int w = wsum[lane][d];
-            int v = w;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int u = __shfl_up_sync(kFull, v, o);
-                if (lane >= o) v += u;
-            }
-            wsum[lane][d] = v - w;  // exclusive over warps
-            if (lane == 31 && d < G) send_count[d] = v;
-        }
-    }
-    __syncthreads();
-    if (tid == 0) {
-        int run = 0;
-        for (int d = 0; d < G; ++d) {
-            send_off[d] = run;
-            run += send_count[d];
-        }
-    }
-#pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) pos[d] += wsum[warp][d];
-    for (int t = t0; t < t1; ++t) {
-        uint32_t mask = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mask |= 1u << (ids[(size_t)t * 8 + j] / E_l);
-#pragma unroll
-        for (int d = 0; d < kMaxRanks; ++d)
-            if (d < G) send_idx[(size_t)t * G + d] = ((mask >> d) & 1u) ? pos[d]++ : -1;
-    }
-}
-
 // Symmetric buffers of one rank, mapped into every rank of the group (CUDA IPC over NVLink).
-// Region s of a buffer holds what rank s wrote into it, row k = the writer's send position k:
-//   rx   [G][cap][D] bf16   token rows dispatched to this rank
-//   meta [G][cap]           their expert ids and probabilities
+// Region s of a buffer holds what rank s wrote into it, row k = rank s's local token k (rows are
+// not compacted: a token's row slot is the same in every destination, so no send layout is built):
+//   rx   [G][cap][D] bf16   token rows dispatched to this rank (written only where the token has
+//                           an expert here)
+//   meta [G][cap]           expert ids and probabilities of every token of rank s (written for
+//                           every token, so that rows without a local expert read as such)
 //   back [G][cap][D] bf16   partial rows returned to this rank (for the tokens it sent out)
 //   sync [4G+2] u32         [0,G) dispatch arrivals from rank s, [G,2G) combine arrivals,
-//                           [2G,3G) dispatch row counts, [3G] abort word, [3G+1], [3G+2]
+//                           [2G,3G) token counts of rank s, [3G] abort word, [3G+1], [3G+2]
 //                           this rank's CTA tickets of its dispatch and of its partial-row send
 // A writing kernel signals every rank once per layer step: after a CTA barrier one thread fences
 // at system scope (cumulative over the CTA's stores, which the barrier orders before it) and takes
@@ -137,9 +75,9 @@ __device__ inline bool ep_wait_counters(const uint32_t *ctr, int G, uint32_t tar
 }
 
 // Last-CTA signal of a writing kernel (all threads call it after their stores): arrival counter
-// `slot` of every rank + 1; the dispatch also publishes its row counts (counts != null).
+// `slot` of every rank + 1; the dispatch also publishes its token count (count >= 0).
 __device__ inline void ep_signal(uint32_t *ticket, const EpPeers &peers, int G, int slot, int count_slot,
-                                 const int32_t *counts) {
+                                 int count) {
     __shared__ uint32_t last;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -151,40 +89,46 @@ __device__ inline void ep_signal(uint32_t *ticket, const EpPeers &peers, int G, 
     if (threadIdx.x == 0) {
         *ticket = 0;  // the next launch counts from zero (launches on one stream do not overlap)
         __threadfence_system();
-        if (counts)
-            for (int q = 0; q < G; ++q) peers.sync[q][count_slot] = (uint32_t)counts[q];
+        if (count >= 0)
+            for (int q = 0; q < G; ++q) peers.sync[q][count_slot] = (uint32_t)count;
         __threadfence_system();
         for (int q = 0; q < G; ++q) atomicAdd_system(peers.sync[q] + slot, 1u);
     }
 }
 
-// Dispatch: one warp per (local token t, destination d) pair copies t's row (and its routing
-// metadata) into region `rank` of d's rx / meta (row send_idx[t, d]) by direct stores over NVLink.
+// Dispatch: one warp per (local token t, destination d) pair writes t's routing metadata into
+// region `rank` of d's meta (row t) and, when one of t's experts lives on d, t's row into d's rx
+// (row t), by direct stores over NVLink. The warp's token row is requested before the metadata
+// test, so the pair costs one round trip to local memory.
 __global__ void __launch_bounds__(256)
 ep_dispatch_kernel(const uint16_t *__restrict__ h, const int32_t *__restrict__ ids, const float *__restrict__ probs,
-                   int T, int D, int G, int rank, int cap, const int32_t *__restrict__ send_idx,
-                   const int32_t *__restrict__ send_count, EpPeers peers, uint32_t *ticket) {
+                   int T, int D, int G, int rank, int cap, int E_l, EpPeers peers, uint32_t *ticket) {
     const int lane = threadIdx.x & 31, warps = gridDim.x * (blockDim.x >> 5);
     for (int td = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); td < T * G; td += warps) {
         const int t = td / G, d = td - t * G;
-        const int k = send_idx[td];
-        if (k < 0) continue;
         const uint4 *src = reinterpret_cast<const uint4 *>(h + (size_t)t * D);
         uint4 v[8];  // D <= 2048: 8 chunks of 16 bytes per lane
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-            if (lane + 32 * c < D / 8) v[c] = src[lane + 32 * c];
-        const size_t row = (size_t)rank * cap + k;
+            if (lane + 32 * c < D / 8) v[c] = __ldg(src + lane + 32 * c);
+        int e = 0;
+        float p = 0.f;
+        if (lane < 8) {
+            e = __ldg(ids + (size_t)t * 8 + lane);
+            p = __ldg(probs + (size_t)t * 8 + lane);
+        }
+        const size_t row = (size_t)rank * cap + t;
+        if (lane < 8) {
+            peers.meta[d][row].ids[lane] = e;
+            peers.meta[d][row].probs[lane] = p;
+        }
+        if (!__any_sync(kFull, lane < 8 && e / E_l == d)) continue;
         uint4 *dst = reinterpret_cast<uint4 *>(peers.rx[d] + row * D);
 #pragma unroll
         for (int c = 0; c < 8; ++c)
             if (lane + 32 * c < D / 8) dst[lane + 32 * c] = v[c];
-        if (lane < 8) {
-            peers.meta[d][row].ids[lane] = ids[(size_t)t * 8 + lane];
-            peers.meta[d][row].probs[lane] = probs[(size_t)t * 8 + lane];
-        }
     }
-    ep_signal(ticket, peers, G, rank, 2 * G + rank, send_count);
+    ep_signal(ticket, peers, G, rank, 2 * G + rank, T);
 }
 
 // Receiver: waits for every rank's dispatch, then the local expert of every (row, slot) of the
@@ -219,9 +163,9 @@ ep_recv_routes_kernel(const RowMeta *__restrict__ meta, const uint32_t *__restri
     for (int i = threadIdx.x; i <= E_l; i += blockDim.x) block_counts[(size_t)blockIdx.x * (E_l + 1) + i] = hist[i];
 }
 
-// Receiver: one warp per filled row (s, k): partial row z = sum over its local slots j (slot
-// order) of p_j * y_j (f32, then bf16), stored straight into region `rank` of rank s's back
-// buffer (row k). y_j = yp[route_pos[8i + j]] (expert rows in expert order).
+// Receiver: one warp per row (s, k) with at least one local slot: partial row z = sum over its
+// local slots j (slot order) of p_j * y_j (f32, then bf16), stored straight into region `rank` of
+// rank s's back buffer (row k). y_j = yp[route_pos[8i + j]] (expert rows in expert order).
 __global__ void __launch_bounds__(256)
 ep_reduce_send_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__ route_pos,
                       const int32_t *__restrict__ ids_local, const RowMeta *__restrict__ meta,
@@ -238,7 +182,9 @@ ep_reduce_send_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict
         // slot j's position and weight in lane j (weight 0: not a local slot)
         int pos = 0;
         float p = 0.f;
-        if (lane < 8 && ids_local[(size_t)i * 8 + lane] < E_l) {
+        const bool mine = lane < 8 && ids_local[(size_t)i * 8 + lane] < E_l;
+        if (!__any_sync(kFull, mine)) continue;  // no expert of this rank: the row was not sent here
+        if (mine) {
             pos = route_pos[(size_t)i * 8 + lane];
             p = __ldcg(&meta[i].probs[lane]);
         }
@@ -275,15 +221,16 @@ ep_reduce_send_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict
             reinterpret_cast<uint4 *>(dst)[c] = r;
         }
     }
-    ep_signal(ticket, peers, G, G + rank, 0, nullptr);
+    ep_signal(ticket, peers, G, G + rank, 0, -1);
 }
 
 // Owner, one CTA of 256 threads per local token: waits for every rank's partial rows, then
-// out[t] = sigmoid(gate_t) * ys[t] + sum over ranks d (ascending) of back[d][send_idx[t, d]];
+// out[t] = sigmoid(gate_t) * ys[t] + sum over the ranks d (ascending) that own one of t's experts
+// of back[d][t];
 // resid[t] += out; and, when norm_w is given, the next layer's input row h[t] = bf16(resid[t] *
 // rsqrt(mean(resid[t]^2) + eps) * norm_w) (gpu_graph.mm:48-61).
 __global__ void __launch_bounds__(256)
-ep_combine_kernel(const uint16_t *__restrict__ back, const int32_t *__restrict__ send_idx, int G, int cap,
+ep_combine_kernel(const uint16_t *__restrict__ back, const int32_t *__restrict__ ids, int E_l, int G, int cap,
                   const uint32_t *__restrict__ sync, uint32_t target, EpPeers peers, const uint16_t *__restrict__ ys,
                   const float *__restrict__ gate_logit, int D, float *__restrict__ resid,
                   const float *__restrict__ norm_w, float eps, uint16_t *__restrict__ h, uint32_t *__restrict__ err) {
@@ -294,9 +241,12 @@ ep_combine_kernel(const uint16_t *__restrict__ back, const int32_t *__restrict__
     if (!ok) return;
     const int t = blockIdx.x, tid = threadIdx.x;
     const float g = sigmoid_ref(gate_logit[t]);
+    uint32_t dests = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dests |= 1u << (__ldg(ids + (size_t)t * 8 + j) / E_l);
     int32_t row[kMaxRanks];
 #pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) row[d] = d < G ? send_idx[(size_t)t * G + d] : -1;
+    for (int d = 0; d < kMaxRanks; ++d) row[d] = (d < G && ((dests >> d) & 1u)) ? t : -1;
     float r[1][8];  // D <= 2048: one chunk of 8 per thread
     float ss = 0.f;
 #pragma unroll

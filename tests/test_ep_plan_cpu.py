@@ -34,7 +34,7 @@ def _worker(rank, world, port, T, E, sizes, q):
         ids = _global_ids(T, E, 3)
         E_l = E // world
         lo = sum(sizes[:rank])
-        rows, send_idx = ep_plan.pack(ids[lo:lo + sizes[rank]], lo, E_l, world)
+        rows, sent = ep_plan.pack(ids[lo:lo + sizes[rank]], lo, E_l, world)
         gathered = [None] * world
         dist.all_gather_object(gathered, rows)
         received = [gathered[src][rank] for src in range(world)]
@@ -45,7 +45,7 @@ def _worker(rank, world, port, T, E, sizes, q):
         # combine bookkeeping: each (token, destination) pair maps to exactly one returned row
         for t in range(sizes[rank]):
             dests = sorted(set((ids[lo + t] // E_l).tolist()))
-            ok &= [d for d in range(world) if send_idx[t, d] >= 0] == dests
+            ok &= [d for d in range(world) if sent[t, d]] == dests
         q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()
