@@ -455,6 +455,7 @@ void configure_kernels() {
     cudaFuncSetAttribute(gg::grouped_gemm_pair_kernel<gg::MODE_DOWN, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          gg::P_SMEM);
     cudaFuncSetAttribute(decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecodeSmemMax);
+    cudaFuncSetAttribute(ep_reduce_send_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ep_send_smem(2048));
     cudaFuncSetAttribute(decode_ffn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(decode_ffn_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     for (int bits : {8, 5})
@@ -2378,7 +2379,8 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                                           L->bits, grid, st);
             // 5. partial row sums straight back into the token owners, then the owner's combine
             mark(l, 6);
-            ep_reduce_send_kernel<<<std::min((RC + 7) / 8, 8 * c->sms), 256, 0, st>>>(
+            ep_reduce_send_kernel<<<std::min((RC + kSendWarps - 1) / kSendWarps, c->sms), kSendWarps * 32,
+                                    ep_send_smem(D), st>>>(
                 y, rpos, il, my_meta, my_sync, G, rank, cap, D, El, peers, my_sync + 3 * G + 2, c->d_err);
             mark(l, 7);
             ep_combine_kernel<<<T, 256, 0, st>>>(my_back, ids, El, G, cap, my_sync, target, peers, y + (size_t)8 * RC * D,

@@ -166,59 +166,98 @@ ep_recv_routes_kernel(const RowMeta *__restrict__ meta, const uint32_t *__restri
 // Receiver: one warp per row (s, k) with at least one local slot: partial row z = sum over its
 // local slots j (slot order) of p_j * y_j (f32, then bf16), stored straight into region `rank` of
 // rank s's back buffer (row k). y_j = yp[route_pos[8i + j]] (expert rows in expert order).
-__global__ void __launch_bounds__(256)
+// The local slots' rows are requested together (kSendSlots at a time) by cp.async into the warp's
+// own shared-memory staging, so a row costs one round trip to memory instead of one per chunk,
+// and the row accumulator (8 chunks x 8 floats per lane) lives in registers. Each lane reads back
+// only the chunks it copied itself, so completion of its own copies is the only wait.
+constexpr int kSendWarps = 8, kSendSlots = 6;
+inline size_t ep_send_smem(int D) { return (size_t)kSendWarps * kSendSlots * D * 2; }
+
+__global__ void __launch_bounds__(kSendWarps * 32, 1)
 ep_reduce_send_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__ route_pos,
                       const int32_t *__restrict__ ids_local, const RowMeta *__restrict__ meta,
                       const uint32_t *__restrict__ sync, int G, int rank, int cap, int D, int E_l, EpPeers peers,
                       uint32_t *ticket, const uint32_t *__restrict__ err) {
+    extern __shared__ uint4 send_stage[];
     __shared__ int32_t cnt[kMaxRanks];
     if (threadIdx.x < G) cnt[threadIdx.x] = (int)__ldcg(sync + 2 * G + threadIdx.x);
     __syncthreads();
     const bool live = !(*reinterpret_cast<const volatile uint32_t *>(err) & kErrTimeout);
-    const int lane = threadIdx.x & 31, warps = gridDim.x * (blockDim.x >> 5);
-    for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); live && i < G * cap; i += warps) {
+    const int lane = threadIdx.x & 31, warps = gridDim.x * kSendWarps, nch = D / 8;
+    uint4 *stage = send_stage + (size_t)(threadIdx.x >> 5) * kSendSlots * nch;
+    for (int i = blockIdx.x * kSendWarps + (threadIdx.x >> 5); live && i < G * cap; i += warps) {
         const int s = i / cap, k = i - s * cap;
         if (k >= cnt[s]) continue;
-        // slot j's position and weight in lane j (weight 0: not a local slot)
+        const bool mine = lane < 8 && ids_local[(size_t)i * 8 + lane] < E_l;
+        const uint32_t slots = __ballot_sync(kFull, mine);
+        if (!slots) continue;  // no expert of this rank: the row was not sent here
         int pos = 0;
         float p = 0.f;
-        const bool mine = lane < 8 && ids_local[(size_t)i * 8 + lane] < E_l;
-        if (!__any_sync(kFull, mine)) continue;  // no expert of this rank: the row was not sent here
         if (mine) {
             pos = route_pos[(size_t)i * 8 + lane];
             p = __ldcg(&meta[i].probs[lane]);
         }
-        uint16_t *dst = peers.back[s] + ((size_t)rank * cap + k) * D;
-        float pj[8];
-        int rj[8];
+        float o[8][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            pj[j] = __shfl_sync(kFull, p, j);
-            rj[j] = __shfl_sync(kFull, pos, j);
-        }
-        for (int c = lane; c < D / 8; c += 32) {
-            uint4 v8[8];  // the local slots' chunks, all requested before any is used
+        for (int cc = 0; cc < 8; ++cc)
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                v8[j] = pj[j] != 0.f ? *reinterpret_cast<const uint4 *>(yp + (size_t)rj[j] * D + c * 8) : make_uint4(0, 0, 0, 0);
-            float o[8] = {};
+            for (int m = 0; m < 8; ++m) o[cc][m] = 0.f;
+        uint32_t left = slots;
+        while (left) {
+            // the next (up to) kSendSlots local slots, ascending
+            int js[kSendSlots];
+            int ng = 0;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (pj[j] == 0.f) continue;
-                const uint4 v = v8[j];
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int m = 0; m < 8; ++m) {
-                    const float prod = pj[j] * ((m & 1) ? bf16_hi(w[m >> 1]) : bf16_lo(w[m >> 1]));
-                    o[m] = o[m] + prod;
+            for (int q = 0; q < kSendSlots; ++q) {
+                js[q] = left ? __ffs(left) - 1 : 0;
+                if (left) {
+                    left &= left - 1;
+                    ++ng;
                 }
             }
+#pragma unroll
+            for (int q = 0; q < kSendSlots; ++q) {
+                const int r = __shfl_sync(kFull, pos, js[q]);
+                if (q < ng) {
+                    const uint16_t *src = yp + (size_t)r * D;
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        const int c = lane + 32 * cc;
+                        if (c < nch) cp_async_16(stage + q * nch + c, src + c * 8, true);
+                    }
+                }
+            }
+            cp_async_commit();
+            cp_async_wait<0>();
+#pragma unroll
+            for (int q = 0; q < kSendSlots; ++q) {
+                const float pj = __shfl_sync(kFull, p, js[q]);
+                if (q >= ng) continue;
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    const int c = lane + 32 * cc;
+                    if (c >= nch) continue;
+                    const uint4 v = stage[q * nch + c];
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {
+                        const float prod = pj * ((m & 1) ? bf16_hi(w[m >> 1]) : bf16_lo(w[m >> 1]));
+                        o[cc][m] = o[cc][m] + prod;
+                    }
+                }
+            }
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(peers.back[s] + ((size_t)rank * cap + k) * D);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const int c = lane + 32 * cc;
+            if (c >= nch) continue;
             uint4 r;
-            r.x = pack_bf16x2(o[0], o[1]);
-            r.y = pack_bf16x2(o[2], o[3]);
-            r.z = pack_bf16x2(o[4], o[5]);
-            r.w = pack_bf16x2(o[6], o[7]);
-            reinterpret_cast<uint4 *>(dst)[c] = r;
+            r.x = pack_bf16x2(o[cc][0], o[cc][1]);
+            r.y = pack_bf16x2(o[cc][2], o[cc][3]);
+            r.z = pack_bf16x2(o[cc][4], o[cc][5]);
+            r.w = pack_bf16x2(o[cc][6], o[cc][7]);
+            dst[c] = r;
         }
     }
     ep_signal(ticket, peers, G, G + rank, 0, -1);
