@@ -391,7 +391,7 @@ def run_expert_parallel(args, di, torch, rank, local, world):
         "clocks": clk.summary(),
         # per layer: router tiles, router GEMM, router select, layout, dispatch, receive, scan, scatter +
         # row permutation, gate_up, down, partial-row send, combine; one RMSNorm before the first layer
-        "gpu_launches": args.steps * (LAYERS * 11 + 1),
+        "gpu_launches": args.steps * (LAYERS * 10 + 1),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

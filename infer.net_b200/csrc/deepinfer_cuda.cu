@@ -694,14 +694,20 @@ void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, Tile *rtile
                                                  0, D, E, 1, approx, T, err),
                                   8, grid, st);
 }
+// dsp: the expert-parallel dispatch fused into the router (block_counts may then be null)
 void enqueue_router_select(const Layer *L, const uint16_t *x, int T, const int32_t *forced, int32_t *ids,
                            float *probs, float *gate, int32_t *block_counts, int nblocks, const float *wn,
-                           const float *wf, const uint16_t *approx, uint32_t *err, cudaStream_t st) {
+                           const float *wf, const uint16_t *approx, uint32_t *err, cudaStream_t st,
+                           const RouterDispatch *dsp = nullptr) {
     const int E = L->E, D = L->D;
     const QView R = L->m[0]->view(), SR = L->m[7]->view();
-    CK(cudaMemsetAsync(block_counts, 0, sizeof(int32_t) * (size_t)nblocks * E, st));
-    router_select_kernel<<<(T + 7) / 8, 256, 0, st>>>(approx, wn, wf, x, T, E, D, R, SR, L->bias, forced, ids, probs,
-                                                      gate, block_counts, err);
+    if (block_counts) CK(cudaMemsetAsync(block_counts, 0, sizeof(int32_t) * (size_t)nblocks * E, st));
+    if (dsp)
+        router_select_kernel<true><<<(T + 7) / 8, 256, 0, st>>>(approx, wn, wf, x, T, E, D, R, SR, L->bias, forced,
+                                                                ids, probs, gate, block_counts, err, *dsp);
+    else
+        router_select_kernel<false><<<(T + 7) / 8, 256, 0, st>>>(approx, wn, wf, x, T, E, D, R, SR, L->bias, forced,
+                                                                 ids, probs, gate, block_counts, err, RouterDispatch{});
 }
 bool router_tc_fits(const Layer *L) { return L->E % 128 == 0 && L->D <= 2048; }
 
@@ -2340,7 +2346,10 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                 const float *rwn = nullptr, *rwf = nullptr;
                 router_norms(L, st, wn, wf, &rwn, &rwf);
                 enqueue_router_approx(L, h, T, rtiles, rnt, approx, grid, c->d_err, st);
-                enqueue_router_select(L, h, T, nullptr, ids, probs, gate, bc, nb_l, rwn, rwf, approx, c->d_err, st);
+                // 2. (fused) one row per (token, destination rank), written into the destinations over NVLink
+                const RouterDispatch dsp{peers, G, rank, cap, El, my_sync + 3 * G + 1};
+                enqueue_router_select(L, h, T, nullptr, ids, probs, gate, nullptr, nb_l, rwn, rwf, approx, c->d_err,
+                                      st, &dsp);
             } else {
                 router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
                                        router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);
@@ -2351,11 +2360,13 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                 CK(cudaMemcpyAsync(dht + (size_t)l * T * D, h, (size_t)T * D * 2, cudaMemcpyDeviceToDevice, st));
             if (dit)
                 CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, st));
-            // 2. one row per (token, destination rank), written into the destinations over NVLink
+            // 2. one row per (token, destination rank), written into the destinations over NVLink (the
+            // tensor-core router writes them itself)
             mark(l, 1);
-            ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
-                                                                                      cap, El, peers,
-                                                                                      my_sync + 3 * G + 1);
+            if (!router_tc_fits(L))
+                ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
+                                                                                          cap, El, peers,
+                                                                                          my_sync + 3 * G + 1);
             // 3. the rows every rank sent here -> local routes, expert segments, GEMM tiles
             mark(l, 2);
             ep_recv_routes_kernel<<<nbr, 256, 0, st>>>(my_meta, my_sync, target, G, cap, L->E_off, El, peers, il, rbc,
