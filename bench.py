@@ -352,7 +352,8 @@ def run_expert_parallel(args, di, torch, rank, local, world):
     dist.barrier()
     ep.stack(layers, norms, x, Tl, 1e-6, di.DEVICE_IO | di.PROFILE)
     prof = list(ctx.last_profile().values())
-    ep_stage_names = ["route", "dispatch", "receive_scan", "scatter", "gate_up", "down", "send", "combine"]
+    ep_stage_names = ["router_logits", "top8_dispatch", "receive_scan", "scatter", "gate_up", "down", "send",
+                      "combine"]
     ep_stages = dict(zip(ep_stage_names, prof[:len(ep_stage_names)]))
     # end to end through the host-buffer API
     xh = x0.cpu().pin_memory()

@@ -206,9 +206,8 @@ void *di_moe_ep_layer_create(void *ep, void *router, void *gate, void *up, void 
    calls it with the same layers. h_trace (bf16 [n_layers, tokens, D]) and ids_trace (int32
    [n_layers, tokens, 8]) are optional per-layer dumps of this rank's tokens, as in di_moe_stack.
    Flags: DI_MOE_DEVICE_IO, DI_MOE_PROFILE (di_moe_last_profile of the ep's context then returns this
-   rank's milliseconds summed over the layers for [route (with the tensor-core router this includes
-   the dispatch stores), dispatch (SIMT router only), receive + scan, scatter, gate_up, down,
-   partial-row send, combine]). */
+   rank's milliseconds summed over the layers for [router logits, top-8 + dispatch, receive + scan,
+   scatter, gate_up, down, partial-row send, combine]). */
 int di_moe_ep_stack(void *ep, void *const *layers, const float *norms, int n_layers, float eps, float *x, int tokens,
                     uint16_t *h_trace, int32_t *ids_trace, int flags, double *ms, char *error, int capacity);
 

@@ -2313,8 +2313,8 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
         Tile *rtiles = at<Tile>(c, o_rt);
         int32_t *rnt = at<int32_t>(c, o_rnt);
         float *wf = at<float>(c, o_wf);
-        // DI_MOE_PROFILE: per-layer events at the stage boundaries [route, dispatch, receive + scan,
-        // scatter, gate_up, down, partial-row send, combine], summed over the layers
+        // DI_MOE_PROFILE: per-layer events at the stage boundaries [router logits, top-8 + dispatch,
+        // receive + scan, scatter, gate_up, down, partial-row send, combine], summed over the layers
         const bool profile = (flags & DI_MOE_PROFILE) != 0;
         constexpr int kEpStages = 8;
         const size_t need_events = profile ? (size_t)n_layers * (kEpStages + 1) : 0;
@@ -2346,6 +2346,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                 const float *rwn = nullptr, *rwf = nullptr;
                 router_norms(L, st, wn, wf, &rwn, &rwf);
                 enqueue_router_approx(L, h, T, rtiles, rnt, approx, grid, c->d_err, st);
+                mark(l, 1);
                 // 2. (fused) one row per (token, destination rank), written into the destinations over NVLink
                 const RouterDispatch dsp{peers, G, rank, cap, El, my_sync + 3 * G + 1};
                 enqueue_router_select(L, h, T, nullptr, ids, probs, gate, nullptr, nb_l, rwn, rwf, approx, c->d_err,
@@ -2353,6 +2354,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             } else {
                 router_logits_kernel<<<dim3((T + router::TT - 1) / router::TT, (E + router::TE - 1) / router::TE),
                                        router::THREADS, sizeof(router::Smem), st>>>(h, T, D, R, L->bias, logits);
+                mark(l, 1);
                 topk_count_kernel<<<nb_l, topk::WARPS * 32, 0, st>>>(logits, T, E, h, D, SR, nullptr, ids, probs, gate,
                                                                       bc, c->d_err);
             }
@@ -2362,7 +2364,6 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                 CK(cudaMemcpyAsync(dit + (size_t)l * T * 8, ids, (size_t)T * 8 * 4, cudaMemcpyDeviceToDevice, st));
             // 2. one row per (token, destination rank), written into the destinations over NVLink (the
             // tensor-core router writes them itself)
-            mark(l, 1);
             if (!router_tc_fits(L))
                 ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
                                                                                           cap, El, peers,

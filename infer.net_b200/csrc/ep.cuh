@@ -107,18 +107,36 @@ ep_reduce_send_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict
     const bool live = !(*reinterpret_cast<const volatile uint32_t *>(err) & kErrTimeout);
     const int lane = threadIdx.x & 31, warps = gridDim.x * kSendWarps, nch = D / 8;
     uint4 *stage = send_stage + (size_t)(threadIdx.x >> 5) * kSendSlots * nch;
-    for (int i = blockIdx.x * kSendWarps + (threadIdx.x >> 5); live && i < G * cap; i += warps) {
+    // a row's slot metadata (lane j < 8: local expert, position of its output row, weight); the
+    // next row's is requested before the current row is processed, so the row's own chain is one
+    // round trip (its output rows)
+    const int rows = G * cap;
+    auto fetch = [&](int r, int &id, int &ps, float &pr) {
+        id = E_l;
+        ps = 0;
+        pr = 0.f;
+        if (r < rows && lane < 8) {
+            id = ids_local[(size_t)r * 8 + lane];
+            ps = route_pos[(size_t)r * 8 + lane];
+            pr = __ldcg(&meta[r].probs[lane]);
+        }
+    };
+    int c_id, c_pos;
+    float c_p;
+    fetch(blockIdx.x * kSendWarps + (threadIdx.x >> 5), c_id, c_pos, c_p);
+    for (int i = blockIdx.x * kSendWarps + (threadIdx.x >> 5); live && i < rows; i += warps) {
+        int n_id, n_pos;
+        float n_p;
+        fetch(i + warps, n_id, n_pos, n_p);
         const int s = i / cap, k = i - s * cap;
-        if (k >= cnt[s]) continue;
-        const bool mine = lane < 8 && ids_local[(size_t)i * 8 + lane] < E_l;
+        const bool mine = k < cnt[s] && lane < 8 && c_id < E_l;
+        const int pos = mine ? c_pos : 0;
+        const float p = mine ? c_p : 0.f;
+        c_id = n_id;
+        c_pos = n_pos;
+        c_p = n_p;
         const uint32_t slots = __ballot_sync(kFull, mine);
         if (!slots) continue;  // no expert of this rank: the row was not sent here
-        int pos = 0;
-        float p = 0.f;
-        if (mine) {
-            pos = route_pos[(size_t)i * 8 + lane];
-            p = __ldcg(&meta[i].probs[lane]);
-        }
         float o[8][8];
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc)
