@@ -1044,6 +1044,20 @@ struct RouterDispatch {
     uint32_t *ticket;  // this rank's CTA ticket of the dispatch
 };
 
+// The token row (canonical lane partition in xr) into row slot rank * cap + t of the rx of every
+// rank in `dests`, by plain stores over NVLink.
+__device__ __forceinline__ void dispatch_row(const RouterDispatch &dsp, uint32_t dests, int t, int D,
+                                             const uint4 (&xr)[8]) {
+    const int lane = threadIdx.x & 31;
+    for (int d = 0; d < dsp.G; ++d) {
+        if (!((dests >> d) & 1u)) continue;
+        uint16_t *dst = dsp.peers.rx[d] + ((size_t)dsp.rank * dsp.cap + t) * D;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (k * 256 < D) *reinterpret_cast<uint4 *>(dst + k * 256 + lane * 8) = xr[k];
+    }
+}
+
 template <bool DISPATCH>
 __device__ __forceinline__ void router_select_token(
     const uint16_t *__restrict__ approx, const float *__restrict__ wn, const float *__restrict__ wf,
@@ -1077,6 +1091,7 @@ __device__ __forceinline__ void router_select_token(
     int32_t sel[8];
     float chosen[8];
     bool bad = false;
+    uint32_t sent_ranks = 0;  // DISPATCH: ranks the row has already gone to
     if (forced_ids) {
         int32_t id = 0;
         if (lane < 8) {
@@ -1116,13 +1131,25 @@ __device__ __forceinline__ void router_select_token(
         const float L8 = eighth_largest(lo_, E);
         uint32_t *mask = cand_mask[threadIdx.x >> 5];
         int ncand = 0;
+        uint32_t cand_ranks = 0;  // ranks owning a candidate (DISPATCH)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const uint32_t mj = __ballot_sync(kFull, lane + 32 * j < E && hi_[j] >= L8);
+            const bool cj = lane + 32 * j < E && hi_[j] >= L8;
+            const uint32_t mj = __ballot_sync(kFull, cj);
             if (lane == 0) mask[j] = mj;
             ncand += __popc(mj);
+            if constexpr (DISPATCH)
+                if (cj) cand_ranks |= 1u << ((lane + 32 * j) / dsp.E_l);
         }
         __syncwarp();
+        if constexpr (DISPATCH) {
+            // the row leaves now, to every rank that owns a candidate (a superset of the ranks of
+            // the final 8), so the NVLink stores overlap the exact dots below; a rank that ends up
+            // owning none of the 8 ignores the row (its metadata, written last, says so)
+            const uint32_t dm = ncand > kRouterMaxCand ? (1u << dsp.G) - 1u : __reduce_or_sync(kFull, cand_ranks);
+            dispatch_row(dsp, dm, t, D, xr);
+            sent_ranks = dm;
+        }
         // exact logits of the candidates (all experts if there are too many), ascending id; the
         // i-th goes to lane i % 32, slot i / 32
         const bool all = ncand > kRouterMaxCand;
@@ -1212,13 +1239,7 @@ __device__ __forceinline__ void router_select_token(
         uint32_t dests = 0;
 #pragma unroll
         for (int n = 0; n < 8; ++n) dests |= 1u << (sel[n] / dsp.E_l);
-        for (int d = 0; d < dsp.G; ++d) {
-            if (!((dests >> d) & 1u)) continue;
-            uint16_t *dst = dsp.peers.rx[d] + ((size_t)dsp.rank * dsp.cap + t) * D;
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-                if (k * 256 < D) *reinterpret_cast<uint4 *>(dst + k * 256 + lane * 8) = xr[k];
-        }
+        dispatch_row(dsp, dests & ~sent_ranks, t, D, xr);  // forced routes: nothing sent yet
     }
 }
 
