@@ -99,6 +99,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may be
+// scheduled before its predecessor on the stream has finished; pdl_enter(), executed by every
+// thread before it touches global memory, waits until the predecessor grid has completed with its
+// memory visible (which covers every earlier kernel of the stream), and lets this grid's successor
+// be scheduled once every CTA of this grid has started. Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+    pdl_wait();
+    pdl_trigger();
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -548,8 +548,10 @@ gg::Params grouped_params(int mode, const QView &w0, const QView &w1, const QVie
 
 template <int MODE>
 void launch_grouped(const gg::Params &p, int bits, int grid, cudaStream_t st) {
-    if (bits == 8) gg::grouped_gemm_kernel<MODE, 8><<<grid, gg::THREADS, gg::smem_bytes<MODE>(), st>>>(p);
-    else gg::grouped_gemm_kernel<MODE, 5><<<grid, gg::THREADS, gg::smem_bytes<MODE>(), st>>>(p);
+    // programmatic dependent launch: the CTAs set up barriers and TMEM while the previous kernel
+    // drains, then wait for it (pdl_wait) before their first global read
+    if (bits == 8) launch(gg::grouped_gemm_kernel<MODE, 8>, dim3(grid), dim3(gg::THREADS), gg::smem_bytes<MODE>(), st, true, p);
+    else launch(gg::grouped_gemm_kernel<MODE, 5>, dim3(grid), dim3(gg::THREADS), gg::smem_bytes<MODE>(), st, true, p);
 }
 
 // The CTA-pair grouped GEMM: clusters of two CTAs, one per SM of a pair of SMs (grid = the even
@@ -689,7 +691,7 @@ void enqueue_router_approx(const Layer *L, const uint16_t *x, int T, Tile *rtile
                            int grid, uint32_t *err, cudaStream_t st) {
     const int E = L->E, D = L->D;
     const QView R = L->m[0]->view();
-    router_tiles_kernel<<<1, 256, 0, st>>>(T, kRouterTileRows, rtiles, rnt);
+    launch(router_tiles_kernel, dim3(1), dim3(256), 0, st, true, T, kRouterTileRows, rtiles, rnt);
     launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, R, R, R, R, x, T, nullptr, 0, nullptr, rtiles, rnt, T,
                                                  0, D, E, 1, approx, T, err),
                                   8, grid, st);
@@ -703,10 +705,10 @@ void enqueue_router_select(const Layer *L, const uint16_t *x, int T, const int32
     const QView R = L->m[0]->view(), SR = L->m[7]->view();
     if (block_counts) CK(cudaMemsetAsync(block_counts, 0, sizeof(int32_t) * (size_t)nblocks * E, st));
     if (dsp)
-        router_select_kernel<true><<<(T + 7) / 8, 256, 0, st>>>(approx, wn, wf, x, T, E, D, R, SR, L->bias, forced,
+        launch(router_select_kernel<true>, dim3((T + 7) / 8), dim3(256), 0, st, true, approx, wn, wf, x, T, E, D, R, SR, L->bias, forced,
                                                                 ids, probs, gate, block_counts, err, *dsp);
     else
-        router_select_kernel<false><<<(T + 7) / 8, 256, 0, st>>>(approx, wn, wf, x, T, E, D, R, SR, L->bias, forced,
+        launch(router_select_kernel<false>, dim3((T + 7) / 8), dim3(256), 0, st, true, approx, wn, wf, x, T, E, D, R, SR, L->bias, forced,
                                                                  ids, probs, gate, block_counts, err, RouterDispatch{});
 }
 bool router_tc_fits(const Layer *L) { return L->E % 128 == 0 && L->D <= 2048; }
@@ -837,13 +839,13 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     }
     if (profile) stage_mark(c, S_SCAN);
     // 3. scan counts, segment offsets, GEMM tile list
-    scan_tiles_kernel<<<1, 1024, 0, st>>>(b.block_counts, b.nblocks, E, E, T, T, gg::BN, b.block_base, b.seg_count,
+    launch(scan_tiles_kernel, dim3(1), dim3(1024), 0, st, true, b.block_counts, b.nblocks, E, E, T, T, gg::BN, b.block_base, b.seg_count,
                                           b.seg_off, b.tiles, b.n_tiles, b.max_tiles, c->d_err);
     if (profile) stage_mark(c, S_SCATTER);
     // 4. stable scatter of routes into expert-grouped order
     // ... and the token rows copied into that order for the gate/up B operand
     // four CTAs per 64-token block share its row copies (measured: 2.26 ms/step against 2.56 for one)
-    scatter_permute_kernel<4><<<b.nblocks * 4, kScatterWarps * 32, 0, st>>>(
+    launch(scatter_permute_kernel<4>, dim3(b.nblocks * 4), dim3(kScatterWarps * 32), 0, st, true, 
         ids, T, E, b.block_base, b.seg_off, b.perm, b.route_pos, x, D, b.xp, E);
     c->last_perm = b.perm;
     c->last_seg_off = b.seg_off;
@@ -867,11 +869,11 @@ void enqueue_block(Context *c, const Layer *L, const uint16_t *x, int T, uint16_
     if (profile) stage_mark(c, S_COMBINE);
     // 7. combine (stacks: fused with the residual update and the next layer's RMSNorm)
     if (resid && !y) {
-        combine_norm_kernel<128><<<T, 128, 0, st>>>(b.yr, b.route_pos, b.ys, b.gate, probs, D, resid, next_norm, eps, next_h,
+        launch(combine_norm_kernel<128>, dim3(T), dim3(128), 0, st, true, b.yr, b.route_pos, b.ys, b.gate, probs, D, resid, next_norm, eps, next_h,
                                                next_trace, c->d_err);
     } else {
         const size_t n = (size_t)T * (D / 8);
-        combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(b.yr, b.route_pos, b.ys, b.gate, probs, T, D, y, resid,
+        launch(combine_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, true, b.yr, b.route_pos, b.ys, b.gate, probs, T, D, y, resid,
                                                                      c->d_err);
     }
     if (profile) stage_mark(c, S_N);
@@ -1339,7 +1341,7 @@ API int di_quant_gemm(void *ctx, void *matrix, int expert, const uint16_t *x, in
         CK(cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream));
         CK(cudaEventRecord(c->ev_start, c->stream));
         if (!dev_io) CK(cudaMemcpyAsync(const_cast<uint16_t *>(dx), x, (size_t)T * K * 2, cudaMemcpyHostToDevice, c->stream));
-        router_tiles_kernel<<<1, 256, 0, c->stream>>>(T, 256, at<Tile>(c, o_t), at<int32_t>(c, o_nt));
+        launch(router_tiles_kernel, dim3(1), dim3(256), 0, c->stream, true, T, 256, at<Tile>(c, o_t), at<int32_t>(c, o_nt));
         launch_grouped<gg::MODE_DOWN>(grouped_params(gg::MODE_DOWN, w, w, w, w, dx, T, nullptr, 0, nullptr,
                                                      at<Tile>(c, o_t), at<int32_t>(c, o_nt), T, 0, K, N, 1, dy, T,
                                                      c->d_err),
@@ -1771,7 +1773,7 @@ API int di_moe_stack(void *ctx, void *const *layers, const float *norms, int n_l
                                   trace_l, nullptr, nullptr, nullptr, (uint32_t)l + 1);
                 } else {
                     // layer l's RMSNorm runs in layer l-1's combine; the first one on its own
-                    if (l == 0) rmsnorm_kernel<<<T, 256, 0, c->stream>>>(dx, dn, D, eps, dh, trace_l);
+                    if (l == 0) launch(rmsnorm_kernel, dim3(T), dim3(256), 0, c->stream, true, dx, dn, D, eps, dh, trace_l);
                     const bool more = l + 1 < n_layers;
                     enqueue_block(c, L, dh, T, nullptr, dx, nullptr, nullptr, false, b, profile, nullptr, eps, nullptr,
                                   more ? dn + (size_t)(l + 1) * D : nullptr, more ? dh : nullptr,
@@ -2340,7 +2342,7 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             const QView SG = L->m[4]->view(), SU = L->m[5]->view(), SD = L->m[6]->view(), SR = L->m[7]->view();
             const uint32_t target = (uint32_t)(ep->steps + (uint64_t)l + 1);  // arrivals per rank so far
             // 1. route the local tokens (layer l's RMSNorm ran in layer l-1's combine)
-            if (l == 0) rmsnorm_kernel<<<T, 256, 0, st>>>(dx, dn, D, eps, h, nullptr);
+            if (l == 0) launch(rmsnorm_kernel, dim3(T), dim3(256), 0, st, true, dx, dn, D, eps, h, nullptr);
             if (router_tc_fits(L)) {
                 uint16_t *approx = reinterpret_cast<uint16_t *>(logits);
                 const float *rwn = nullptr, *rwf = nullptr;
@@ -2365,18 +2367,18 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
             // 2. one row per (token, destination rank), written into the destinations over NVLink (the
             // tensor-core router writes them itself)
             if (!router_tc_fits(L))
-                ep_dispatch_kernel<<<std::min((T * G + 7) / 8, 8 * c->sms), 256, 0, st>>>(h, ids, probs, T, D, G, rank,
+                launch(ep_dispatch_kernel, dim3(std::min((T * G + 7) / 8, 8 * c->sms)), dim3(256), 0, st, true, h, ids, probs, T, D, G, rank,
                                                                                           cap, El, peers,
                                                                                           my_sync + 3 * G + 1);
             // 3. the rows every rank sent here -> local routes, expert segments, GEMM tiles
             mark(l, 2);
-            ep_recv_routes_kernel<<<nbr, 256, 0, st>>>(my_meta, my_sync, target, G, cap, L->E_off, El, peers, il, rbc,
+            launch(ep_recv_routes_kernel, dim3(nbr), dim3(256), 0, st, true, my_meta, my_sync, target, G, cap, L->E_off, El, peers, il, rbc,
                                                        c->d_err);
-            scan_tiles_kernel<<<1, 1024, 0, st>>>(rbc, nbr, El + 1, El, RC, T, gg::BN, rbb, sgc, sgo, tiles, nt,
+            launch(scan_tiles_kernel, dim3(1), dim3(1024), 0, st, true, rbc, nbr, El + 1, El, RC, T, gg::BN, rbb, sgc, sgo, tiles, nt,
                                                   max_tiles, c->d_err);
             // stable scatter of the local routes and their received rows copied into expert order
             mark(l, 3);
-            scatter_permute_kernel<4><<<nbr * 4, kScatterWarps * 32, 0, st>>>(il, RC, El + 1, rbb, sgo, perm, rpos,
+            launch(scatter_permute_kernel<4>, dim3(nbr * 4), dim3(kScatterWarps * 32), 0, st, true, il, RC, El + 1, rbb, sgo, perm, rpos,
                                                                               my_rx, D, xp, El);
             // 4. local experts over the received rows, shared expert over the local rows
             mark(l, 4);
@@ -2391,11 +2393,10 @@ API int di_moe_ep_stack(void *ep_, void *const *layers, const float *norms, int 
                                           L->bits, grid, st);
             // 5. partial row sums straight back into the token owners, then the owner's combine
             mark(l, 6);
-            ep_reduce_send_kernel<<<std::min((RC + kSendWarps - 1) / kSendWarps, c->sms), kSendWarps * 32,
-                                    ep_send_smem(D), st>>>(
+            launch(ep_reduce_send_kernel, dim3(std::min((RC + kSendWarps - 1) / kSendWarps, c->sms)), dim3(kSendWarps * 32), ep_send_smem(D), st, true, 
                 y, rpos, il, my_meta, my_sync, G, rank, cap, D, El, peers, my_sync + 3 * G + 2, c->d_err);
             mark(l, 7);
-            ep_combine_kernel<<<T, 256, 0, st>>>(my_back, ids, El, G, cap, my_sync, target, peers, y + (size_t)8 * RC * D,
+            launch(ep_combine_kernel, dim3(T), dim3(256), 0, st, true, my_back, ids, El, G, cap, my_sync, target, peers, y + (size_t)8 * RC * D,
                                                  gate, D, dx, l + 1 < n_layers ? dn + (size_t)(l + 1) * D : nullptr,
                                                  eps, h, c->d_err);
             mark(l, 8);

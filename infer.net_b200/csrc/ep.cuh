@@ -25,6 +25,7 @@ namespace di {
 __global__ void __launch_bounds__(256)
 ep_dispatch_kernel(const uint16_t *__restrict__ h, const int32_t *__restrict__ ids, const float *__restrict__ probs,
                    int T, int D, int G, int rank, int cap, int E_l, EpPeers peers, uint32_t *ticket) {
+    pdl_enter();
     const int lane = threadIdx.x & 31, warps = gridDim.x * (blockDim.x >> 5);
     for (int td = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); td < T * G; td += warps) {
         const int t = td / G, d = td - t * G;
@@ -60,6 +61,7 @@ __global__ void __launch_bounds__(256)
 ep_recv_routes_kernel(const RowMeta *__restrict__ meta, const uint32_t *__restrict__ sync, uint32_t target, int G,
                       int cap, int E_off, int E_l, EpPeers peers, int32_t *__restrict__ ids_local,
                       int32_t *__restrict__ block_counts, uint32_t *__restrict__ err) {
+    pdl_enter();
     __shared__ int32_t hist[kMaxBuckets];
     __shared__ int32_t cnt[kMaxRanks];
     __shared__ int ok;
@@ -100,6 +102,7 @@ ep_reduce_send_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict
                       const int32_t *__restrict__ ids_local, const RowMeta *__restrict__ meta,
                       const uint32_t *__restrict__ sync, int G, int rank, int cap, int D, int E_l, EpPeers peers,
                       uint32_t *ticket, const uint32_t *__restrict__ err) {
+    pdl_enter();
     extern __shared__ uint4 send_stage[];
     __shared__ int32_t cnt[kMaxRanks];
     if (threadIdx.x < G) cnt[threadIdx.x] = (int)__ldcg(sync + 2 * G + threadIdx.x);
@@ -213,6 +216,7 @@ ep_combine_kernel(const uint16_t *__restrict__ back, const int32_t *__restrict__
                   const uint32_t *__restrict__ sync, uint32_t target, EpPeers peers, const uint16_t *__restrict__ ys,
                   const float *__restrict__ gate_logit, int D, float *__restrict__ resid,
                   const float *__restrict__ norm_w, float eps, uint16_t *__restrict__ h, uint32_t *__restrict__ err) {
+    pdl_enter();
     __shared__ int ok;
     __shared__ float part[8];
     if (threadIdx.x == 0) ok = ep_wait_counters(sync + G, G, target, sync + 3 * G, peers, err);

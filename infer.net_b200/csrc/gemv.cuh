@@ -125,6 +125,7 @@ __device__ __forceinline__ void load_x16_bf16(const uint16_t *x, int c, float *v
 // h[t] = bf16(x[t] * rsqrt(mean(x[t]^2) + eps) * w) (gpu_graph.mm:48-61), one CTA per token.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int D,
                                                       float eps, uint16_t *__restrict__ h, uint16_t *__restrict__ trace) {
+    pdl_enter();
     __shared__ float part[8];
     const int t = blockIdx.x;
     const float *xr = x + (size_t)t * D;

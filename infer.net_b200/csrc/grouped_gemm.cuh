@@ -230,9 +230,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     const int RB = (p.rows + RPU - 1) / RPU;
     const int nk = p.K / BK;  // K is a multiple of 64
     const int gpr = p.K / 64;
-    const int n_units = (*p.n_tiles) * RB;
     const int tkind = MODE + (p.E == 1 ? 2 : 0);  // timing build: gate_up, down, router logits
     const long long t_kernel = gg_now();
+    pdl_trigger();  // the set-up below (barriers, TMEM, tensor maps) touches no global memory
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -266,6 +266,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
+    pdl_wait();  // the predecessor's tile list, rows and counts
+    const int n_units = (*p.n_tiles) * RB;
 
     // Flat pipeline index `it` = ul * nk + kb over this CTA's units ul (unit u = blockIdx.x +
     // ul * gridDim.x) and K-blocks kb. Stage s = it % STAGES, phase (it / STAGES) & 1.

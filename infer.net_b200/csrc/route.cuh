@@ -427,6 +427,7 @@ scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int n_h
                   int shared_count, int bn, int32_t *__restrict__ block_base, int32_t *__restrict__ seg_count,
                   int32_t *__restrict__ seg_off, Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles, int max_tiles,
                   uint32_t *__restrict__ err) {
+    pdl_enter();
     __shared__ int32_t cnt[kMaxBuckets], ntile[kMaxBuckets], toff[kMaxBuckets + 1], off[kMaxBuckets + 1];
     __shared__ int32_t wsum[32][2];
     const int tid = threadIdx.x, S = n_hist;  // segment S = shared expert
@@ -570,6 +571,7 @@ scatter_permute_kernel(const int32_t *__restrict__ ids, int T, int E, const int3
                        const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route,
                        int32_t *__restrict__ route_pos, const uint16_t *__restrict__ x, int D,
                        uint16_t *__restrict__ xp, int copy_buckets) {
+    pdl_enter();
     __shared__ int32_t cnt[kScatterWarps][kMaxBuckets];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int i = threadIdx.x; i < kScatterWarps * kMaxBuckets; i += blockDim.x) (&cnt[0][0])[i] = 0;
@@ -648,6 +650,7 @@ combine_norm_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__
                     const float *__restrict__ probs, int D, float *__restrict__ resid,
                     const float *__restrict__ norm_w, float eps, uint16_t *__restrict__ h,
                     uint16_t *__restrict__ h_trace, const uint32_t *__restrict__ err) {
+    pdl_enter();
     __shared__ float part[NT / 32];
     if (*err) return;  // a failed call leaves the residual untouched
     const int t = blockIdx.x, tid = threadIdx.x;
@@ -759,6 +762,7 @@ __global__ void combine_kernel(const uint16_t *__restrict__ yp, const int32_t *_
                                const float *__restrict__ gate_logit, const float *__restrict__ probs, int T, int D,
                                uint16_t *__restrict__ out, float *__restrict__ resid,
                                const uint32_t *__restrict__ err) {
+    pdl_enter();
     const int per_tok = D / 8;
     const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (size_t)T * per_tok) return;
@@ -858,6 +862,7 @@ __global__ void __launch_bounds__(256) router_row_norms_kernel(QView R, int E, i
 // Work tiles of a one-segment grouped GEMM (the approximate-logit GEMM, dense projections): segment
 // 0, `rows` tokens each (at most 256).
 __global__ void router_tiles_kernel(int T, int rows, Tile *__restrict__ tiles, int32_t *__restrict__ n_tiles) {
+    pdl_enter();
     const int n = (T + rows - 1) / rows;
     for (int i = threadIdx.x; i < n; i += blockDim.x) tiles[i] = Tile{0, i * rows, min(rows, T - i * rows)};
     if (threadIdx.x == 0) *n_tiles = n;
@@ -1258,6 +1263,7 @@ router_select_kernel(const uint16_t *__restrict__ approx, const float *__restric
                      const int32_t *__restrict__ forced_ids, int32_t *__restrict__ ids, float *__restrict__ probs,
                      float *__restrict__ gate_logit, int32_t *__restrict__ block_counts, uint32_t *__restrict__ err,
                      RouterDispatch dsp) {
+    pdl_enter();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t < T) router_select_token<DISPATCH>(approx, wn, wf, x, t, E, D, R, SR, bias, forced_ids, ids, probs,
                                              gate_logit, block_counts, err, dsp);
