@@ -72,3 +72,21 @@ def test_single_rank_plan_is_identity():
     segs = ep_plan.receive_permutation([rows[0]], 0, 32)
     counts, offsets, routes = O.permute(ids, 32)
     assert all(segs[e] == routes[offsets[e]:offsets[e] + counts[e]].tolist() for e in range(32))
+
+
+def test_rows_sent_to_extra_ranks_are_ignored():
+    # the router stores a token's row into every rank that owns one of its CANDIDATE experts before
+    # the exact top-8 is known; a rank that owns none of the final 8 receives the row but no route
+    E, G, T = 64, 4, 97
+    E_l = E // G
+    ids = _global_ids(T, E, 5)
+    counts, offsets, routes = O.permute(ids, E)
+    rng = np.random.default_rng(6)
+    rows, sent = ep_plan.pack(ids, 0, E_l, G)
+    extra = rng.random((T, G)) < 0.3
+    for d in range(G):
+        rows[d] = [(tok, i, s or bool(extra[tok, d])) for tok, i, s in rows[d]]
+    for r in range(G):
+        segs = ep_plan.receive_permutation([rows[r]], r, E_l)
+        assert all(segs[e] == routes[offsets[r * E_l + e]:offsets[r * E_l + e] + counts[r * E_l + e]].tolist()
+                   for e in range(E_l))
