@@ -526,40 +526,7 @@ scan_tiles_kernel(const int32_t *__restrict__ block_counts, int nblocks, int n_h
 // route r = t*8 + slot at seg_off[e] + block_base[blk][e] + (rank of r among earlier
 // routes of e in this block): the stable counting sort (prefill_moe.mm:12-14 order).
 constexpr int kScatterWarps = topk::TOK_PER_CTA * 8 / 32;  // one warp per 32 routes of a block
-__global__ void __launch_bounds__(kScatterWarps * 32)
-scatter_routes_kernel(const int32_t *__restrict__ ids, int T, int E, const int32_t *__restrict__ block_base,
-                      const int32_t *__restrict__ seg_off, int32_t *__restrict__ perm_route,
-                      int32_t *__restrict__ route_pos) {
-    // cnt[w][e]: routes of e in warp w's 32 routes, then the count in warps before w
-    __shared__ int32_t cnt[kScatterWarps][kMaxBuckets];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < kScatterWarps * kMaxBuckets; i += blockDim.x) (&cnt[0][0])[i] = 0;
-    __syncthreads();
-    const int r = blockIdx.x * topk::TOK_PER_CTA * 8 + warp * 32 + lane;
-    const bool valid = r < T * 8;
-    const int e = valid ? ids[r] : -1 - lane;  // invalid lanes never match real experts
-    const unsigned peers = __match_any_sync(kFull, e);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    if (valid && lane == __ffs(peers) - 1) cnt[warp][e] = __popc(peers);
-    __syncthreads();
-    for (int x = threadIdx.x; x < E; x += blockDim.x) {  // exclusive prefix over the warps, per bucket
-        int run = 0;
-#pragma unroll
-        for (int w = 0; w < kScatterWarps; ++w) {
-            const int v = cnt[w][x];
-            cnt[w][x] = run;
-            run += v;
-        }
-    }
-    __syncthreads();
-    if (valid) {
-        const int pos = seg_off[e] + block_base[(size_t)blockIdx.x * E + e] + cnt[warp][e] + rank;
-        perm_route[pos] = r;
-        route_pos[r] = pos;  // inverse permutation: where route r's expert row is stored
-    }
-}
-
-// scatter_routes_kernel fused with the copy of the block's token rows into expert order: after
+// The stable scatter fused with the copy of the block's token rows into expert order: after
 // the positions are known, each warp copies its tokens' rows (read once) to their 8 positions
 // each, so the permuted rows are written without a second pass over the permutation. SPLIT CTAs
 // share a block of 64 tokens: each recomputes the block's positions (cheap), the first writes the
@@ -719,36 +686,6 @@ combine_norm_kernel(const uint16_t *__restrict__ yp, const int32_t *__restrict__
         o.w = (uint32_t)f32_to_bf16_bits(r[k][6] * scale * wv[6]) | ((uint32_t)f32_to_bf16_bits(r[k][7] * scale * wv[7]) << 16);
         *reinterpret_cast<uint4 *>(h + (size_t)t * D + c) = o;
         if (h_trace) *reinterpret_cast<uint4 *>(h_trace + (size_t)t * D + c) = o;
-    }
-}
-
-// ------------------------------------------------------------------ permuted token rows
-//
-// xp[pos] = src[perm_route[pos] / 8] for the routed positions pos < *count (expert order), so
-// the grouped gate/up GEMM reads each expert's tokens as contiguous rows. One warp per row,
-// 16 bytes per lane per step; D % 256 == 0.
-__global__ void __launch_bounds__(256)
-permute_rows_kernel(const uint16_t *__restrict__ src, const int32_t *__restrict__ perm_route,
-                    const int32_t *__restrict__ count, int D, uint16_t *__restrict__ dst) {
-    const int lane = threadIdx.x & 31;
-    const int n = *count;
-    const int chunks = D / 8;  // 16-byte chunks per row
-    for (int pos = blockIdx.x * 8 + (threadIdx.x >> 5); pos < n; pos += gridDim.x * 8) {
-        const uint4 *s = reinterpret_cast<const uint4 *>(src + (size_t)(perm_route[pos] >> 3) * D);
-        uint4 *d = reinterpret_cast<uint4 *>(dst + (size_t)pos * D);
-        for (int c0 = 0; c0 < chunks; c0 += 256) {
-            uint4 v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int c = c0 + j * 32 + lane;
-                if (c < chunks) v[j] = s[c];
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int c = c0 + j * 32 + lane;
-                if (c < chunks) d[c] = v[j];
-            }
-        }
     }
 }
 
