@@ -67,9 +67,4 @@ __global__ void gen_quant_kernel(uint64_t base, float scale, int64_t total_rows,
     for (int i = 0; i < wpg; ++i) dst[i] = words[i];
 }
 
-__global__ void gen_bf16_kernel(uint64_t base, float scale, int64_t n, uint16_t *__restrict__ out) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) out[i] = f32_to_bf16_bits(normal_sample(base, (uint64_t)i, scale));
-}
-
 }  // namespace di
